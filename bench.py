@@ -1,0 +1,553 @@
+#!/usr/bin/env python
+"""Benchmark of the FP8 block-scaled matmul path (qwen35-c's q35_mm.c) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (``value``): benchmark configuration 3 -- one full
+64-layer FP8 decode weight stream (48 Gated-DeltaNet + 16 GQA layers, the
+configuration-2 projection shapes plus the MLP in every layer, 24.33 GB of
+FP8 weights), one token, tensor-parallel over the N GPUs (column-parallel +
+NCCL all-gather, row-parallel + NCCL all-reduce), captured in one CUDA graph
+per rank.  ``value`` = weight bytes streamed by all ranks / step time (GB/s),
+``ms_per_step`` = ms per decode token.  Inputs are resident in HBM; the
+weights (24.33 GB / N per GPU) are far larger than L2, so every step reads
+them from DRAM.
+
+Also reported on the same line: the isolated decode GEMV of configuration 0
+(17408x5120, five rotating weight copies so L2 never holds the next one) and
+the configuration-1 sweep (gate/up and down at M in {1,4,16,64}) -- rank 0,
+N=1 only; the live roofline of the dominant kernel; the end-to-end figure
+through the reference-facing C-ABI with host buffers; the CPU baseline
+(the reference's own q35_mm.c, compiled from its sources) on the host cores.
+
+For N > 1 launch with torchrun (one process per GPU, rendezvous on
+127.0.0.1); rank 0 prints the single JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "qwen38-in-c_b200"))
+
+METRIC = "FP8 decode GEMV HBM GB/s (% peak); prefill GEMM TFLOP/s; 64-layer ms/token"
+HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=64, help="decode-stack depth (64 = configuration 3)")
+    ap.add_argument("--no-extras", action="store_true", help="skip the C0/C1 sweep, e2e and CPU baseline")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", HBM_FALLBACK_GBS), d.get("bf16_tflops", BF16_FALLBACK_TFLOPS), d.get(
+            "bf16_tflops_sustained", BF16_FALLBACK_TFLOPS), "measured"
+    return HBM_FALLBACK_GBS, BF16_FALLBACK_TFLOPS, BF16_FALLBACK_TFLOPS, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.out = ""
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.out, _ = self.proc.communicate()
+        sm, mx, reasons, pw = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [t.strip() for t in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                pw.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(pw) if pw else None}
+
+
+# ---------------------------------------------------------------------------
+# the reference arm / CPU baseline: qwen35-c's q35_mm.c on the host cores
+# ---------------------------------------------------------------------------
+def cpu_layer_sample():
+    """Host weights for one DeltaNet and one GQA layer (the per-layer-kind
+    projections of the decode chain), seeded like the GPU run."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # noqa: F401  (test infrastructure: CPU baseline only)
+    import stack
+
+    orc = oracle.Oracle()
+    ws = {}
+    for layer, kind in ((0, "dn"), (3, "gqa")):
+        cols = stack.DN_COL if kind == "dn" else stack.GQA_COL
+        for name, rows in cols:
+            ws[(layer, name)] = orc.synth_fp8(stack.seed_of(layer, name), rows, stack.HIDDEN)
+        ao = "out" if kind == "dn" else "o"
+        ws[(layer, ao)] = orc.synth_fp8(stack.seed_of(layer, ao), stack.HIDDEN, stack.OUT_K)
+        ws[(layer, "gate")] = orc.synth_fp8(stack.seed_of(layer, "gate"), stack.MLP, stack.HIDDEN)
+        ws[(layer, "up")] = orc.synth_fp8(stack.seed_of(layer, "up"), stack.MLP, stack.HIDDEN)
+        ws[(layer, "down")] = orc.synth_fp8(stack.seed_of(layer, "down"), stack.HIDDEN, stack.MLP)
+    x = orc.synth_act(77, (2, stack.HIDDEN))
+    return orc, ws, x
+
+
+def layer_chain(mm_fp8, mm_multi4, ws, layer, kind, x):
+    """One layer of the decode chain through host-pointer matmul entry points."""
+    import stack
+
+    cols = stack.DN_COL if kind == "dn" else stack.GQA_COL
+    outs = mm_multi4([ws[(layer, n)][0] for n, _ in cols], [ws[(layer, n)][1] for n, _ in cols], x)[: len(cols)]
+    src = outs[-1] if kind == "dn" else outs[0]
+    ao = ws[(layer, "out" if kind == "dn" else "o")]
+    o = mm_fp8(ao[0], ao[1], src[: stack.OUT_K].copy())
+    g, u = mm_multi4([ws[(layer, "gate")][0], ws[(layer, "up")][0]], [ws[(layer, "gate")][1], ws[(layer, "up")][1]], o)[:2]
+    d = ws[(layer, "down")]
+    return mm_fp8(d[0], d[1], g)
+
+
+def time_cpu_reference(steps: int, warmup: int):
+    """Reference q35_mm.c (oracle/_ref, or the oracle port if it was not built)
+    over one DeltaNet + one GQA layer per step, all host threads."""
+    import stack
+
+    orc, ws, x = cpu_layer_sample()
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+
+    if oracle.Reference.available():
+        R = oracle.Reference()
+        kind = "reference"
+        mm_fp8, mm_multi4 = R.mm_fp8, R.mm_fp8_multi4
+    else:
+        kind = "port"
+        mm_fp8 = orc.mm_fp8
+
+        def mm_multi4(Ws, Ss, xx):
+            return [orc.mm_fp8(w, s, xx) for w, s in zip(Ws, Ss)]
+    sample_bytes = sum(w.nbytes for w, _ in ws.values())
+    times = {"dn": [], "gqa": []}
+    for i in range(warmup + steps):
+        for layer, k in ((0, "dn"), (3, "gqa")):
+            t0 = time.perf_counter()
+            layer_chain(mm_fp8, mm_multi4, ws, layer, k, x[0 if k == "dn" else 1])
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times[k].append(dt)
+    t_dn, t_gqa = statistics.median(times["dn"]), statistics.median(times["gqa"])
+    n_dn = sum(1 for k in stack.layer_kinds() if k == "dn")
+    n_gqa = stack.N_LAYERS - n_dn
+    step_s = n_dn * t_dn + n_gqa * t_gqa  # extrapolated to 64 layers
+    gbs = stack.weight_bytes() / step_s / 1e9
+    return {
+        "value": gbs, "unit": "GB/s", "cores": orc.threads(), "kind": kind,
+        "ms_per_step_extrapolated": step_s * 1e3,
+        "sample": f"one DeltaNet + one GQA layer chain per step ({sample_bytes / 1e6:.0f} MB FP8), median of "
+                  f"{steps} steps after {warmup} warm-up, extrapolated x48/x16 to the 64-layer stream",
+        "impl": "q35_mm.c compiled -O2 -mavx2 -mfma -fopenmp" if kind == "reference" else "oracle C port",
+    }
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cb = time_cpu_reference(max(1, args.steps // 4), max(1, args.warmup // 2))
+    line = {
+        "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": cb["ms_per_step_extrapolated"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (FP8 e4m3 weights, bf16 scales)",
+        "data": "synthetic (seeded N(0,0.02) weights, 128x128 block-quantised; N(0,1) activations)",
+        "config": {"workload": "configuration 3: 64-layer FP8 decode weight stream, M=1",
+                   "weight_bytes_per_step": __import__("stack").weight_bytes()},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def gemv_bytes(rows, cols, m=1):
+    return rows * cols + 4 * ((rows + 127) // 128) * ((cols + 127) // 128) + 4 * m * (rows + cols)
+
+
+def time_gemv_rotating(q35cu, torch, rows, cols, m, copies=5, rounds=20):
+    """Isolated GEMV: `copies` distinct weights cycled so none is L2-resident."""
+    ws = [q35cu.Weight.synth_fp8(1000 + i, rows, cols) for i in range(copies)]
+    try:
+        X = torch.randn((m, cols), device="cuda")
+        Y = torch.empty((m, rows), device="cuda")
+        for w in ws:
+            q35cu.gemv(w, X, Y, m)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(rounds):
+            for w in ws:
+                q35cu.gemv(w, X, Y, m)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (rounds * copies)
+    finally:
+        for w in ws:
+            w.free()
+    b = gemv_bytes(rows, cols, m)
+    return {"rows": rows, "cols": cols, "m": m, "us": round(us, 2), "GBps": round(b / us / 1e3, 1),
+            "TFLOPs": round(2 * m * rows * cols / us / 1e6, 3)}
+
+
+def kernel_roofline(q35cu, torch, st, hbm_peak, reps=3):
+    """Per-launch CUDA-event timing of every GEMV launch of one step (no
+    collectives), on the stream they run on; sum of algorithmic bytes / sum of
+    launch durations."""
+    stream = torch.cuda.current_stream()
+    launches = []
+    for L in st.layers:
+        launches.append(("multi", [p.w for p in L.col_in]))
+        launches.append(("gemv", L.attn_out.w))
+        launches.append(("multi", [L.gate.w, L.up.w]))
+        launches.append(("gemv", L.down.w))
+    total_bytes = 0
+    for kind, w in launches:
+        ws = w if kind == "multi" else [w]
+        for ww in ws:
+            total_bytes += gemv_bytes(ww.rows, ww.cols)
+    xs = torch.randn((stack_max_cols(st),), device="cuda")
+    ybuf = torch.empty((40000,), device="cuda")
+    durs = []
+    for _ in range(reps):
+        evs = []
+        for kind, w in launches:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            if kind == "multi":
+                outs, off = [], 0
+                for ww in w:
+                    outs.append(ybuf[off:off + ww.rows])
+                    off += ww.rows
+                q35cu.multi(w, xs[: w[0].cols], outs, 1)
+            else:
+                q35cu.gemv(w, xs[: w.cols], ybuf[: w.rows], 1)
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        durs.append(sum(a.elapsed_time(b) for a, b in evs) * 1e-3)
+    t = statistics.median(durs)
+    ach = total_bytes / t / 1e9
+    return ach, total_bytes / len(launches), t / len(launches), len(launches)
+
+
+def stack_max_cols(st):
+    return max(max(p.w.cols for p in L.col_in + [L.attn_out, L.gate, L.up, L.down]) for L in st.layers)
+
+
+def e2e_c_abi(q35cu, st, steps, warmup):
+    """configuration 3 through the reference-facing q35_mm_* entry points with
+    HOST buffers (N=1): every call copies its input in and its output out."""
+    import numpy as np
+
+    import stack
+
+    # host keys bound to the device-resident weights (a loader that streamed
+    # the tensors to HBM itself; see q35cu_weight_bind)
+    keys = []
+    hostw = {}
+    for i, L in enumerate(st.layers):
+        for p in L.col_in + [L.attn_out, L.gate, L.up, L.down]:
+            kw = np.zeros(16, np.uint8)
+            ks = np.zeros(16, np.uint16)
+            p.w.bind(kw, ks)
+            keys.append((kw, ks))
+            hostw[(i, p.name)] = (kw, ks, p.w.rows, p.w.cols)
+    lib = q35cu.load()
+    import ctypes as C
+
+    def mm_fp8(key, x, rows):
+        kw, ks, r, c = key
+        y = np.empty(r, np.float32)
+        lib.q35_mm_fp8(kw.ctypes.data_as(q35cu._u8p), ks.ctypes.data_as(q35cu._u16p), r, c,
+                       x.ctypes.data_as(q35cu._f32p), y.ctypes.data_as(q35cu._f32p))
+        return y
+
+    def mm_multi(keys4, x):
+        n = len(keys4)
+        rows = (C.c_uint32 * 4)(*([k[2] for k in keys4] + [0] * (4 - n)))
+        outs = [np.empty(k[2], np.float32) for k in keys4] + [np.empty(1, np.float32)] * (4 - n)
+        wp = (q35cu._u8p * 4)(*([k[0].ctypes.data_as(q35cu._u8p) for k in keys4] + [q35cu._u8p()] * (4 - n)))
+        sp = (q35cu._u16p * 4)(*([k[1].ctypes.data_as(q35cu._u16p) for k in keys4] + [q35cu._u16p()] * (4 - n)))
+        yp = (q35cu._f32p * 4)(*[o.ctypes.data_as(q35cu._f32p) for o in outs])
+        lib.q35_mm_fp8_multi4(wp, sp, rows, keys4[0][3], x.ctypes.data_as(q35cu._f32p), yp)
+        return outs[:n]
+
+    rng = np.random.default_rng(5)
+    xs = rng.standard_normal((len(st.layers), stack.HIDDEN)).astype(np.float32)
+    h2d = d2h = 0
+    for s in range(warmup + steps):
+        if s == warmup:
+            t0 = time.perf_counter()
+            h2d = d2h = 0
+        for i, L in enumerate(st.layers):
+            cols = [hostw[(i, p.name)] for p in L.col_in]
+            outs = mm_multi(cols, xs[i])
+            h2d += 4 * stack.HIDDEN
+            d2h += 4 * sum(k[2] for k in cols)
+            src = outs[-1] if L.kind == "dn" else outs[0]
+            o = mm_fp8(hostw[(i, L.attn_out.name)], np.ascontiguousarray(src[: stack.OUT_K]), stack.HIDDEN)
+            h2d += 4 * stack.OUT_K
+            d2h += 4 * stack.HIDDEN
+            g, u = mm_multi([hostw[(i, "gate")], hostw[(i, "up")]], o)
+            h2d += 4 * stack.HIDDEN
+            d2h += 8 * stack.MLP
+            mm_fp8(hostw[(i, "down")], g, stack.HIDDEN)
+            h2d += 4 * stack.MLP
+            d2h += 4 * stack.HIDDEN
+    dt = (time.perf_counter() - t0) / steps
+    lib.q35cu_release_all()  # drop the bindings (the weights stay owned by the stack)
+    return {"value": round(stack.weight_bytes(st.n_layers) / dt / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(dt * 1e3, 3), "h2d_bytes_per_step": h2d // steps,
+            "d2h_bytes_per_step": d2h // steps,
+            "path": "q35_mm_fp8_multi4 / q35_mm_fp8 (host pointers, synchronous) per projection"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import q35cu
+    import stack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}; using WORLD_SIZE", file=sys.stderr)
+    torch.cuda.set_device(local)
+    q35cu.load()
+    q35cu.check(q35cu.load().q35cu_set_device(local))
+    cpu_group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        cpu_group = dist.new_group(backend="gloo")
+        uid = [q35cu.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0, group=cpu_group)
+        q35cu.tp_init(rank, world, uid[0])
+
+    hbm_peak, bf16_peak, bf16_sus, peak_src = peaks()
+    st = stack.Stack(rank, world, n_layers=args.layers, scheme="literal")
+    torch.manual_seed(1234 + rank * 0)
+    st.x.copy_(torch.randn(st.x.shape, generator=torch.Generator().manual_seed(1234)).cuda())
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    results = {}
+    graphs = []
+    for scheme in (["literal", "paired"] if world > 1 else ["literal"]):
+        st.scheme = scheme
+        # eager warm-up, then capture one step in a CUDA graph
+        for _ in range(2):
+            st.step()
+        torch.cuda.synchronize()
+        barrier()
+        n0 = q35cu.load().q35cu_launch_count()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                st.step()
+        torch.cuda.current_stream().wait_stream(s)
+        kernels_per_step = q35cu.load().q35cu_launch_count() - n0
+        graphs.append(g)
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        barrier()
+        clk = Clocks(local)
+        clk.start()
+        time.sleep(0.3)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        clocks = clk.stop()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        results[scheme] = {"ms": ms, "clocks": clocks, "kernels_per_step": kernels_per_step}
+
+    main = results["literal"]
+    total_bytes = stack.weight_bytes(args.layers)
+    value = total_bytes / (main["ms"] * 1e-3) / 1e9
+
+    # e2e through the public API with host buffers
+    e2e = None
+    if world == 1 and not args.no_extras:
+        e2e = e2e_c_abi(q35cu, st, steps=max(2, args.steps // 4), warmup=2)
+    else:
+        # TP: H2D of the step's inputs from pinned memory, the step, D2H of its outputs
+        hx = torch.randn(st.x.shape).pin_memory()
+        hy = torch.empty(st.y.shape).pin_memory()
+        g = graphs[0]
+        st.scheme = "literal"
+        for _ in range(2):
+            st.x.copy_(hx, non_blocking=True)
+            g.replay()
+            hy.copy_(st.y, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            st.x.copy_(hx, non_blocking=True)
+            g.replay()
+            hy.copy_(st.y, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        e2e = {"value": round(total_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 3),
+               "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4,
+               "path": "pinned H2D of the 64 layer inputs + graphed TP step + D2H of the 64 layer outputs"}
+
+    # live roofline of the dominant kernel (the decode GEMV), this rank
+    ach, bytes_per_launch, s_per_launch, nl = kernel_roofline(q35cu, torch, st, hbm_peak)
+    ach = max_over_ranks(-ach) * -1 if world > 1 else ach  # slowest rank
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            tj = json.load(f)
+        if "gemv_c3_bytes_per_algorithmic_byte" in tj:
+            traffic = round(tj["gemv_c3_bytes_per_algorithmic_byte"] * bytes_per_launch)
+
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        extras["config0_gemv"] = time_gemv_rotating(q35cu, torch, 17408, 5120, 1)
+        sweep = []
+        for rows, cols in ((17408, 5120), (5120, 17408)):
+            for m in (1, 4, 16, 64):
+                sweep.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10))
+        extras["config1_sweep"] = sweep
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_extras:
+        try:
+            cpu = time_cpu_reference(steps=3, warmup=1)
+        except Exception as e:  # the CPU baseline must not sink the GPU line
+            cpu = {"value": None, "error": repr(e)}
+
+    kernels, colls = st.launches_per_step()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(main["ms"], 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (FP8 e4m3 weights x fp32 activations)",
+            "data": "synthetic (seeded N(0,0.02) weights, 128x128 block-quantised in HBM; N(0,1) activations)",
+            "config": {"workload": f"configuration 3: {args.layers}-layer FP8 decode weight stream, M=1, "
+                                   f"48 DeltaNet + 16 GQA layers",
+                       "weight_bytes_per_step": total_bytes, "parallelism": f"tp{world}",
+                       "tp_scheme": "literal (all-gather after column-parallel, all-reduce after row-parallel)",
+                       "l2": "inputs larger than L2 (weights per GPU per step >> 126 MB)", "cuda_graph": True},
+            "gpu_launches": main["kernels_per_step"] * args.steps,
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(ach / hbm_peak, 4), "traffic": traffic,
+                         "kernel": "gemv_vec_kernel<fp8,1> (decode GEMV), all launches of one step",
+                         "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
+                         "launches_timed": nl, "algorithmic_bytes_per_launch": round(bytes_per_launch),
+                         "us_per_launch": round(s_per_launch * 1e6, 2)},
+            "clocks": main["clocks"],
+            "e2e": e2e,
+        }
+        if world > 1:
+            line["paired"] = {"ms_per_step": round(results["paired"]["ms"], 4),
+                              "value": round(total_bytes / (results["paired"]["ms"] * 1e-3) / 1e9, 1),
+                              "note": "Megatron pairing: no all-gather, the row-parallel projection consumes the local shard"}
+            line["collectives_per_step"] = colls
+        if cpu is not None:
+            line["cpu_baseline"] = {k: cpu.get(k) for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline"]["ms_per_step_extrapolated"] = cpu.get("ms_per_step_extrapolated")
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+
+    for g in graphs:
+        del g
+    graphs.clear()
+    st.free()
+    if world > 1:
+        q35cu.tp_finalize()
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

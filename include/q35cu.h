@@ -1,0 +1,153 @@
+/*
+ * q35cu.h -- the native API of libq35cuda.so beyond the reference's
+ * q35_mm.h: device-resident weights, device-pointer launches on a caller
+ * stream, error reporting, and the tensor-parallel (NCCL) primitives.
+ *
+ * The reference engine has no counterpart for most of this (it is a
+ * single-process CPU library, qwen35-c/include/q35/q35_mm.h); each entry
+ * below says which reference behaviour it extends.  Host-pointer callers
+ * only ever need q35_mm.h.
+ *
+ * Conventions
+ *   - every function returns a q35cu_status (0 = OK) unless stated;
+ *   - the last failure of the calling thread is kept for q35cu_last_error();
+ *   - "stream" is a cudaStream_t passed as void* (NULL = the library's own
+ *     per-device stream);
+ *   - activations are fp32 row-major, token-major: X [m, ldx], Y [m, ldy].
+ */
+#ifndef Q35CU_H
+#define Q35CU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    Q35CU_OK = 0,
+    Q35CU_ERR_ARG = 1,          /* null pointer, zero/oversized shape, bad stride */
+    Q35CU_ERR_NOMEM = 2,        /* device allocation failed or the budget is spent */
+    Q35CU_ERR_CUDA = 3,         /* CUDA runtime error (message has the name) */
+    Q35CU_ERR_UNSUPPORTED = 4,  /* shape or alignment the requested kernel cannot take */
+    Q35CU_ERR_NCCL = 5,         /* NCCL call failed, or tensor parallel not initialised */
+    Q35CU_ERR_NODEV = 6,        /* no CUDA device / not an sm_100 part */
+    Q35CU_ERR_TIMEOUT = 7       /* a bounded device-side wait gave up */
+} q35cu_status;
+
+typedef enum { Q35CU_ON_ERROR_ABORT = 0, Q35CU_ON_ERROR_RECORD = 1 } q35cu_error_mode;
+
+/* ---- errors ------------------------------------------------------------ */
+/* The reference's matmuls return void and have no error channel
+ * (qwen35-c/src/q35_mm.c:144-198); these add one. */
+int q35cu_last_error(void);
+const char *q35cu_last_error_message(void);
+void q35cu_clear_error(void);
+/* ABORT (default; env Q35CU_ON_ERROR=record flips it): a failing q35_mm_*
+ * call prints the error and aborts.  RECORD: it records the error, fills
+ * the outputs with NaN and returns. */
+void q35cu_set_error_mode(int mode);
+int q35cu_get_error_mode(void);
+
+/* ---- device and residency cache --------------------------------------- */
+int q35cu_device_count(void);                 /* 0 without a usable GPU */
+int q35cu_set_device(int device);             /* device for later calls of this process */
+int q35cu_sm_count(void);
+/* Bytes of weights held by the q35_mm_* residency cache. */
+size_t q35cu_cache_bytes(void);
+/* Cap on device bytes for uploads (0 = no cap).  An upload over the cap
+ * fails with Q35CU_ERR_NOMEM exactly like a failed cudaMalloc. */
+void q35cu_set_memory_budget(size_t bytes);
+/* Drop every cached upload (the engine's model free, qwen35-c/src/q35_model.c:714-729,
+ * unmaps the weights; call this before reusing the host memory). */
+void q35cu_release_all(void);
+/* Drop cached uploads whose host weight pointer is W; returns how many. */
+int q35cu_forget(const void *W);
+
+/* ---- device-resident weights ------------------------------------------ */
+typedef struct q35cu_weight q35cu_weight;
+
+/* Upload a whole FP8 weight (host W [rows, cols] e4m3, host BF16 scales). */
+int q35cu_weight_upload_fp8(const uint8_t *W, const uint16_t *scale_bf16,
+                            uint32_t rows, uint32_t cols, q35cu_weight **out);
+/* Upload the window [row0, row0+nrows) x [col0, col0+ncols) of a host FP8
+ * weight [rows, cols] (a tensor-parallel shard).  row0 and col0 must be
+ * multiples of 128 so no scale block is split. */
+int q35cu_weight_upload_fp8_window(const uint8_t *W, const uint16_t *scale_bf16,
+                                   uint32_t rows, uint32_t cols,
+                                   uint32_t row0, uint32_t nrows,
+                                   uint32_t col0, uint32_t ncols, q35cu_weight **out);
+/* Upload a BF16 weight (the lm_head of q35_mm_bf16). */
+int q35cu_weight_upload_bf16(const uint16_t *W, uint32_t rows, uint32_t cols,
+                             q35cu_weight **out);
+/* Generate a seeded synthetic FP8 weight directly in HBM: the window
+ * [row0, +nrows) x [col0, +ncols) of a global [grows, gcols] matrix
+ * W0 ~ N(0, stddev^2) quantised per global 128x128 block
+ * (s = bf16(amax/448), W = e4m3_rne(W0/s)).  Every rank of a
+ * tensor-parallel group generating its own window reproduces the shards of
+ * one global matrix. */
+int q35cu_weight_synth_fp8(uint64_t seed, float stddev, uint32_t grows, uint32_t gcols,
+                           uint32_t row0, uint32_t nrows, uint32_t col0, uint32_t ncols,
+                           q35cu_weight **out);
+/* Copy a device weight back (W [rows, cols], BF16 scales) -- for checks. */
+int q35cu_weight_download_fp8(const q35cu_weight *w, uint8_t *W, uint16_t *scale_bf16);
+/* Make q35_mm_fp8 / _multi4 / _batch serve the host key (host_W, host_sc,
+ * rows, cols) from the device weight w without an upload (a loader that
+ * streamed the tensor to HBM itself).  w must outlive the binding. */
+int q35cu_weight_bind(const uint8_t *host_W, const uint16_t *host_sc, const q35cu_weight *w);
+void q35cu_weight_free(q35cu_weight *w);
+uint32_t q35cu_weight_rows(const q35cu_weight *w);
+uint32_t q35cu_weight_cols(const q35cu_weight *w);
+size_t q35cu_weight_device_bytes(const q35cu_weight *w);
+
+/* ---- device-pointer compute (asynchronous on `stream`) ----------------- */
+/* Y[t, r] = sum_k X[t, k] * W[r, k] * s[r/128, k/128] for t < m, on the
+ * CUDA cores in fp32 (the decode GEMV; q35_mm_fp8 / q35_mm_fp8_batch with
+ * small n).  Deterministic; row results do not depend on m. */
+int q35cu_gemv_fp8(const q35cu_weight *w, const float *X, uint32_t ldx, uint32_t m,
+                   float *Y, uint32_t ldy, void *stream);
+/* o[i] = silu(g[i]) * u[i] for i < n -- the engine's swiglu between the
+ * gate/up and down projections (qwen35-c/src/q35_kern.c), used by the
+ * decode-step harness to chain the projections. */
+int q35cu_swiglu(const float *g, const float *u, float *o, size_t n, void *stream);
+/* Up to four weights sharing X and cols in one launch (q35_mm_fp8_multi4);
+ * w[s] == NULL skips segment s; Y[s] is [m, rows_s] (row stride rows_s). */
+int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint32_t ldx, uint32_t m,
+                    float *const Y[4], void *stream);
+/* Tensor-core GEMM for prefill: Y [m, rows] fp32 = Xb [m, cols] bf16 times
+ * the dequantised weight, fp32 accumulation with per-128-K block-scale
+ * promotion.  Needs cols % 16 == 0. */
+int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m,
+                   float *Y, void *stream);
+/* fp32 -> bf16 (nearest even) conversion of n values. */
+int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream);
+/* y[rows] = W x for a bf16 weight (q35_mm_bf16). */
+int q35cu_gemv_bf16(const q35cu_weight *w, const float *x, float *y, void *stream);
+
+/* ---- tensor parallel (NCCL over NVLink) -------------------------------- */
+/* The reference is single-process; these are new.  Column-parallel layers
+ * (gate/up/qkv/z/q/k/v) split W by rows and all-gather Y; row-parallel
+ * layers (down/o/out) split W by columns and all-reduce Y. */
+typedef enum { Q35CU_SHARD_COLUMN = 0, Q35CU_SHARD_ROW = 1 } q35cu_shard_mode;
+/* Host-only: the window of W [rows, cols] held by `rank` of `world`
+ * (128-aligned; the last rank takes the remainder).  No GPU needed. */
+int q35cu_shard_window(uint32_t rows, uint32_t cols, int mode, int rank, int world,
+                       uint32_t *row0, uint32_t *nrows, uint32_t *col0, uint32_t *ncols);
+int q35cu_nccl_unique_id(void *out, size_t cap);   /* cap >= 128 */
+int q35cu_tp_init(int rank, int world, const void *id, size_t idlen);
+int q35cu_tp_world(void);
+int q35cu_tp_rank(void);
+int q35cu_tp_finalize(void);
+int q35cu_allreduce_f32(float *buf, size_t n, void *stream);
+int q35cu_allgather_f32(const float *send, float *recv, size_t n_per_rank, void *stream);
+
+/* ---- info --------------------------------------------------------------- */
+const char *q35cu_build_info(void);
+/* Kernel launches this library issued since load (all entry points). */
+uint64_t q35cu_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q35CU_H */

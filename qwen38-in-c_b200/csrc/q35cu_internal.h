@@ -1,0 +1,68 @@
+// Internal declarations shared by the libq35cuda translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "q35cu.h"
+
+#define Q35CU_STR2(x) #x
+#define Q35CU_STR(x) Q35CU_STR2(x)
+
+struct q35cu_weight {
+    int kind;            // 0 = FP8 e4m3 + fp32 block scales, 1 = BF16
+    uint32_t rows, cols; // logical shape of the device tensor
+    void *d_w;           // [rows, cols] bytes (fp8) or bf16
+    float *d_s;          // [rows_blk, cols_blk] fp32 scales (fp8 only)
+    uint32_t rows_blk, cols_blk;
+    size_t bytes;        // device bytes held
+    int device;
+};
+
+namespace q35cu {
+
+// ---- error plumbing (shim.cu) ----
+int set_error(int code, const char *fmt, ...);
+int cuda_error(cudaError_t e, const char *what);
+#define Q35CU_CUDA(call)                                         \
+    do {                                                         \
+        cudaError_t e_ = (call);                                 \
+        if (e_ != cudaSuccess) return q35cu::cuda_error(e_, #call); \
+    } while (0)
+
+int device_sms();
+void count_launch(uint64_t n = 1);
+cudaStream_t default_stream();
+
+// ---- device memory with the budget check (shim.cu) ----
+int dev_alloc(void **p, size_t bytes);
+void dev_free(void *p, size_t bytes);
+
+// ---- kernels (gemv.cu / gemm.cu / synth.cu) ----
+struct GemvSeg {
+    const uint8_t *W;   // [rows, K] (fp8 bytes, or bf16 when kind == 1)
+    const float *S;     // [ceil(rows/128), ceil(K/128)] (fp8 only)
+    float *Y;           // output for this segment, token-major [m, ldy]
+    uint32_t rows;
+    uint32_t ldy;
+    uint32_t wpt;       // warps that split K for one task (1, 2, 4, 8)
+    uint32_t cta_begin; // first CTA of this segment in the grid
+};
+
+int launch_gemv(int kind, const GemvSeg *segs, int nseg, const float *X,
+                uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st);
+int launch_swiglu(const float *g, const float *u, float *o, size_t n, cudaStream_t st);
+uint32_t gemv_wpt(uint32_t rows, uint32_t K, int sms);
+
+int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y,
+                    cudaStream_t st);
+int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
+int launch_bf16_to_f32_scales(const uint16_t *src, float *dst, size_t n, cudaStream_t st);
+int launch_f32_to_bf16_scales(const float *src, uint16_t *dst, size_t n, cudaStream_t st);
+int launch_synth_fp8(uint64_t seed, float stddev, uint32_t grows, uint32_t gcols,
+                     uint32_t row0, uint32_t col0, uint32_t nrows, uint32_t ncols,
+                     uint8_t *W, float *S, cudaStream_t st);
+int launch_fill_nan(float *p, size_t n, cudaStream_t st);
+
+}  // namespace q35cu

@@ -1,0 +1,891 @@
+// libq35cuda host side: the reference-facing C-ABI (q35_mm.h) and the
+// native API (q35cu.h).
+//
+// The q35_mm_* entry points keep the signatures and synchronous host-pointer
+// semantics of qwen35-c/src/q35_mm.c:144-246.  Behind them:
+//   * a residency cache keyed by (host W, host scale, rows, cols): the first
+//     call uploads the weight (scales widened bf16 -> fp32, exact), later
+//     calls reuse it -- the engine's weights are immutable mmaps
+//     (qwen35-c/src/q35_model.c:253-273), so the key identifies the tensor;
+//   * pinned host staging + one stream per device: copy x in, launch, copy
+//     y out, synchronise, copy to the caller's buffer;
+//   * errors: the signatures return void, so by default a failure aborts
+//     with a message; Q35CU_ON_ERROR=record (or q35cu_set_error_mode) makes
+//     it record the error and fill the outputs with NaN instead.
+#include <nccl.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "q35_mm.h"
+#include "q35cu_internal.h"
+
+#define Q35_API extern "C" __attribute__((visibility("default")))
+
+// ------------------------------------------------------------------------
+// errors
+// ------------------------------------------------------------------------
+namespace {
+thread_local int t_err = Q35CU_OK;
+thread_local char t_msg[512] = "";
+std::atomic<int> g_mode{-1};
+std::atomic<uint64_t> g_launches{0};
+
+int error_mode()
+{
+    int m = g_mode.load();
+    if (m < 0) {
+        const char *e = getenv("Q35CU_ON_ERROR");
+        m = (e && (!strcmp(e, "record") || !strcmp(e, "1"))) ? Q35CU_ON_ERROR_RECORD : Q35CU_ON_ERROR_ABORT;
+        g_mode.store(m);
+    }
+    return m;
+}
+}  // namespace
+
+namespace q35cu {
+
+int set_error(int code, const char *fmt, ...)
+{
+    t_err = code;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_msg, sizeof t_msg, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char *what)
+{
+    return set_error(e == cudaErrorMemoryAllocation ? Q35CU_ERR_NOMEM : Q35CU_ERR_CUDA, "%s: %s (%s)", what,
+                     cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+}  // namespace q35cu
+
+using namespace q35cu;
+
+// ------------------------------------------------------------------------
+// per-device state, budget, cache
+// ------------------------------------------------------------------------
+namespace {
+
+struct DevState {
+    bool ready = false;
+    int sms = 0;
+    int major = 0;
+    cudaStream_t stream = nullptr;
+    void *h_stage = nullptr;  // pinned, in + out
+    size_t h_cap = 0;
+    void *d_stage = nullptr;  // device, in + out
+    size_t d_cap = 0;
+};
+
+struct Key {
+    const void *w, *s;
+    uint32_t rows, cols;
+    int kind;
+    bool operator==(const Key &o) const
+    {
+        return w == o.w && s == o.s && rows == o.rows && cols == o.cols && kind == o.kind;
+    }
+};
+struct KeyHash {
+    size_t operator()(const Key &k) const
+    {
+        size_t h = std::hash<const void *>()(k.w);
+        h ^= std::hash<const void *>()(k.s) + 0x9e3779b97f4a7c15ULL + (h << 6) + (h >> 2);
+        h ^= ((size_t)k.rows << 32 | k.cols) + 0x9e3779b97f4a7c15ULL + (h << 6) + (h >> 2);
+        return h ^ (size_t)k.kind;
+    }
+};
+struct Entry {
+    q35cu_weight *w;
+    bool owned;  // false for q35cu_weight_bind
+};
+
+std::recursive_mutex g_mu;
+int g_device = 0;
+std::vector<DevState> g_dev;
+std::unordered_map<Key, Entry, KeyHash> g_cache;
+size_t g_cache_bytes = 0;
+size_t g_budget = 0;
+size_t g_alloc_bytes = 0;
+
+DevState *dev_state()
+{
+    if (g_dev.empty()) {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            set_error(Q35CU_ERR_NODEV, "no CUDA device visible");
+            return nullptr;
+        }
+        g_dev.resize(n);
+    }
+    if (g_device < 0 || g_device >= (int)g_dev.size()) {
+        set_error(Q35CU_ERR_NODEV, "device %d out of range", g_device);
+        return nullptr;
+    }
+    DevState &d = g_dev[g_device];
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != g_device) {
+        if (cudaSetDevice(g_device) != cudaSuccess) {
+            cuda_error(cudaGetLastError(), "cudaSetDevice");
+            return nullptr;
+        }
+    }
+    if (!d.ready) {
+        cudaDeviceProp p;
+        cudaError_t e = cudaGetDeviceProperties(&p, g_device);
+        if (e != cudaSuccess) { cuda_error(e, "cudaGetDeviceProperties"); return nullptr; }
+        if (p.major != 10) {
+            set_error(Q35CU_ERR_NODEV, "device %d is sm_%d%d; this library is built for sm_100a only", g_device,
+                      p.major, p.minor);
+            return nullptr;
+        }
+        d.sms = p.multiProcessorCount;
+        d.major = p.major;
+        e = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { cuda_error(e, "cudaStreamCreate"); return nullptr; }
+        d.ready = true;
+    }
+    return &d;
+}
+
+int ensure_stage(DevState *d, size_t bytes)
+{
+    bytes = (bytes + 255) & ~(size_t)255;
+    if (bytes > d->h_cap) {
+        if (d->h_stage) cudaFreeHost(d->h_stage);
+        d->h_stage = nullptr;
+        d->h_cap = 0;
+        size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
+        Q35CU_CUDA(cudaMallocHost(&d->h_stage, cap));
+        d->h_cap = cap;
+    }
+    if (bytes > d->d_cap) {
+        if (d->d_stage) dev_free(d->d_stage, d->d_cap);
+        d->d_stage = nullptr;
+        d->d_cap = 0;
+        size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
+        int rc = dev_alloc(&d->d_stage, cap);
+        if (rc) return rc;
+        d->d_cap = cap;
+    }
+    return Q35CU_OK;
+}
+
+void weight_release(q35cu_weight *w)
+{
+    if (!w) return;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (w->device != cur) cudaSetDevice(w->device);
+    dev_free(w->d_w, w->bytes - (w->d_s ? (size_t)w->rows_blk * w->cols_blk * 4 : 0));
+    if (w->d_s) dev_free(w->d_s, (size_t)w->rows_blk * w->cols_blk * 4);
+    if (w->device != cur) cudaSetDevice(cur);
+    delete w;
+}
+
+// fail according to the error mode: abort, or record + NaN-fill host outputs
+void fail_host(float *const *outs, const size_t *counts, int nout)
+{
+    if (error_mode() == Q35CU_ON_ERROR_ABORT) {
+        fprintf(stderr, "libq35cuda: fatal: %s (code %d)\n", t_msg, t_err);
+        abort();
+    }
+    for (int i = 0; i < nout; ++i)
+        if (outs[i])
+            for (size_t j = 0; j < counts[i]; ++j) outs[i][j] = __builtin_nanf("");
+}
+
+}  // namespace
+
+namespace q35cu {
+
+int device_sms()
+{
+    if (g_device >= 0 && g_device < (int)g_dev.size() && g_dev[g_device].ready) return g_dev[g_device].sms;
+    DevState *d = dev_state();
+    return d ? d->sms : 148;
+}
+
+cudaStream_t default_stream()
+{
+    if (g_device >= 0 && g_device < (int)g_dev.size() && g_dev[g_device].ready) return g_dev[g_device].stream;
+    DevState *d = dev_state();
+    return d ? d->stream : nullptr;
+}
+
+int dev_alloc(void **p, size_t bytes)
+{
+    *p = nullptr;
+    if (g_budget && g_alloc_bytes + bytes > g_budget)
+        return set_error(Q35CU_ERR_NOMEM, "device budget exceeded: %zu + %zu > %zu bytes", g_alloc_bytes, bytes,
+                         g_budget);
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *p = nullptr;
+        return cuda_error(e, "cudaMalloc");
+    }
+    g_alloc_bytes += bytes;
+    return Q35CU_OK;
+}
+
+void dev_free(void *p, size_t bytes)
+{
+    if (!p) return;
+    cudaFree(p);
+    g_alloc_bytes -= bytes < g_alloc_bytes ? bytes : g_alloc_bytes;
+}
+
+}  // namespace q35cu
+
+// ------------------------------------------------------------------------
+// weights
+// ------------------------------------------------------------------------
+namespace {
+
+int weight_alloc(int kind, uint32_t rows, uint32_t cols, q35cu_weight **out)
+{
+    *out = nullptr;
+    if (!rows || !cols) return set_error(Q35CU_ERR_ARG, "weight shape %ux%u", rows, cols);
+    if (!dev_state()) return t_err;
+    auto *w = new q35cu_weight{};
+    w->kind = kind;
+    w->rows = rows;
+    w->cols = cols;
+    w->rows_blk = (rows + 127) / 128;
+    w->cols_blk = (cols + 127) / 128;
+    w->device = g_device;
+    const size_t wb = (size_t)rows * cols * (kind == 0 ? 1 : 2);
+    int rc = dev_alloc(&w->d_w, wb);
+    if (rc) { delete w; return rc; }
+    w->bytes = wb;
+    if (kind == 0) {
+        const size_t sb = (size_t)w->rows_blk * w->cols_blk * 4;
+        rc = dev_alloc(reinterpret_cast<void **>(&w->d_s), sb);
+        if (rc) { dev_free(w->d_w, wb); delete w; return rc; }
+        w->bytes += sb;
+    }
+    *out = w;
+    return Q35CU_OK;
+}
+
+// copy host FP8 window + bf16 scale window into w (synchronous)
+int weight_fill_fp8(q35cu_weight *w, const uint8_t *W, const uint16_t *sc, uint32_t cols, uint32_t row0,
+                    uint32_t col0)
+{
+    DevState *d = dev_state();
+    if (!d) return t_err;
+    cudaStream_t st = d->stream;
+    if (col0 == 0 && w->cols == cols) {
+        Q35CU_CUDA(cudaMemcpyAsync(w->d_w, W + (size_t)row0 * cols, (size_t)w->rows * cols,
+                                   cudaMemcpyHostToDevice, st));
+    } else {
+        Q35CU_CUDA(cudaMemcpy2DAsync(w->d_w, w->cols, W + (size_t)row0 * cols + col0, cols, w->cols, w->rows,
+                                     cudaMemcpyHostToDevice, st));
+    }
+    const uint32_t gcb = (cols + 127) / 128;
+    const size_t n = (size_t)w->rows_blk * w->cols_blk;
+    int rc = ensure_stage(d, n * 2);
+    if (rc) return rc;
+    uint16_t *hs = static_cast<uint16_t *>(d->h_stage);
+    Q35CU_CUDA(cudaStreamSynchronize(st));  // staging may be in use
+    for (uint32_t i = 0; i < w->rows_blk; ++i)
+        memcpy(hs + (size_t)i * w->cols_blk, sc + (size_t)(row0 / 128 + i) * gcb + col0 / 128,
+               (size_t)w->cols_blk * 2);
+    Q35CU_CUDA(cudaMemcpyAsync(d->d_stage, hs, n * 2, cudaMemcpyHostToDevice, st));
+    rc = launch_bf16_to_f32_scales(static_cast<uint16_t *>(d->d_stage), w->d_s, n, st);
+    if (rc) return rc;
+    Q35CU_CUDA(cudaStreamSynchronize(st));
+    return Q35CU_OK;
+}
+
+// find or upload the weight for a host key (q35_mm_* path)
+q35cu_weight *cached_weight(int kind, const void *W, const void *sc, uint32_t rows, uint32_t cols)
+{
+    Key k{W, sc, rows, cols, kind};
+    auto it = g_cache.find(k);
+    if (it != g_cache.end()) return it->second.w;
+    q35cu_weight *w = nullptr;
+    if (weight_alloc(kind, rows, cols, &w)) return nullptr;
+    int rc;
+    if (kind == 0) {
+        rc = weight_fill_fp8(w, static_cast<const uint8_t *>(W), static_cast<const uint16_t *>(sc), cols, 0, 0);
+    } else {
+        DevState *d = dev_state();
+        rc = cudaMemcpyAsync(w->d_w, W, (size_t)rows * cols * 2, cudaMemcpyHostToDevice, d->stream) == cudaSuccess
+                 ? cudaStreamSynchronize(d->stream) == cudaSuccess ? Q35CU_OK : cuda_error(cudaGetLastError(), "sync")
+                 : cuda_error(cudaGetLastError(), "cudaMemcpyAsync");
+    }
+    if (rc) { weight_release(w); return nullptr; }
+    g_cache.emplace(k, Entry{w, true});
+    g_cache_bytes += w->bytes;
+    return w;
+}
+
+GemvSeg seg_of(const q35cu_weight *w, float *Y, uint32_t ldy)
+{
+    GemvSeg g{};
+    g.W = static_cast<const uint8_t *>(w->d_w);
+    g.S = w->d_s;
+    g.Y = Y;
+    g.rows = w->rows;
+    g.ldy = ldy;
+    return g;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------
+// q35cu.h: errors, device, cache
+// ------------------------------------------------------------------------
+Q35_API int q35cu_last_error(void) { return t_err; }
+Q35_API const char *q35cu_last_error_message(void) { return t_msg; }
+Q35_API void q35cu_clear_error(void) { t_err = Q35CU_OK; t_msg[0] = 0; }
+Q35_API void q35cu_set_error_mode(int mode) { g_mode.store(mode ? Q35CU_ON_ERROR_RECORD : Q35CU_ON_ERROR_ABORT); }
+Q35_API int q35cu_get_error_mode(void) { return error_mode(); }
+
+Q35_API int q35cu_device_count(void)
+{
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n;
+}
+
+Q35_API int q35cu_set_device(int device)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    int n = q35cu_device_count();
+    if (device < 0 || device >= n) return set_error(Q35CU_ERR_NODEV, "device %d of %d", device, n);
+    g_device = device;
+    return dev_state() ? Q35CU_OK : t_err;
+}
+
+Q35_API int q35cu_sm_count(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    DevState *d = dev_state();
+    return d ? d->sms : 0;
+}
+
+Q35_API size_t q35cu_cache_bytes(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    return g_cache_bytes;
+}
+
+Q35_API void q35cu_set_memory_budget(size_t bytes)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    g_budget = bytes;
+}
+
+Q35_API void q35cu_release_all(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    for (auto &kv : g_cache)
+        if (kv.second.owned) weight_release(kv.second.w);
+    g_cache.clear();
+    g_cache_bytes = 0;
+}
+
+Q35_API int q35cu_forget(const void *W)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    int n = 0;
+    for (auto it = g_cache.begin(); it != g_cache.end();) {
+        if (it->first.w == W) {
+            if (it->second.owned) {
+                g_cache_bytes -= it->second.w->bytes;
+                weight_release(it->second.w);
+            }
+            it = g_cache.erase(it);
+            ++n;
+        } else {
+            ++it;
+        }
+    }
+    return n;
+}
+
+// ------------------------------------------------------------------------
+// q35cu.h: weights
+// ------------------------------------------------------------------------
+Q35_API int q35cu_weight_upload_fp8_window(const uint8_t *W, const uint16_t *sc, uint32_t rows, uint32_t cols,
+                                           uint32_t row0, uint32_t nrows, uint32_t col0, uint32_t ncols,
+                                           q35cu_weight **out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!out) return set_error(Q35CU_ERR_ARG, "out is NULL");
+    *out = nullptr;
+    if (!W || !sc) return set_error(Q35CU_ERR_ARG, "weight or scale pointer is NULL");
+    if ((row0 & 127) || (col0 & 127)) return set_error(Q35CU_ERR_ARG, "window origin (%u,%u) not 128-aligned", row0, col0);
+    if (!nrows || !ncols || row0 + nrows > rows || col0 + ncols > cols)
+        return set_error(Q35CU_ERR_ARG, "window [%u+%u, %u+%u] outside %ux%u", row0, nrows, col0, ncols, rows, cols);
+    q35cu_weight *w = nullptr;
+    int rc = weight_alloc(0, nrows, ncols, &w);
+    if (rc) return rc;
+    rc = weight_fill_fp8(w, W, sc, cols, row0, col0);
+    if (rc) { weight_release(w); return rc; }
+    *out = w;
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_weight_upload_fp8(const uint8_t *W, const uint16_t *sc, uint32_t rows, uint32_t cols,
+                                    q35cu_weight **out)
+{
+    return q35cu_weight_upload_fp8_window(W, sc, rows, cols, 0, rows, 0, cols, out);
+}
+
+Q35_API int q35cu_weight_upload_bf16(const uint16_t *W, uint32_t rows, uint32_t cols, q35cu_weight **out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!out) return set_error(Q35CU_ERR_ARG, "out is NULL");
+    *out = nullptr;
+    if (!W) return set_error(Q35CU_ERR_ARG, "weight pointer is NULL");
+    q35cu_weight *w = nullptr;
+    int rc = weight_alloc(1, rows, cols, &w);
+    if (rc) return rc;
+    DevState *d = dev_state();
+    cudaError_t e = cudaMemcpy(w->d_w, W, (size_t)rows * cols * 2, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { weight_release(w); return cuda_error(e, "cudaMemcpy"); }
+    (void)d;
+    *out = w;
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_weight_synth_fp8(uint64_t seed, float stddev, uint32_t grows, uint32_t gcols, uint32_t row0,
+                                   uint32_t nrows, uint32_t col0, uint32_t ncols, q35cu_weight **out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!out) return set_error(Q35CU_ERR_ARG, "out is NULL");
+    *out = nullptr;
+    if ((row0 & 127) || (col0 & 127)) return set_error(Q35CU_ERR_ARG, "window origin not 128-aligned");
+    if (!nrows || !ncols || row0 + nrows > grows || col0 + ncols > gcols)
+        return set_error(Q35CU_ERR_ARG, "window outside the global matrix");
+    q35cu_weight *w = nullptr;
+    int rc = weight_alloc(0, nrows, ncols, &w);
+    if (rc) return rc;
+    DevState *d = dev_state();
+    rc = launch_synth_fp8(seed, stddev, grows, gcols, row0, col0, nrows, ncols, static_cast<uint8_t *>(w->d_w),
+                          w->d_s, d->stream);
+    if (!rc && cudaStreamSynchronize(d->stream) != cudaSuccess) rc = cuda_error(cudaGetLastError(), "synth sync");
+    if (rc) { weight_release(w); return rc; }
+    *out = w;
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_weight_download_fp8(const q35cu_weight *w, uint8_t *W, uint16_t *sc)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!w || w->kind != 0 || !W || !sc) return set_error(Q35CU_ERR_ARG, "download: bad arguments");
+    DevState *d = dev_state();
+    if (!d) return t_err;
+    Q35CU_CUDA(cudaMemcpy(W, w->d_w, (size_t)w->rows * w->cols, cudaMemcpyDeviceToHost));
+    const size_t n = (size_t)w->rows_blk * w->cols_blk;
+    int rc = ensure_stage(d, n * 2);
+    if (rc) return rc;
+    rc = launch_f32_to_bf16_scales(w->d_s, static_cast<uint16_t *>(d->d_stage), n, d->stream);
+    if (rc) return rc;
+    Q35CU_CUDA(cudaMemcpyAsync(sc, d->d_stage, n * 2, cudaMemcpyDeviceToHost, d->stream));
+    Q35CU_CUDA(cudaStreamSynchronize(d->stream));
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_weight_bind(const uint8_t *host_W, const uint16_t *host_sc, const q35cu_weight *w)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!host_W || !host_sc || !w || w->kind != 0) return set_error(Q35CU_ERR_ARG, "bind: bad arguments");
+    Key k{host_W, host_sc, w->rows, w->cols, 0};
+    auto it = g_cache.find(k);
+    if (it != g_cache.end()) {
+        if (it->second.owned) {
+            g_cache_bytes -= it->second.w->bytes;
+            weight_release(it->second.w);
+        }
+        g_cache.erase(it);
+    }
+    g_cache.emplace(k, Entry{const_cast<q35cu_weight *>(w), false});
+    return Q35CU_OK;
+}
+
+Q35_API void q35cu_weight_free(q35cu_weight *w)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!w) return;
+    for (auto it = g_cache.begin(); it != g_cache.end();) {
+        if (it->second.w == w) {
+            if (it->second.owned) g_cache_bytes -= w->bytes;
+            it = g_cache.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    weight_release(w);
+}
+
+Q35_API uint32_t q35cu_weight_rows(const q35cu_weight *w) { return w ? w->rows : 0; }
+Q35_API uint32_t q35cu_weight_cols(const q35cu_weight *w) { return w ? w->cols : 0; }
+Q35_API size_t q35cu_weight_device_bytes(const q35cu_weight *w) { return w ? w->bytes : 0; }
+
+// ------------------------------------------------------------------------
+// q35cu.h: device-pointer compute
+// ------------------------------------------------------------------------
+static cudaStream_t pick(void *stream)
+{
+    return stream ? static_cast<cudaStream_t>(stream) : default_stream();
+}
+
+Q35_API int q35cu_gemv_fp8(const q35cu_weight *w, const float *X, uint32_t ldx, uint32_t m, float *Y, uint32_t ldy,
+                           void *stream)
+{
+    if (!w || w->kind != 0 || !X || !Y) return set_error(Q35CU_ERR_ARG, "gemv_fp8: bad arguments");
+    if (!m) return Q35CU_OK;
+    if (ldx < w->cols || ldy < w->rows) return set_error(Q35CU_ERR_ARG, "gemv_fp8: ld smaller than the row");
+    GemvSeg g = seg_of(w, Y, ldy);
+    return launch_gemv(0, &g, 1, X, w->cols, ldx, m, pick(stream));
+}
+
+Q35_API int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint32_t ldx, uint32_t m,
+                            float *const Y[4], void *stream)
+{
+    if (!w || !Y || !X) return set_error(Q35CU_ERR_ARG, "multi_fp8: bad arguments");
+    GemvSeg segs[4];
+    int n = 0;
+    uint32_t K = 0;
+    for (int s = 0; s < 4; ++s) {
+        if (!w[s]) continue;
+        if (w[s]->kind != 0 || !Y[s]) return set_error(Q35CU_ERR_ARG, "multi_fp8: segment %d", s);
+        if (K && w[s]->cols != K) return set_error(Q35CU_ERR_ARG, "multi_fp8: segments disagree on cols");
+        K = w[s]->cols;
+        segs[n++] = seg_of(w[s], Y[s], w[s]->rows);
+    }
+    if (!n || !m) return Q35CU_OK;
+    if (ldx < K) return set_error(Q35CU_ERR_ARG, "multi_fp8: ldx < cols");
+    return launch_gemv(0, segs, n, X, K, ldx, m, pick(stream));
+}
+
+Q35_API int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y, void *stream)
+{
+    if (!w || w->kind != 0 || !Xb || !Y) return set_error(Q35CU_ERR_ARG, "gemm_fp8: bad arguments");
+    if (!m) return Q35CU_OK;
+    return launch_gemm_fp8(w, Xb, m, Y, pick(stream));
+}
+
+Q35_API int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream)
+{
+    if (!x || !y) return set_error(Q35CU_ERR_ARG, "f32_to_bf16: NULL");
+    return launch_f32_to_bf16(x, y, n, pick(stream));
+}
+
+Q35_API int q35cu_swiglu(const float *g, const float *u, float *o, size_t n, void *stream)
+{
+    if (!g || !u || !o) return set_error(Q35CU_ERR_ARG, "swiglu: NULL");
+    return launch_swiglu(g, u, o, n, pick(stream));
+}
+
+Q35_API int q35cu_gemv_bf16(const q35cu_weight *w, const float *x, float *y, void *stream)
+{
+    if (!w || w->kind != 1 || !x || !y) return set_error(Q35CU_ERR_ARG, "gemv_bf16: bad arguments");
+    GemvSeg g = seg_of(w, y, w->rows);
+    return launch_gemv(1, &g, 1, x, w->cols, w->cols, 1, pick(stream));
+}
+
+Q35_API const char *q35cu_build_info(void)
+{
+    return "libq35cuda sm_100a (nvcc " Q35CU_STR(__CUDACC_VER_MAJOR__) "." Q35CU_STR(__CUDACC_VER_MINOR__) ")";
+}
+
+Q35_API uint64_t q35cu_launch_count(void) { return g_launches.load(); }
+
+// ------------------------------------------------------------------------
+// q35_mm.h: the reference-facing entry points
+// ------------------------------------------------------------------------
+__attribute__((visibility("default"))) float q35_mm_fp8_lut[256];
+namespace {
+std::once_flag g_lut_once;
+}
+
+Q35_API float q35_mm_e4m3_to_f32(uint8_t v)
+{
+    const int neg = v >> 7, e = (v >> 3) & 15, m = v & 7;
+    float mag;
+    if (e == 15 && m == 7) return __builtin_nanf("");
+    if (e == 0) mag = (float)m * (1.0f / 512.0f);
+    else mag = ldexpf((float)(8 + m), e - 10);
+    return neg ? -mag : mag;
+}
+
+Q35_API float q35_mm_bf16_to_f32(uint16_t v)
+{
+    uint32_t u = (uint32_t)v << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+Q35_API void q35_mm_init(void)
+{
+    std::call_once(g_lut_once, [] {
+        for (int i = 0; i < 256; ++i) q35_mm_fp8_lut[i] = q35_mm_e4m3_to_f32((uint8_t)i);
+    });
+}
+
+Q35_API const char *q35_mm_impl_fp8(void) { return "sm_100a"; }
+
+namespace {
+
+// stage X in, run `fn` (which launches on d->stream into the device output
+// region), stage Y out.  in_bytes / out_bytes are exact byte counts.
+template <class F>
+int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
+{
+    DevState *d = dev_state();
+    if (!d) return t_err;
+    const size_t in_al = (in_bytes + 255) & ~(size_t)255;
+    int rc = ensure_stage(d, in_al + out_bytes);
+    if (rc) return rc;
+    char *h = static_cast<char *>(d->h_stage);
+    char *dv = static_cast<char *>(d->d_stage);
+    memcpy(h, X, in_bytes);
+    Q35CU_CUDA(cudaMemcpyAsync(dv, h, in_bytes, cudaMemcpyHostToDevice, d->stream));
+    rc = fn(reinterpret_cast<const float *>(dv), reinterpret_cast<float *>(dv + in_al), d->stream);
+    if (rc) return rc;
+    Q35CU_CUDA(cudaMemcpyAsync(h + in_al, dv + in_al, out_bytes, cudaMemcpyDeviceToHost, d->stream));
+    Q35CU_CUDA(cudaStreamSynchronize(d->stream));
+    memcpy(Y, h + in_al, out_bytes);
+    return Q35CU_OK;
+}
+
+}  // namespace
+
+Q35_API void q35_mm_fp8(const uint8_t *W, const uint16_t *scale_bf16, uint32_t rows, uint32_t cols,
+                        const float *x, float *y)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (rows == 0) return;
+    const size_t nout = rows;
+    if (!y) { set_error(Q35CU_ERR_ARG, "q35_mm_fp8: y is NULL"); float *o[1] = {nullptr}; fail_host(o, &nout, 1); return; }
+    if (cols == 0) { memset(y, 0, (size_t)rows * 4); return; }
+    int rc = Q35CU_OK;
+    if (!W || !scale_bf16 || !x) rc = set_error(Q35CU_ERR_ARG, "q35_mm_fp8: NULL input");
+    q35cu_weight *w = rc ? nullptr : cached_weight(0, W, scale_bf16, rows, cols);
+    if (!rc && !w) rc = t_err;
+    if (!rc)
+        rc = host_call(x, (size_t)cols * 4, y, (size_t)rows * 4, [&](const float *dx, float *dy, cudaStream_t st) {
+            GemvSeg g = seg_of(w, dy, rows);
+            return launch_gemv(0, &g, 1, dx, cols, cols, 1, st);
+        });
+    if (rc) { float *o[1] = {y}; fail_host(o, &nout, 1); }
+}
+
+Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint32_t rows, uint32_t cols,
+                              uint32_t n, const float *X, float *Y)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (rows == 0 || n == 0) return;
+    const size_t nout = (size_t)rows * n;
+    if (!Y) { set_error(Q35CU_ERR_ARG, "q35_mm_fp8_batch: Y is NULL"); float *o[1] = {nullptr}; fail_host(o, &nout, 1); return; }
+    if (cols == 0) { memset(Y, 0, nout * 4); return; }
+    int rc = Q35CU_OK;
+    if (!W || !scale_bf16 || !X) rc = set_error(Q35CU_ERR_ARG, "q35_mm_fp8_batch: NULL input");
+    q35cu_weight *w = rc ? nullptr : cached_weight(0, W, scale_bf16, rows, cols);
+    if (!rc && !w) rc = t_err;
+    if (!rc)
+        rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
+            GemvSeg g = seg_of(w, dy, rows);
+            // token tiles of at most 64 per launch keep the grid's y extent small
+            for (uint32_t t0 = 0; t0 < n; t0 += 65535u * 4u) {
+                const uint32_t mt = n - t0 < 65535u * 4u ? n - t0 : 65535u * 4u;
+                GemvSeg gt = g;
+                gt.Y = dy + (size_t)t0 * rows;
+                int r = launch_gemv(0, &gt, 1, dx + (size_t)t0 * cols, cols, cols, mt, st);
+                if (r) return r;
+            }
+            return (int)Q35CU_OK;
+        });
+    if (rc) { float *o[1] = {Y}; fail_host(o, &nout, 1); }
+}
+
+Q35_API void q35_mm_fp8_multi4(const uint8_t *W[4], const uint16_t *sc[4], uint32_t rows[4], uint32_t cols,
+                               const float *x, float *y[4])
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!W || !sc || !rows || !y) { set_error(Q35CU_ERR_ARG, "q35_mm_fp8_multi4: NULL array"); fail_host(nullptr, nullptr, 0); return; }
+    uint32_t total = 0;
+    for (int s = 0; s < 4; ++s) total += rows[s];
+    if (total == 0) return;  // qwen35-c/src/q35_mm.c:187
+    float *outs[4];
+    size_t counts[4];
+    for (int s = 0; s < 4; ++s) { outs[s] = rows[s] ? y[s] : nullptr; counts[s] = rows[s]; }
+    if (cols == 0) { for (int s = 0; s < 4; ++s) if (rows[s]) memset(y[s], 0, (size_t)rows[s] * 4); return; }
+    int rc = Q35CU_OK;
+    q35cu_weight *ws[4] = {nullptr, nullptr, nullptr, nullptr};
+    if (!x) rc = set_error(Q35CU_ERR_ARG, "q35_mm_fp8_multi4: x is NULL");
+    for (int s = 0; s < 4 && !rc; ++s) {
+        if (!rows[s]) continue;
+        if (!W[s] || !sc[s] || !y[s]) { rc = set_error(Q35CU_ERR_ARG, "q35_mm_fp8_multi4: segment %d NULL", s); break; }
+        ws[s] = cached_weight(0, W[s], sc[s], rows[s], cols);
+        if (!ws[s]) rc = t_err;
+    }
+    if (!rc) {
+        // outputs of the segments packed back to back in the staging area
+        const size_t out_bytes = (size_t)total * 4;
+        DevState *d = dev_state();
+        rc = d ? Q35CU_OK : t_err;
+        if (!rc) {
+            const size_t in_al = ((size_t)cols * 4 + 255) & ~(size_t)255;
+            rc = ensure_stage(d, in_al + out_bytes);
+            if (!rc) {
+                char *h = static_cast<char *>(d->h_stage);
+                char *dv = static_cast<char *>(d->d_stage);
+                memcpy(h, x, (size_t)cols * 4);
+                GemvSeg segs[4];
+                int n = 0;
+                size_t off = 0;
+                for (int s = 0; s < 4; ++s) {
+                    if (!ws[s]) continue;
+                    segs[n++] = seg_of(ws[s], reinterpret_cast<float *>(dv + in_al) + off, rows[s]);
+                    off += rows[s];
+                }
+                cudaError_t e = cudaMemcpyAsync(dv, h, (size_t)cols * 4, cudaMemcpyHostToDevice, d->stream);
+                if (e != cudaSuccess) rc = cuda_error(e, "cudaMemcpyAsync");
+                if (!rc) rc = launch_gemv(0, segs, n, reinterpret_cast<const float *>(dv), cols, cols, 1, d->stream);
+                if (!rc) {
+                    e = cudaMemcpyAsync(h + in_al, dv + in_al, out_bytes, cudaMemcpyDeviceToHost, d->stream);
+                    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+                    if (e != cudaSuccess) rc = cuda_error(e, "copy-out");
+                }
+                if (!rc) {
+                    off = 0;
+                    for (int s = 0; s < 4; ++s) {
+                        if (!ws[s]) continue;
+                        memcpy(y[s], reinterpret_cast<float *>(h + in_al) + off, (size_t)rows[s] * 4);
+                        off += rows[s];
+                    }
+                }
+            }
+        }
+    }
+    if (rc) fail_host(outs, counts, 4);
+}
+
+Q35_API void q35_mm_bf16(const uint16_t *W, uint32_t rows, uint32_t cols, const float *x, float *y)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (rows == 0) return;
+    const size_t nout = rows;
+    if (!y) { set_error(Q35CU_ERR_ARG, "q35_mm_bf16: y is NULL"); float *o[1] = {nullptr}; fail_host(o, &nout, 1); return; }
+    if (cols == 0) { memset(y, 0, (size_t)rows * 4); return; }
+    int rc = Q35CU_OK;
+    if (!W || !x) rc = set_error(Q35CU_ERR_ARG, "q35_mm_bf16: NULL input");
+    q35cu_weight *w = rc ? nullptr : cached_weight(1, W, nullptr, rows, cols);
+    if (!rc && !w) rc = t_err;
+    if (!rc)
+        rc = host_call(x, (size_t)cols * 4, y, (size_t)rows * 4, [&](const float *dx, float *dy, cudaStream_t st) {
+            GemvSeg g = seg_of(w, dy, rows);
+            return launch_gemv(1, &g, 1, dx, cols, cols, 1, st);
+        });
+    if (rc) { float *o[1] = {y}; fail_host(o, &nout, 1); }
+}
+
+// ------------------------------------------------------------------------
+// tensor parallel: shard math (host only) and NCCL
+// ------------------------------------------------------------------------
+Q35_API int q35cu_shard_window(uint32_t rows, uint32_t cols, int mode, int rank, int world, uint32_t *row0,
+                               uint32_t *nrows, uint32_t *col0, uint32_t *ncols)
+{
+    if (!row0 || !nrows || !col0 || !ncols) return set_error(Q35CU_ERR_ARG, "shard_window: NULL output");
+    if (world < 1 || rank < 0 || rank >= world || !rows || !cols)
+        return set_error(Q35CU_ERR_ARG, "shard_window: rank %d of %d, shape %ux%u", rank, world, rows, cols);
+    const uint32_t dim = mode == Q35CU_SHARD_COLUMN ? rows : cols;
+    const uint32_t blocks = (dim + 127) / 128;
+    if ((uint32_t)world > blocks)
+        return set_error(Q35CU_ERR_ARG, "shard_window: %u blocks cannot feed %d ranks", blocks, world);
+    // equal 128-blocks per rank, the remainder spread over the first ranks
+    const uint32_t per = blocks / world, extra = blocks % world;
+    const uint32_t b0 = per * rank + (rank < (int)extra ? rank : extra);
+    const uint32_t nb = per + (rank < (int)extra ? 1 : 0);
+    uint32_t s0 = b0 * 128, len = nb * 128;
+    if (s0 + len > dim) len = dim - s0;
+    if (mode == Q35CU_SHARD_COLUMN) { *row0 = s0; *nrows = len; *col0 = 0; *ncols = cols; }
+    else { *row0 = 0; *nrows = rows; *col0 = s0; *ncols = len; }
+    return Q35CU_OK;
+}
+
+namespace {
+ncclComm_t g_comm = nullptr;
+int g_tp_rank = 0, g_tp_world = 1;
+int nccl_err(ncclResult_t r, const char *what)
+{
+    return set_error(Q35CU_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
+}
+}  // namespace
+
+Q35_API int q35cu_nccl_unique_id(void *out, size_t cap)
+{
+    if (!out || cap < sizeof(ncclUniqueId)) return set_error(Q35CU_ERR_ARG, "nccl id needs %zu bytes", sizeof(ncclUniqueId));
+    ncclUniqueId id;
+    ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return nccl_err(r, "ncclGetUniqueId");
+    memcpy(out, &id, sizeof id);
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_tp_init(int rank, int world, const void *id, size_t idlen)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!id || idlen < sizeof(ncclUniqueId) || world < 1 || rank < 0 || rank >= world)
+        return set_error(Q35CU_ERR_ARG, "tp_init: rank %d world %d", rank, world);
+    if (!dev_state()) return t_err;
+    if (g_comm) { ncclCommDestroy(g_comm); g_comm = nullptr; }
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof uid);
+    ncclResult_t r = ncclCommInitRank(&g_comm, world, uid, rank);
+    if (r != ncclSuccess) { g_comm = nullptr; return nccl_err(r, "ncclCommInitRank"); }
+    g_tp_rank = rank;
+    g_tp_world = world;
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_tp_world(void) { return g_comm ? g_tp_world : 1; }
+Q35_API int q35cu_tp_rank(void) { return g_comm ? g_tp_rank : 0; }
+
+Q35_API int q35cu_tp_finalize(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (g_comm) {
+        ncclResult_t r = ncclCommDestroy(g_comm);
+        g_comm = nullptr;
+        if (r != ncclSuccess) return nccl_err(r, "ncclCommDestroy");
+    }
+    g_tp_world = 1;
+    g_tp_rank = 0;
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_allreduce_f32(float *buf, size_t n, void *stream)
+{
+    if (!g_comm) return set_error(Q35CU_ERR_NCCL, "tensor parallel not initialised");
+    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, g_comm, pick(stream));
+    return r == ncclSuccess ? Q35CU_OK : nccl_err(r, "ncclAllReduce");
+}
+
+Q35_API int q35cu_allgather_f32(const float *send, float *recv, size_t n_per_rank, void *stream)
+{
+    if (!g_comm) return set_error(Q35CU_ERR_NCCL, "tensor parallel not initialised");
+    ncclResult_t r = ncclAllGather(send, recv, n_per_rank, ncclFloat32, g_comm, pick(stream));
+    return r == ncclSuccess ? Q35CU_OK : nccl_err(r, "ncclAllGather");
+}

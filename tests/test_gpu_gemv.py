@@ -1,0 +1,222 @@
+"""Decode GEMV on the GPU through the C-ABI, against the oracle.
+
+Every call here goes through libq35cuda's reference-facing entry points
+(q35_mm_fp8 / _batch / _multi4 / q35_mm_bf16) with host buffers, exactly as
+the engine calls them, unless a test says it uses the device API.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import mm_fixtures as M
+import q35cu
+from parity import GEMV_RTOL, gemv_report
+
+pytestmark = pytest.mark.gpu
+
+
+def _synth(orc, seed, rows, cols):
+    return orc.synth_fp8(seed, rows, cols)
+
+
+def _check(orc, W, sc, X, Y, Yref, what):
+    Y64, A = orc.mm_fp8_f64(W, sc, X)
+    rep = gemv_report(Y, Yref, Y64, A)
+    assert rep["ok"], (what, rep)
+    return rep
+
+
+@pytest.mark.parametrize("name", [c[0] for c in M.CASES])
+def test_known_answer_fixtures(gpu, golden, orc, name):
+    """qwen35-c/tests/test_mm.c: every manifest case, tol 5e-4, plus the 1e-5 rule vs the oracle."""
+    W, sc, x, yref = golden[name]
+    if sc is None:
+        y = q35cu.mm_bf16(W, x)
+        yo = orc.mm_bf16(W, x)
+        assert np.all(np.abs(y - yref) <= M.TOL + M.TOL * np.abs(yref))
+        y64 = W.astype(np.uint32) << 16
+        A = np.abs(y64.view(np.float32).astype(np.float64) * x).sum(1)
+        assert gemv_report(y, yo, yref, A)["ok"]
+        return
+    y = q35cu.mm_fp8(W, sc, x)
+    assert np.all(np.abs(y - yref) <= M.TOL + M.TOL * np.abs(yref)), name
+    _check(orc, W, sc, x, y, orc.mm_fp8(W, sc, x), name)
+
+
+def test_config0_full_size(gpu, orc, ref):
+    """C0: N=17408, K=5120, M=1 against the compiled reference q35_mm_fp8."""
+    W, sc = _synth(orc, 1001, 17408, 5120)
+    x = orc.synth_act(2001, (5120,))
+    y = q35cu.mm_fp8(W, sc, x)
+    rep = _check(orc, W, sc, x, y, ref.mm_fp8(W, sc, x), "C0")
+    # the GPU is no further from the exact product than the reference itself (+1 ulp of sum|.|)
+    assert rep["gpu_vs_f64_max_ulps_of_abs"] <= rep["ref_vs_f64_max_ulps_of_abs"] + 1.0
+
+
+@pytest.mark.parametrize("m", [1, 4, 16, 64])
+@pytest.mark.parametrize("shape", [(17408, 5120), (5120, 17408)])
+def test_config1_batch_sweep(gpu, orc, ref, shape, m):
+    """C1: gate/up [17408x5120] and down [5120x17408] at M in {1,4,16,64} (q35_mm_fp8_batch)."""
+    rows, cols = shape
+    W, sc = _synth(orc, 3000 + rows, rows, cols)
+    X = orc.synth_act(4000 + m, (m, cols))
+    Y = q35cu.mm_fp8_batch(W, sc, X)
+    _check(orc, W, sc, X, Y, ref.mm_fp8_batch(W, sc, X), f"C1 {shape} m={m}")
+
+
+def test_batch_equals_single_bitwise(gpu, orc):
+    """qwen35-c/tests/test_batch_mm.c on the GPU: batch == n x single == multi4."""
+    rows, cols, n = 10240, 5120, 5
+    W, sc = _synth(orc, 77, rows, cols)
+    X = orc.synth_act(78, (n, cols))
+    Yb = q35cu.mm_fp8_batch(W, sc, X)
+    for t in range(n):
+        assert np.array_equal(Yb[t].view(np.uint32), q35cu.mm_fp8(W, sc, X[t]).view(np.uint32))
+    m4 = q35cu.mm_fp8_multi4([W], [sc], X[0])
+    assert np.array_equal(m4[0].view(np.uint32), Yb[0].view(np.uint32))
+
+
+def test_batch_mm_reference_inputs(gpu, orc):
+    """The exact inputs of test_batch_mm (W[i]=i*7+13, zero scales): all outputs 0, batch == single."""
+    rows, cols, n = 10240, 5120, 5
+    W = ((np.arange(rows * cols, dtype=np.uint64) * 7 + 13) & 0xFF).astype(np.uint8).reshape(rows, cols)
+    sc = np.zeros((80, 40), np.uint16)
+    X = (((np.arange(n * cols) % 200) - 100) * 0.001).astype(np.float32).reshape(n, cols)
+    Yb = q35cu.mm_fp8_batch(W, sc, X)
+    Yo = orc.mm_fp8_batch(W, sc, X)
+    # NaN codes (0x7F/0xFF) times a zero scale are NaN on both sides
+    assert np.array_equal(np.isnan(Yb), np.isnan(Yo))
+    for t in range(n):
+        ys = q35cu.mm_fp8(W, sc, X[t])
+        assert np.array_equal(Yb[t].view(np.uint32), ys.view(np.uint32))
+
+
+def test_multi4_deltanet_shapes(gpu, orc, ref):
+    """q35_mm_fp8_multi4 as q35_deltanet.c:329 calls it: qkv 10240, z 6144, a 48, b 48 (K=5120)."""
+    shapes = [10240, 6144, 48, 48]
+    Ws, Ss = zip(*[_synth(orc, 500 + i, r, 5120) for i, r in enumerate(shapes)])
+    x = orc.synth_act(600, (5120,))
+    ys = q35cu.mm_fp8_multi4(list(Ws), list(Ss), x)
+    rs = ref.mm_fp8_multi4(list(Ws), list(Ss), x)
+    for W, sc, y, r in zip(Ws, Ss, ys, rs):
+        _check(orc, W, sc, x, y, r, f"multi4 {W.shape}")
+        assert np.array_equal(y.view(np.uint32), q35cu.mm_fp8(W, sc, x).view(np.uint32))
+
+
+def test_multi4_skips_zero_rows(gpu, orc):
+    W, sc = _synth(orc, 11, 256, 512)
+    x = orc.synth_act(12, (512,))
+    ys = q35cu.mm_fp8_multi4([None, W, None, W[:100]], [None, sc, None, sc[:1]], x)
+    assert ys[0] is None and ys[2] is None
+    assert np.array_equal(ys[1].view(np.uint32), q35cu.mm_fp8(W, sc, x).view(np.uint32))
+    assert np.array_equal(ys[3], ys[1][:100])
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (7, 33), (129, 129), (130, 4096), (5, 5120), (1023, 1040)])
+def test_odd_shapes(gpu, orc, ref, rows, cols):
+    """Ragged rows (not a multiple of 4 or 128) and ragged K (not a multiple of 16)."""
+    g = np.random.default_rng(rows * 31 + cols)
+    W = g.integers(0, 256, size=(rows, cols), dtype=np.uint8)
+    W[(W & 0x7F) == 0x7F] = 0x41
+    import oracle
+
+    sc = oracle.bf16_bits((g.random(((rows + 127) // 128, (cols + 127) // 128)) + 0.5).astype(np.float32))
+    X = g.standard_normal((3, cols)).astype(np.float32)
+    _check(orc, W, sc, X[0], q35cu.mm_fp8(W, sc, X[0]), ref.mm_fp8(W, sc, X[0]), "single")
+    _check(orc, W, sc, X, q35cu.mm_fp8_batch(W, sc, X), ref.mm_fp8_batch(W, sc, X), "batch")
+
+
+def test_zero_sizes(gpu):
+    W = np.zeros((4, 8), np.uint8)
+    sc = np.zeros((1, 1), np.uint16)
+    y = np.full(4, 7.0, np.float32)
+    q35cu.load().q35_mm_fp8(q35cu._p(W, q35cu._u8p), q35cu._p(sc, q35cu._u16p), 0, 8,
+                            q35cu._p(np.zeros(8, np.float32), q35cu._f32p), q35cu._p(y, q35cu._f32p))
+    assert np.all(y == 7.0)  # rows == 0: nothing written
+    q35cu.load().q35_mm_fp8(q35cu._p(W, q35cu._u8p), q35cu._p(sc, q35cu._u16p), 4, 0,
+                            q35cu._p(np.zeros(8, np.float32), q35cu._f32p), q35cu._p(y, q35cu._f32p))
+    assert np.all(y == 0.0)  # cols == 0: empty sums
+
+
+def test_nan_codes_propagate(gpu, orc):
+    W, sc = _synth(orc, 21, 256, 256)
+    W[5, 17] = 0x7F
+    W[200, 3] = 0xFF
+    x = orc.synth_act(22, (256,))
+    y = q35cu.mm_fp8(W, sc, x)
+    assert np.isnan(y[5]) and np.isnan(y[200])
+    assert np.isfinite(np.delete(y, [5, 200])).all()
+
+
+def test_repeatable_and_cached(gpu, orc):
+    W, sc = _synth(orc, 31, 4096, 5120)
+    x = orc.synth_act(32, (5120,))
+    a = q35cu.mm_fp8(W, sc, x)
+    before = q35cu.load().q35cu_cache_bytes()
+    b = q35cu.mm_fp8(W, sc, x)
+    assert q35cu.load().q35cu_cache_bytes() == before  # second call hit the cache
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert q35cu.load().q35cu_forget(W.ctypes.data) == 1
+
+
+def test_bf16_lm_head_shape(gpu, orc, ref):
+    """q35_mm_bf16 (the lm_head matvec), a 16384-row slice of 248320x5120."""
+    g = np.random.default_rng(41)
+    import oracle
+
+    W16 = oracle.bf16_bits(g.standard_normal((16384, 5120)).astype(np.float32) * 0.02)
+    x = g.standard_normal(5120).astype(np.float32)
+    y = q35cu.mm_bf16(W16, x)
+    yr = ref.mm_bf16(W16, x)
+    wf = (W16.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    y64 = wf @ x.astype(np.float64)
+    A = np.abs(wf * x).sum(1)
+    assert gemv_report(y, yr, y64, A)["ok"]
+
+
+def test_device_api_and_synth(gpu, orc):
+    """Device-resident synthetic weight == the host generator; device-pointer gemv == host ABI."""
+    import torch
+
+    w = q35cu.Weight.synth_fp8(123, 1024, 5120)
+    try:
+        Wd, scd = w.download_fp8()
+        Wh, sch = orc.synth_fp8(123, 1024, 5120)
+        assert np.array_equal(scd, sch)
+        assert (Wd != Wh).mean() < 1e-4  # libm vs CUDA logf/cosf may move a rare element by one code
+        X = torch.from_numpy(orc.synth_act(124, (4, 5120))).cuda()
+        Y = torch.empty((4, 1024), device="cuda")
+        q35cu.gemv(w, X, Y)
+        torch.cuda.synchronize()
+        Yh = q35cu.mm_fp8_batch(Wd, scd, X.cpu().numpy())
+        assert np.array_equal(Y.cpu().numpy().view(np.uint32), Yh.view(np.uint32))
+    finally:
+        w.free()
+
+
+def test_budget_reports_nomem_and_nan(gpu, orc):
+    lib = q35cu.load()
+    lib.q35cu_release_all()
+    W, sc = _synth(orc, 51, 2048, 2048)
+    x = orc.synth_act(52, (2048,))
+    lib.q35cu_set_memory_budget(1 << 20)  # smaller than the weight
+    try:
+        lib.q35cu_clear_error()
+        y = q35cu.mm_fp8(W, sc, x)
+        code, msg = q35cu.last_error()
+        assert code == q35cu.ERR_NOMEM and "budget" in msg
+        assert np.isnan(y).all()
+    finally:
+        lib.q35cu_set_memory_budget(0)
+    y = q35cu.mm_fp8(W, sc, x)
+    assert np.isfinite(y).all()
+
+
+def test_bad_arguments_are_recorded(gpu):
+    lib = q35cu.load()
+    lib.q35cu_clear_error()
+    y = np.zeros(8, np.float32)
+    lib.q35_mm_fp8(None, None, 8, 16, None, q35cu._p(y, q35cu._f32p))
+    assert q35cu.last_error()[0] == q35cu.ERR_ARG
+    assert np.isnan(y).all()

@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=64, help="decode-stack depth (64 = configuration 3)")
     ap.add_argument("--no-extras", action="store_true", help="skip the C0/C1 sweep, e2e and CPU baseline")
+    ap.add_argument("--profile-c0", action="store_true",
+                    help="only the isolated configuration-0 GEMV (a small command for ncu captures)")
     return ap.parse_args()
 
 
@@ -542,8 +544,22 @@ def run_ours(args):
     return 0
 
 
+def run_profile_c0(args):
+    import torch
+
+    import q35cu
+
+    torch.cuda.set_device(0)
+    q35cu.check(q35cu.load().q35cu_set_device(0))
+    r = time_gemv_rotating(q35cu, torch, 17408, 5120, 1, copies=5, rounds=max(1, args.steps))
+    print(json.dumps({"config0_gemv": r}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.profile_c0:
+        return run_profile_c0(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

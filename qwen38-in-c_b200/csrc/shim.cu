@@ -109,7 +109,8 @@ struct KeyHash {
 };
 struct Entry {
     q35cu_weight *w;
-    bool owned;  // false for q35cu_weight_bind
+    bool owned;    // false for q35cu_weight_bind
+    uint64_t fp;   // content fingerprint of the host tensor at upload
 };
 
 std::recursive_mutex g_mu;
@@ -312,12 +313,63 @@ int weight_fill_fp8(q35cu_weight *w, const uint8_t *W, const uint16_t *sc, uint3
     return Q35CU_OK;
 }
 
+// Content fingerprint of a host weight: the whole scale grid (up to 64 KB)
+// plus 16 evenly spaced 8-byte words of W.  A cache hit whose fingerprint
+// differs (the caller freed the tensor and reused the address for another
+// one) is treated as a miss.  Q35CU_CACHE_CHECK=0 skips the check.
+uint64_t fingerprint(const void *W, size_t wbytes, const void *S, size_t sbytes)
+{
+    uint64_t h = 0x9E3779B97F4A7C15ULL ^ wbytes;
+    auto mix = [&h](uint64_t v) {
+        h ^= v;
+        h *= 0xFF51AFD7ED558CCDULL;
+        h ^= h >> 32;
+    };
+    const uint8_t *s = static_cast<const uint8_t *>(S);
+    if (sbytes > 65536) sbytes = 65536;
+    size_t i = 0;
+    for (; i + 8 <= sbytes; i += 8) {
+        uint64_t v;
+        memcpy(&v, s + i, 8);
+        mix(v);
+    }
+    for (; i < sbytes; ++i) mix(s[i]);
+    const uint8_t *w = static_cast<const uint8_t *>(W);
+    const size_t take = wbytes < 8 ? wbytes : 8;
+    for (int j = 0; j < 16; ++j) {
+        const size_t off = wbytes <= 8 ? 0 : (wbytes - 8) * j / 15;
+        uint64_t v = 0;
+        memcpy(&v, w + off, take);
+        mix(v);
+    }
+    return h;
+}
+
+bool cache_check_enabled()
+{
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("Q35CU_CACHE_CHECK");
+        on = !(e && !strcmp(e, "0"));
+    }
+    return on != 0;
+}
+
 // find or upload the weight for a host key (q35_mm_* path)
 q35cu_weight *cached_weight(int kind, const void *W, const void *sc, uint32_t rows, uint32_t cols)
 {
     Key k{W, sc, rows, cols, kind};
+    const size_t wbytes = (size_t)rows * cols * (kind == 0 ? 1 : 2);
+    const size_t sbytes = kind == 0 ? (size_t)((rows + 127) / 128) * ((cols + 127) / 128) * 2 : 0;
+    const bool verify = cache_check_enabled();
+    const uint64_t fp = verify ? fingerprint(W, wbytes, sc, sbytes) : 0;
     auto it = g_cache.find(k);
-    if (it != g_cache.end()) return it->second.w;
+    if (it != g_cache.end()) {
+        if (!it->second.owned || !verify || it->second.fp == fp) return it->second.w;
+        g_cache_bytes -= it->second.w->bytes;  // stale: same address, other contents
+        weight_release(it->second.w);
+        g_cache.erase(it);
+    }
     q35cu_weight *w = nullptr;
     if (weight_alloc(kind, rows, cols, &w)) return nullptr;
     int rc;
@@ -330,7 +382,7 @@ q35cu_weight *cached_weight(int kind, const void *W, const void *sc, uint32_t ro
                  : cuda_error(cudaGetLastError(), "cudaMemcpyAsync");
     }
     if (rc) { weight_release(w); return nullptr; }
-    g_cache.emplace(k, Entry{w, true});
+    g_cache.emplace(k, Entry{w, true, fp});
     g_cache_bytes += w->bytes;
     return w;
 }
@@ -517,7 +569,7 @@ Q35_API int q35cu_weight_bind(const uint8_t *host_W, const uint16_t *host_sc, co
         }
         g_cache.erase(it);
     }
-    g_cache.emplace(k, Entry{const_cast<q35cu_weight *>(w), false});
+    g_cache.emplace(k, Entry{const_cast<q35cu_weight *>(w), false, 0});
     return Q35CU_OK;
 }
 

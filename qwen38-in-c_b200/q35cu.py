@@ -244,12 +244,22 @@ def _ptr(t) -> int:
     return int(t.data_ptr())
 
 
-def _stream(stream) -> int | None:
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream torch reports as handle 0
+
+
+def _stream(stream) -> int:
+    """The CUDA stream handle to launch on: torch's current stream by default.
+
+    A NULL handle means "the library's own stream" to the C-ABI, so torch's
+    legacy default stream (handle 0) is passed as cudaStreamLegacy instead;
+    launches then land on the stream the caller's events and copies use.
+    """
     if stream is None:
         import torch
 
-        return int(torch.cuda.current_stream().cuda_stream)
-    return int(stream)
+        stream = torch.cuda.current_stream().cuda_stream
+    s = int(stream)
+    return s if s != 0 else CUDA_STREAM_LEGACY
 
 
 def gemv(w: Weight, X, Y, m: int | None = None, stream=None) -> None:

@@ -16,6 +16,15 @@ from parity import GEMV_RTOL, gemv_report
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _fresh_cache(gpu):
+    # numpy may hand a new array the address of a freed one; start every test
+    # with an empty residency cache (the fingerprint check is tested below)
+    gpu.q35cu_release_all()
+    yield
+    gpu.q35cu_release_all()
+
+
 def _synth(orc, seed, rows, cols):
     return orc.synth_fp8(seed, rows, cols)
 
@@ -220,3 +229,16 @@ def test_bad_arguments_are_recorded(gpu):
     lib.q35_mm_fp8(None, None, 8, 16, None, q35cu._p(y, q35cu._f32p))
     assert q35cu.last_error()[0] == q35cu.ERR_ARG
     assert np.isnan(y).all()
+
+
+def test_cache_detects_reused_address(gpu, orc):
+    """Same host address and shape, new contents: the fingerprint forces a re-upload."""
+    W, sc = _synth(orc, 61, 512, 1024)
+    x = orc.synth_act(62, (1024,))
+    a = q35cu.mm_fp8(W, sc, x)
+    W2, sc2 = _synth(orc, 63, 512, 1024)
+    W[...] = W2          # same buffers, other tensor
+    sc[...] = sc2
+    b = q35cu.mm_fp8(W, sc, x)
+    assert np.array_equal(b.view(np.uint32), q35cu.mm_fp8(W2, sc2, x).view(np.uint32))
+    assert not np.array_equal(a, b)

@@ -515,7 +515,7 @@ def run_ours(args):
             "gpu_launches": main["kernels_per_step"] * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "traffic": traffic,
-                         "kernel": "gemv_vec_kernel<fp8,1> (decode GEMV), all launches of one step",
+                         "kernel": "gemv_rs_kernel (decode GEMV, row stream), all launches of one step",
                          "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
                          "launches_timed": nl, "algorithmic_bytes_per_launch": round(bytes_per_launch),
                          "us_per_launch": round(s_per_launch * 1e6, 2)},

@@ -18,6 +18,7 @@ struct q35cu_weight {
     uint32_t rows_blk, cols_blk;
     size_t bytes;        // device bytes held
     int device;
+    uint32_t has_nan;    // FP8 weight holds NaN codes 0x7F / 0xFF (set by the upload scan)
 };
 
 namespace q35cu {
@@ -46,14 +47,14 @@ struct GemvSeg {
     float *Y;           // output for this segment, token-major [m, ldy]
     uint32_t rows;
     uint32_t ldy;
-    uint32_t wpt;       // warps that split K for one task (1, 2, 4, 8)
-    uint32_t cta_begin; // first CTA of this segment in the grid
+    uint32_t has_nan;   // weight holds e4m3 NaN codes
 };
 
 int launch_gemv(int kind, const GemvSeg *segs, int nseg, const float *X,
                 uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st);
 int launch_swiglu(const float *g, const float *u, float *o, size_t n, cudaStream_t st);
-uint32_t gemv_wpt(uint32_t rows, uint32_t K, int sms);
+void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes);
+int scan_nan_codes(const uint8_t *W, size_t bytes, uint32_t *d_flag, cudaStream_t st, bool *has_nan);
 
 int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y,
                     cudaStream_t st);

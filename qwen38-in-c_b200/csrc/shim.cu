@@ -12,7 +12,8 @@
 //   * errors: the signatures return void, so by default a failure aborts
 //     with a message; Q35CU_ON_ERROR=record (or q35cu_set_error_mode) makes
 //     it record the error and fill the outputs with NaN instead.
-#include <nccl.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types only: NCCL is resolved at run time (see load_nccl)
 
 #include <cstdarg>
 #include <cstdio>
@@ -87,6 +88,7 @@ struct DevState {
     size_t h_cap = 0;
     void *d_stage = nullptr;  // device, in + out
     size_t d_cap = 0;
+    uint32_t *d_flag = nullptr;  // 4-byte scratch word for upload scans
 };
 
 struct Key {
@@ -157,6 +159,8 @@ DevState *dev_state()
         d.major = p.major;
         e = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking);
         if (e != cudaSuccess) { cuda_error(e, "cudaStreamCreate"); return nullptr; }
+        e = cudaMalloc(reinterpret_cast<void **>(&d.d_flag), 16);
+        if (e != cudaSuccess) { cuda_error(e, "cudaMalloc(flag)"); return nullptr; }
         d.ready = true;
     }
     return &d;
@@ -309,7 +313,10 @@ int weight_fill_fp8(q35cu_weight *w, const uint8_t *W, const uint16_t *sc, uint3
     Q35CU_CUDA(cudaMemcpyAsync(d->d_stage, hs, n * 2, cudaMemcpyHostToDevice, st));
     rc = launch_bf16_to_f32_scales(static_cast<uint16_t *>(d->d_stage), w->d_s, n, st);
     if (rc) return rc;
-    Q35CU_CUDA(cudaStreamSynchronize(st));
+    bool nan = false;
+    rc = scan_nan_codes(static_cast<const uint8_t *>(w->d_w), (size_t)w->rows * w->cols, d->d_flag, st, &nan);
+    if (rc) return rc;
+    w->has_nan = nan;
     return Q35CU_OK;
 }
 
@@ -362,10 +369,12 @@ q35cu_weight *cached_weight(int kind, const void *W, const void *sc, uint32_t ro
     const size_t wbytes = (size_t)rows * cols * (kind == 0 ? 1 : 2);
     const size_t sbytes = kind == 0 ? (size_t)((rows + 127) / 128) * ((cols + 127) / 128) * 2 : 0;
     const bool verify = cache_check_enabled();
-    const uint64_t fp = verify ? fingerprint(W, wbytes, sc, sbytes) : 0;
     auto it = g_cache.find(k);
+    // a bound entry's host key need not hold the tensor (q35cu_weight_bind): never read it
+    if (it != g_cache.end() && !it->second.owned) return it->second.w;
+    const uint64_t fp = verify ? fingerprint(W, wbytes, sc, sbytes) : 0;
     if (it != g_cache.end()) {
-        if (!it->second.owned || !verify || it->second.fp == fp) return it->second.w;
+        if (!verify || it->second.fp == fp) return it->second.w;
         g_cache_bytes -= it->second.w->bytes;  // stale: same address, other contents
         weight_release(it->second.w);
         g_cache.erase(it);
@@ -395,6 +404,7 @@ GemvSeg seg_of(const q35cu_weight *w, float *Y, uint32_t ldy)
     g.Y = Y;
     g.rows = w->rows;
     g.ldy = ldy;
+    g.has_nan = w->has_nan;
     return g;
 }
 
@@ -533,7 +543,9 @@ Q35_API int q35cu_weight_synth_fp8(uint64_t seed, float stddev, uint32_t grows, 
     DevState *d = dev_state();
     rc = launch_synth_fp8(seed, stddev, grows, gcols, row0, col0, nrows, ncols, static_cast<uint8_t *>(w->d_w),
                           w->d_s, d->stream);
-    if (!rc && cudaStreamSynchronize(d->stream) != cudaSuccess) rc = cuda_error(cudaGetLastError(), "synth sync");
+    bool nan = false;
+    if (!rc) rc = scan_nan_codes(static_cast<const uint8_t *>(w->d_w), (size_t)nrows * ncols, d->d_flag, d->stream, &nan);
+    if (!rc) w->has_nan = nan;
     if (rc) { weight_release(w); return rc; }
     *out = w;
     return Q35CU_OK;
@@ -880,17 +892,57 @@ Q35_API int q35cu_shard_window(uint32_t rows, uint32_t cols, int mode, int rank,
 namespace {
 ncclComm_t g_comm = nullptr;
 int g_tp_rank = 0, g_tp_world = 1;
+
+// NCCL is not a link-time dependency: a process that already holds a NCCL
+// (torch's, for instance) keeps it, and one that never uses tensor
+// parallelism never loads it.  Q35CU_NCCL_LIB names a library to dlopen
+// when none is loaded yet.
+struct Nccl {
+    bool ok = false;
+    decltype(&ncclGetUniqueId) GetUniqueId = nullptr;
+    decltype(&ncclCommInitRank) CommInitRank = nullptr;
+    decltype(&ncclCommDestroy) CommDestroy = nullptr;
+    decltype(&ncclAllReduce) AllReduce = nullptr;
+    decltype(&ncclAllGather) AllGather = nullptr;
+    decltype(&ncclGetErrorString) GetErrorString = nullptr;
+} g_nccl;
+
+int load_nccl()
+{
+    if (g_nccl.ok) return Q35CU_OK;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) {
+        const char *e = getenv("Q35CU_NCCL_LIB");
+        h = dlopen(e && *e ? e : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    }
+    if (!h) return set_error(Q35CU_ERR_NCCL, "cannot load NCCL: %s", dlerror());
+#define Q35CU_SYM(n)                                                                   \
+    g_nccl.n = reinterpret_cast<decltype(g_nccl.n)>(dlsym(h, "nccl" #n));              \
+    if (!g_nccl.n) return set_error(Q35CU_ERR_NCCL, "NCCL lacks nccl%s", #n);
+    Q35CU_SYM(GetUniqueId)
+    Q35CU_SYM(CommInitRank)
+    Q35CU_SYM(CommDestroy)
+    Q35CU_SYM(AllReduce)
+    Q35CU_SYM(AllGather)
+    Q35CU_SYM(GetErrorString)
+#undef Q35CU_SYM
+    g_nccl.ok = true;
+    return Q35CU_OK;
+}
+
 int nccl_err(ncclResult_t r, const char *what)
 {
-    return set_error(Q35CU_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
+    return set_error(Q35CU_ERR_NCCL, "%s: %s", what, g_nccl.GetErrorString ? g_nccl.GetErrorString(r) : "?");
 }
 }  // namespace
 
 Q35_API int q35cu_nccl_unique_id(void *out, size_t cap)
 {
     if (!out || cap < sizeof(ncclUniqueId)) return set_error(Q35CU_ERR_ARG, "nccl id needs %zu bytes", sizeof(ncclUniqueId));
+    int rc = load_nccl();
+    if (rc) return rc;
     ncclUniqueId id;
-    ncclResult_t r = ncclGetUniqueId(&id);
+    ncclResult_t r = g_nccl.GetUniqueId(&id);
     if (r != ncclSuccess) return nccl_err(r, "ncclGetUniqueId");
     memcpy(out, &id, sizeof id);
     return Q35CU_OK;
@@ -902,10 +954,12 @@ Q35_API int q35cu_tp_init(int rank, int world, const void *id, size_t idlen)
     if (!id || idlen < sizeof(ncclUniqueId) || world < 1 || rank < 0 || rank >= world)
         return set_error(Q35CU_ERR_ARG, "tp_init: rank %d world %d", rank, world);
     if (!dev_state()) return t_err;
-    if (g_comm) { ncclCommDestroy(g_comm); g_comm = nullptr; }
+    int rc = load_nccl();
+    if (rc) return rc;
+    if (g_comm) { g_nccl.CommDestroy(g_comm); g_comm = nullptr; }
     ncclUniqueId uid;
     memcpy(&uid, id, sizeof uid);
-    ncclResult_t r = ncclCommInitRank(&g_comm, world, uid, rank);
+    ncclResult_t r = g_nccl.CommInitRank(&g_comm, world, uid, rank);
     if (r != ncclSuccess) { g_comm = nullptr; return nccl_err(r, "ncclCommInitRank"); }
     g_tp_rank = rank;
     g_tp_world = world;
@@ -919,7 +973,7 @@ Q35_API int q35cu_tp_finalize(void)
 {
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     if (g_comm) {
-        ncclResult_t r = ncclCommDestroy(g_comm);
+        ncclResult_t r = g_nccl.CommDestroy(g_comm);
         g_comm = nullptr;
         if (r != ncclSuccess) return nccl_err(r, "ncclCommDestroy");
     }
@@ -931,13 +985,13 @@ Q35_API int q35cu_tp_finalize(void)
 Q35_API int q35cu_allreduce_f32(float *buf, size_t n, void *stream)
 {
     if (!g_comm) return set_error(Q35CU_ERR_NCCL, "tensor parallel not initialised");
-    ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, g_comm, pick(stream));
+    ncclResult_t r = g_nccl.AllReduce(buf, buf, n, ncclFloat32, ncclSum, g_comm, pick(stream));
     return r == ncclSuccess ? Q35CU_OK : nccl_err(r, "ncclAllReduce");
 }
 
 Q35_API int q35cu_allgather_f32(const float *send, float *recv, size_t n_per_rank, void *stream)
 {
     if (!g_comm) return set_error(Q35CU_ERR_NCCL, "tensor parallel not initialised");
-    ncclResult_t r = ncclAllGather(send, recv, n_per_rank, ncclFloat32, g_comm, pick(stream));
+    ncclResult_t r = g_nccl.AllGather(send, recv, n_per_rank, ncclFloat32, g_comm, pick(stream));
     return r == ncclSuccess ? Q35CU_OK : nccl_err(r, "ncclAllGather");
 }

@@ -307,13 +307,22 @@ def shard_window(rows: int, cols: int, mode: int, rank: int, world: int):
     return r0.value, nr.value, c0.value, nc.value
 
 
+def _torch_nccl_first() -> None:
+    """libq35cuda resolves NCCL at run time and reuses a NCCL already in the
+    process.  torch links its own (newer) NCCL under the same soname, so it
+    must be imported before the library loads one."""
+    import torch  # noqa: F401
+
+
 def nccl_unique_id() -> bytes:
+    _torch_nccl_first()
     buf = C.create_string_buffer(128)
     check(load().q35cu_nccl_unique_id(buf, 128))
     return buf.raw
 
 
 def tp_init(rank: int, world: int, uid: bytes) -> None:
+    _torch_nccl_first()
     buf = C.create_string_buffer(uid, len(uid))
     check(load().q35cu_tp_init(rank, world, buf, len(uid)))
 

@@ -146,6 +146,11 @@ int q35cu_allgather_f32(const float *send, float *recv, size_t n_per_rank, void 
 const char *q35cu_build_info(void);
 /* Kernel launches this library issued since load (all entry points). */
 uint64_t q35cu_launch_count(void);
+/* The device status word of the current device: 0, or the q35cu_status of
+ * a bounded device-side wait that gave up (Q35CU_ERR_TIMEOUT) since the
+ * last clear.  Asynchronous device-pointer callers check it after a
+ * synchronisation; the q35_mm_* entry points check it on every call. */
+int q35cu_device_status(uint32_t *status, int clear);
 
 #ifdef __cplusplus
 }

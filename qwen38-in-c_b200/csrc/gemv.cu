@@ -9,44 +9,44 @@
 // (x2 for bf16) + 4*ceil(rows/128)*ceil(cols/128) scale bytes
 // + 4*m*cols activation bytes + 4*m*rows output bytes.
 //
-// Decomposition ("row stream"):
-//   * one CTA per SM; CTA c owns the contiguous virtual rows
-//     [c*R/G, (c+1)*R/G) of the launch (R = rows of all segments, G = grid),
-//     so every SM streams the same number of bytes (no partial waves);
-//   * thread t owns a fixed K-slice: 16 bytes (one 16-byte vector) per pass
-//     at k = p*T*16 + t*16, with T = blockDim.x and P = ceil(K/16/T) passes,
-//     T and P a function of K only.  Its activation slice x[k..k+16) stays
-//     in registers for the whole kernel when P == 1;
-//   * rows stream through a double-buffered register pipeline in groups of
-//     GR rows: the next group's 16-byte loads (and block scales) are issued
-//     before the current group is converted and multiplied, across block,
-//     pass and segment boundaries;
-//   * per row and pass the thread forms d = sum_{j<16} w_j x_j and folds
-//     part_r = fma(s[r/128, k/128], d, part_r);
+// Decomposition (one CTA per SM, "row stream"):
+//   * CTA c owns the contiguous virtual rows [c*R/G, (c+1)*R/G) of the launch
+//     (R = rows of all segments, G = grid), so every SM streams the same
+//     number of bytes and there is no partial wave;
+//   * a producer warp streams those rows, a few whole rows per stage, into a
+//     shared-memory ring with cp.async.bulk (TMA bulk copies completing on
+//     mbarriers): memory-level parallelism comes from the copy engine, not
+//     from registers, so the ring keeps ~100 KB per SM in flight;
+//   * consumer thread t owns a fixed K-slice -- one 16-byte vector per pass
+//     at k = p*T*16 + t*16 (T consumer threads, P = ceil(K/16/T) passes, both
+//     a function of K only) -- and keeps x[k..k+16) of every pass and token
+//     in registers for the whole kernel; it reads its vector of each staged
+//     row from shared memory (a warp reads 512 contiguous bytes) and folds
+//       part_r = fma(s[r/128, k/128], sum_{j<16} w_j x_j, part_r)
+//     in pass order;
 //   * every 32/MT rows the 32 x 32 partials of a warp are reduced with a
-//     transpose butterfly (31 shuffles; the same association as a plain xor
-//     butterfly), warps are summed in fixed order through shared memory and
-//     one thread per (row, token) writes Y.
-// The per-row arithmetic is therefore independent of m, of the token tile
-// width and of the other weights sharing a launch: batch, multi and single
-// calls agree bit for bit (the contract of qwen35-c/tests/test_batch_mm.c),
-// and repeated runs are identical (no atomics).
+//     transpose butterfly (31 shuffles, the association of a plain xor
+//     butterfly), the warps are summed in fixed order through shared memory
+//     and one thread per (row, token) writes Y.
+// The per-row arithmetic is therefore independent of m, of the token tile,
+// of the ring geometry and of the other weights sharing a launch: batch,
+// multi and single calls agree bit for bit (the contract of
+// qwen35-c/tests/test_batch_mm.c), and repeated runs are identical.
 //
-// e4m3 decoding.  The hardware unpack (cvt.rn.{f16x2,bf16x2}.e4m3x2) runs on
-// the quarter-rate XU pipe, which would cap the kernel below HBM speed if it
-// decoded every byte.  Variant CONV splits each vector: half through the
-// hardware unpack, half through an ALU bit transform that places the 7
-// exponent+mantissa bits of e4m3 under an f16 exponent (value * 2^-8 exactly,
-// subnormals included; the 2^8 is restored by one exact fma per vector).  The
-// bit transform maps the NaN codes 0x7F/0xFF to finite values, so a weight
-// in which the upload scan found a NaN code takes a checked path that turns
-// the affected dot products into NaN, as the reference's LUT does.
+// e4m3 decoding uses the hardware unpack cvt.rn.f16x2.e4m3x2 (exact; NaN
+// codes stay NaN, as in the reference's LUT) and products run as packed
+// fma.rn.f32x2: about two issued instructions per weight byte.
 //
 // Programmatic dependent launch: the kernel triggers its dependents at
-// entry and issues its first weight loads before griddepcontrol.wait, so in
-// a chain of projections the next kernel's weight stream starts while the
-// previous kernel drains.  Nothing is written and no activation is read
-// before the wait.
+// entry; the producer streams weights without waiting for the previous
+// kernel, and only the consumers execute griddepcontrol.wait before they
+// read activations, so in a chain of projections the next weight stream
+// starts while the previous kernel drains.
+//
+// Every mbarrier wait is bounded.  A wait that gives up records
+// Q35CU_ERR_TIMEOUT in the device status word (read by q35cu_device_status),
+// and the CTA winds down: the producer stops issuing and waits, bounded, for
+// the copies it has in flight before the CTA exits.
 #include <cuda_fp16.h>
 
 #include <type_traits>
@@ -54,41 +54,80 @@
 #include "q35cu_internal.h"
 
 namespace q35cu {
+
+// bounded device-side waits that gave up leave their code here
+__device__ uint32_t g_device_status;
+
 namespace {
 
-constexpr int kMaxThreads = 384;
-constexpr int kMaxWarps = kMaxThreads / 32;
+constexpr int kMaxCons = 384;  // consumer threads per CTA
+constexpr int kMaxWarps = kMaxCons / 32;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kFull = 0xffffffffu;
+constexpr uint32_t kRingBudget = 100 * 1024;
 
 struct Seg {
     const uint8_t *W;
     const float *S;
     float *Y;
     uint32_t rows, ldy, vbegin;  // vbegin: first virtual row of the segment
-    uint32_t has_nan;            // weight holds e4m3 NaN codes (0x7F / 0xFF)
+    uint32_t has_nan;
 };
 
 struct Args {
     Seg seg[4];
     const float *X;
-    uint32_t K, ldx, m, kblocks, total_rows, passes;
+    uint32_t K, ldx, m, kblocks, total_rows;
+    uint32_t cons;         // consumer threads (multiple of 32)
+    uint32_t stages;       // ring slots
+    uint32_t slot_bytes;   // bytes of one ring slot (stage rows * row bytes)
     int nseg;
 };
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-__device__ __forceinline__ uint4 ld_stream(const void *p)
+__device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count)
 {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait; false = gave up (status recorded)
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity)
+{
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(b, parity)) return true;
+    atomicExch(&g_device_status, (uint32_t)Q35CU_ERR_TIMEOUT);
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(saddr(dst)), "l"(src), "r"(bytes), "r"(saddr(bar))
+                 : "memory");
 }
 
-// ---- e4m3 decoding -------------------------------------------------------
-// hardware: bytes (b1 b0) of the low half -> f16x2 (b0 low), exact
+// ---- decoding + dot products ---------------------------------------------
 __device__ __forceinline__ void hw_f16x2(uint32_t w, uint32_t &lo, uint32_t &hi)
 {
     asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
@@ -96,18 +135,7 @@ __device__ __forceinline__ void hw_f16x2(uint32_t w, uint32_t &lo, uint32_t &hi)
         : "=r"(lo), "=r"(hi)
         : "r"(w));
 }
-// ALU: f16x2 holding value * 2^-8 of bytes b0 (low) and b1 (high) of
-// h = [b1 0 b0 0] (a prmt of the word); sign to bit 15, E and M under the
-// f16 exponent/mantissa: exact for normals and subnormals alike.
-__device__ __forceinline__ uint32_t bt_f16x2(uint32_t h)
-{
-    return ((h & 0x7F007F00u) >> 1) | (h & 0x80008000u);
-}
-__device__ __forceinline__ float2 h2f(uint32_t h)
-{
-    return __half22float2(*reinterpret_cast<__half2 *>(&h));
-}
-
+__device__ __forceinline__ float2 h2f(uint32_t h) { return __half22float2(*reinterpret_cast<__half2 *>(&h)); }
 __device__ __forceinline__ unsigned long long pk(float a, float b)
 {
     return (unsigned long long)__float_as_uint(a) | ((unsigned long long)__float_as_uint(b) << 32);
@@ -121,50 +149,23 @@ __device__ __forceinline__ float hsum2(unsigned long long v)
     return __uint_as_float((uint32_t)v) + __uint_as_float((uint32_t)(v >> 32));
 }
 
-// any byte of w equal to 0x7F or 0xFF
-__device__ __forceinline__ bool nan_code(uint32_t w)
-{
-    return __vcmpeq4(w | 0x80808080u, 0xFFFFFFFFu) != 0u;
-}
-
-// dot of one 16-byte fp8 vector with x[16]
-template <int CONV>
-__device__ __forceinline__ float dot_fp8(const uint4 &v, const float *x, bool check_nan)
+// 16 e4m3 values . x[16]: two packed accumulators (even/odd pairs of words)
+__device__ __forceinline__ float dot_fp8(const uint4 &v, const float *x)
 {
     unsigned long long a = 0ull, b = 0ull;
     const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-    if constexpr (CONV == 0) {  // all hardware
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t lo, hi;
-            hw_f16x2(wd[q], lo, hi);
-            const float2 f0 = h2f(lo), f1 = h2f(hi);
-            fma2(q < 2 ? a : b, f0.x, f0.y, x[4 * q], x[4 * q + 1]);
-            fma2(q < 2 ? a : b, f1.x, f1.y, x[4 * q + 2], x[4 * q + 3]);
-        }
-        return hsum2(a) + hsum2(b);
-    } else {  // words 0,1 hardware, words 2,3 bit transform (x 2^-8)
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            uint32_t lo, hi;
-            hw_f16x2(wd[q], lo, hi);
-            const float2 f0 = h2f(lo), f1 = h2f(hi);
-            fma2(a, f0.x, f0.y, x[4 * q], x[4 * q + 1]);
-            fma2(a, f1.x, f1.y, x[4 * q + 2], x[4 * q + 3]);
-        }
-#pragma unroll
-        for (int q = 2; q < 4; ++q) {
-            const float2 f0 = h2f(bt_f16x2(__byte_perm(wd[q], 0u, 0x1404)));
-            const float2 f1 = h2f(bt_f16x2(__byte_perm(wd[q], 0u, 0x3424)));
-            fma2(b, f0.x, f0.y, x[4 * q], x[4 * q + 1]);
-            fma2(b, f1.x, f1.y, x[4 * q + 2], x[4 * q + 3]);
-        }
-        float d = fmaf(256.0f, hsum2(b), hsum2(a));
-        if (check_nan && (nan_code(v.z) || nan_code(v.w))) d = __int_as_float(0x7fffffff);
-        return d;
+    for (int q = 0; q < 4; ++q) {
+        uint32_t lo, hi;
+        hw_f16x2(wd[q], lo, hi);
+        const float2 f0 = h2f(lo), f1 = h2f(hi);
+        fma2(q & 1 ? b : a, f0.x, f0.y, x[4 * q], x[4 * q + 1]);
+        fma2(q & 1 ? b : a, f1.x, f1.y, x[4 * q + 2], x[4 * q + 3]);
     }
+    return hsum2(a) + hsum2(b);
 }
 
+// 8 bf16 values . x[8]
 __device__ __forceinline__ float dot_bf16(const uint4 &v, const float *x)
 {
     unsigned long long a = 0ull;
@@ -191,81 +192,101 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[32], uint32_t lane)
     return v[0];
 }
 
-// position of one row group in the CTA's walk over (block, pass, group)
-struct Pos {
-    uint32_t b0, b1;  // block: virtual rows [b0, b1)
-    uint32_t p, g;    // pass, group index inside the block
+// the CTA's walk over blocks (<= BR rows, inside one segment) and stages
+// (<= R rows of a block); identical for the producer and the consumers
+struct Walk {
+    uint32_t b0, b1;  // block rows [b0, b1) (virtual)
+    uint32_t r0;      // first row of the current stage
     int s;            // segment
     bool ok;
 };
 
-template <int KIND, int CONV, int MT, int GR>
-__global__ void __launch_bounds__(kMaxThreads, 1) gemv_rs_kernel(const __grid_constant__ Args a)
+template <int BR>
+__device__ __forceinline__ Walk walk_block(const Args &a, uint32_t vr, uint32_t vr1)
+{
+    Walk w;
+    w.ok = vr < vr1;
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < 4; ++i)
+        if (i < a.nseg && vr >= a.seg[i].vbegin) s = i;
+    w.s = s;
+    const uint32_t send = a.seg[s].vbegin + a.seg[s].rows;
+    uint32_t e = vr + BR;
+    e = e < vr1 ? e : vr1;
+    w.b0 = vr;
+    w.b1 = e < send ? e : send;
+    w.r0 = vr;
+    return w;
+}
+
+template <int KIND, int MT, int P, int R>
+__global__ void __launch_bounds__(kMaxCons + 32, 1) gemv_tma_kernel(const __grid_constant__ Args a)
 {
     constexpr uint32_t EPV = KIND == 0 ? 16 : 8;  // values per 16-byte vector
     constexpr uint32_t ESZ = KIND == 0 ? 1 : 2;
     constexpr int BR = 32 / MT;                   // rows per reduction block
-    constexpr int NG = BR / GR;                   // groups per (block, pass)
-    static_assert(BR % GR == 0, "group must divide block");
-    __shared__ float red[kMaxWarps][32];
+    constexpr int NST = BR / R;                   // stages per full block
+    static_assert(BR % R == 0, "stage rows must divide the block");
 
-    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
-    const uint32_t T = blockDim.x, K = a.K, P = a.passes;
-    const uint32_t tok0 = blockIdx.y * MT;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *ring = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + a.stages * a.slot_bytes);
+    uint64_t *empty = full + kMaxStages;
+    float(*red)[32] = reinterpret_cast<float(*)[32]>(empty + kMaxStages);
+    __shared__ uint32_t abort_flag;
+
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const uint32_t ncons = a.cons, ncw = ncons >> 5;
+    const uint32_t K = a.K, S = a.stages;
+    const uint32_t row_bytes = K * ESZ;
     const uint32_t vr0 = (uint32_t)(((uint64_t)blockIdx.x * a.total_rows) / gridDim.x);
     const uint32_t vr1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.total_rows) / gridDim.x);
+    const uint32_t tok0 = blockIdx.y * MT;
 
     griddep_launch();
-
-    auto seg_of = [&](uint32_t vr) {
-        int s = 0;
-#pragma unroll
-        for (int i = 1; i < 4; ++i)
-            if (i < a.nseg && vr >= a.seg[i].vbegin) s = i;
-        return s;
-    };
-    auto block_at = [&](uint32_t vr) {
-        Pos q;
-        q.ok = vr < vr1;
-        q.b0 = vr;
-        q.s = q.ok ? seg_of(vr) : 0;
-        const uint32_t send = a.seg[q.s].vbegin + a.seg[q.s].rows;
-        uint32_t e = vr + BR;
-        e = e < vr1 ? e : vr1;
-        q.b1 = e < send ? e : send;
-        q.p = 0;
-        q.g = 0;
-        return q;
-    };
-    auto advance = [&](Pos q) {
-        if (q.g + 1 < (uint32_t)NG && q.b0 + (q.g + 1) * GR < q.b1) { q.g++; return q; }
-        if (q.p + 1 < P) { q.p++; q.g = 0; return q; }
-        return block_at(q.b1);
-    };
-    auto kpos = [&](uint32_t p) { return p * T * EPV + t * EPV; };
-
-    uint4 wb[2][GR];
-    float sb[2][GR];
-    // B: buffer index as a compile-time constant, so wb/sb stay in registers
-    auto load = [&](auto B, const Pos &q) {
-        constexpr int b = decltype(B)::value;
-        const Seg &sg = a.seg[q.s];
-        const uint32_t k = kpos(q.p);
-        const bool kv = k < K;
-        const uint32_t kb = k >> 7;
-#pragma unroll
-        for (int i = 0; i < GR; ++i) {
-            const uint32_t vr = q.b0 + q.g * GR + i;
-            const bool v = kv && vr < q.b1;
-            const uint32_t r = vr - sg.vbegin;
-            wb[b][i] = v ? ld_stream(sg.W + ((size_t)r * K + k) * ESZ) : make_uint4(0, 0, 0, 0);
-            if constexpr (KIND == 0) sb[b][i] = v ? __ldg(sg.S + (size_t)(r >> 7) * a.kblocks + kb) : 0.f;
+    if (t == 0) {
+        for (uint32_t i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], ncw);
         }
-    };
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
 
-    float xr[MT][EPV];
-    auto load_x = [&](uint32_t p) {
-        const uint32_t k = kpos(p);
+    if (t >= ncons) {
+        // ---------------- producer warp: stream the rows into the ring --------
+        if (lane != 0) return;
+        uint32_t issued = 0;
+        bool ok = true;
+        for (Walk w = walk_block<BR>(a, vr0, vr1); w.ok && ok;) {
+            const uint32_t slot = issued % S;
+            if (issued >= S) {
+                ok = mbar_wait(&empty[slot], ((issued / S) - 1) & 1);
+                if (!ok || abort_flag) { abort_flag = 1; break; }
+            }
+            const uint32_t nrows = (w.b1 - w.r0) < (uint32_t)R ? (w.b1 - w.r0) : (uint32_t)R;
+            const Seg &sg = a.seg[w.s];
+            const uint32_t bytes = nrows * row_bytes;
+            mbar_expect_tx(&full[slot], bytes);
+            bulk_g2s(ring + (size_t)slot * a.slot_bytes, sg.W + (size_t)(w.r0 - sg.vbegin) * row_bytes, bytes,
+                     &full[slot]);
+            ++issued;
+            w.r0 += R;
+            if (w.r0 >= w.b1) w = walk_block<BR>(a, w.b1, vr1);
+        }
+        // wind down: every issued copy must have landed before the CTA exits
+        for (uint32_t i = (issued > S ? issued - S : 0); i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
+        return;
+    }
+
+    // ---------------- consumers --------------------------------------------
+    griddep_wait();  // activations of the previous kernel are visible from here on
+    float xr[P][MT][EPV];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+        const uint32_t k = (p * ncons + t) * EPV;
 #pragma unroll
         for (int tt = 0; tt < MT; ++tt) {
             const bool v = k < K && tok0 + tt < a.m;
@@ -273,72 +294,80 @@ __global__ void __launch_bounds__(kMaxThreads, 1) gemv_rs_kernel(const __grid_co
 #pragma unroll
             for (int q = 0; q < (int)EPV / 4; ++q) {
                 const float4 f = v ? __ldg(xp + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-                xr[tt][4 * q] = f.x; xr[tt][4 * q + 1] = f.y; xr[tt][4 * q + 2] = f.z; xr[tt][4 * q + 3] = f.w;
+                xr[p][tt][4 * q] = f.x;
+                xr[p][tt][4 * q + 1] = f.y;
+                xr[p][tt][4 * q + 2] = f.z;
+                xr[p][tt][4 * q + 3] = f.w;
             }
         }
-    };
+    }
 
-    float part[32];
+    uint32_t consumed = 0;
+    bool ok = true;
+    for (Walk w = walk_block<BR>(a, vr0, vr1); w.ok && ok; w = walk_block<BR>(a, w.b1, vr1)) {
+        const Seg &sg = a.seg[w.s];
+        float part[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) part[i] = 0.f;
-
-    // one group: prefetch the next group into the other buffer, multiply the
-    // current one, close the block when it ends.  Returns the next position.
-    auto step = [&](auto B, const Pos &cur) {
-        constexpr int b = decltype(B)::value;
-        const Pos nx = advance(cur);
-        if (nx.ok) load(std::integral_constant<int, b ^ 1>{}, nx);
-        const bool chk = KIND == 0 && a.seg[cur.s].has_nan;
+        for (int i = 0; i < 32; ++i) part[i] = 0.f;
 #pragma unroll
-        for (int g = 0; g < NG; ++g) {
-            if (cur.g == (uint32_t)g) {
+        for (int st = 0; st < NST; ++st) {
+            if (ok && w.b0 + st * R < w.b1) {
+                const uint32_t slot = consumed % S;
+                ok = mbar_wait(&full[slot], (consumed / S) & 1);
+                if (ok) {
+                    const uint8_t *stage = ring + (size_t)slot * a.slot_bytes;
 #pragma unroll
-                for (int i = 0; i < GR; ++i) {
+                    for (int r = 0; r < R; ++r) {
+                        const uint32_t vr = w.b0 + st * R + r;
+                        if (vr < w.b1) {
+                            const uint32_t row = vr - sg.vbegin;
 #pragma unroll
-                    for (int tt = 0; tt < MT; ++tt) {
-                        float &pr = part[(g * GR + i) * MT + tt];
-                        if constexpr (KIND == 0) pr = fmaf(sb[b][i], dot_fp8<CONV>(wb[b][i], xr[tt], chk), pr);
-                        else pr += dot_bf16(wb[b][i], xr[tt]);
+                            for (int p = 0; p < P; ++p) {
+                                const uint32_t k = (p * ncons + t) * EPV;
+                                if (k < K) {
+                                    const uint4 v = *reinterpret_cast<const uint4 *>(stage + r * row_bytes + k * ESZ);
+                                    if constexpr (KIND == 0) {
+                                        const float sc = __ldg(sg.S + (size_t)(row >> 7) * a.kblocks + (k >> 7));
+#pragma unroll
+                                        for (int tt = 0; tt < MT; ++tt) {
+                                            float &pr = part[(st * R + r) * MT + tt];
+                                            pr = fmaf(sc, dot_fp8(v, xr[p][tt]), pr);
+                                        }
+                                    } else {
+#pragma unroll
+                                        for (int tt = 0; tt < MT; ++tt) part[(st * R + r) * MT + tt] += dot_bf16(v, xr[p][tt]);
+                                    }
+                                }
+                            }
+                        }
                     }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[slot]);
+                    ++consumed;
+                } else {
+                    abort_flag = 1;
                 }
             }
         }
-        if (!nx.ok || nx.b0 != cur.b0) {  // block complete: reduce and store
-            const float v = transpose_reduce(part, lane);
-            red[warp][lane] = v;
-            __syncthreads();
-            if (warp == 0) {
-                float acc = red[0][lane];
-                for (uint32_t w = 1; w < nw; ++w) acc += red[w][lane];
-                const uint32_t vr = cur.b0 + lane / MT, tt = lane % MT;
-                const Seg &sg = a.seg[cur.s];
-                if (vr < cur.b1 && tok0 + tt < a.m) sg.Y[(size_t)(tok0 + tt) * sg.ldy + (vr - sg.vbegin)] = acc;
-            }
-            __syncthreads();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) part[i] = 0.f;
+        if (!ok) break;
+        const float v = transpose_reduce(part, lane);
+        red[warp][lane] = v;
+        asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
+        if (warp == 0) {
+            float acc = red[0][lane];
+            for (uint32_t q = 1; q < ncw; ++q) acc += red[q][lane];
+            const uint32_t vr = w.b0 + lane / MT, tt = lane % MT;
+            if (vr < w.b1 && tok0 + tt < a.m) sg.Y[(size_t)(tok0 + tt) * sg.ldy + (vr - sg.vbegin)] = acc;
         }
-        if (nx.ok && P > 1 && nx.p != cur.p) load_x(nx.p);
-        return nx;
-    };
-
-    Pos cur = block_at(vr0);
-    if (cur.ok) load(std::integral_constant<int, 0>{}, cur);
-    griddep_wait();  // activations of the previous kernel are visible from here on
-    if (!cur.ok) return;
-    load_x(0);
-    while (true) {
-        cur = step(std::integral_constant<int, 0>{}, cur);
-        if (!cur.ok) break;
-        cur = step(std::integral_constant<int, 1>{}, cur);
-        if (!cur.ok) break;
+        asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
     }
 }
 
 // Any shape, any alignment: one warp per (row, token), lanes over k, one
 // value per lane per step.  Used only when cols is not a multiple of the
-// 16-byte vector or an activation row is not 16-byte aligned (the odd
-// shapes of the reference's known-answer tests, e.g. 3x5 and 129x129).
+// 16-byte vector, an activation row is not 16-byte aligned, or K needs more
+// register passes than the streaming kernel keeps (the odd shapes of the
+// reference's known-answer tests, e.g. 3x5 and 129x129).
 template <int KIND>
 __global__ void __launch_bounds__(256) gemv_any_kernel(const __grid_constant__ Args a)
 {
@@ -384,6 +413,8 @@ __global__ void swiglu_kernel(const float *g, const float *u, float *o, size_t n
     }
 }
 
+__device__ __forceinline__ bool nan_code(uint32_t w) { return __vcmpeq4(w | 0x80808080u, 0xFFFFFFFFu) != 0u; }
+
 // scan an FP8 weight for the NaN codes 0x7F / 0xFF
 __global__ void nan_scan_kernel(const uint4 *w, size_t n16, const uint8_t *tail, uint32_t ntail, uint32_t *flag)
 {
@@ -398,12 +429,12 @@ __global__ void nan_scan_kernel(const uint4 *w, size_t n16, const uint8_t *tail,
 }
 
 template <typename Kern>
-int launch_pdl(Kern k, dim3 grid, dim3 block, cudaStream_t st, const Args &a)
+int launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, const Args &a)
 {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -415,32 +446,47 @@ int launch_pdl(Kern k, dim3 grid, dim3 block, cudaStream_t st, const Args &a)
     return Q35CU_OK;
 }
 
-int conv_variant()
+template <int KIND, int MT, int P, int R>
+int launch_tma(const Args &a, dim3 grid, size_t smem, cudaStream_t st)
 {
-    static int v = -1;
-    if (v < 0) {
-        const char *e = getenv("Q35CU_GEMV_CONV");
-        v = (e && e[0] == '0') ? 0 : 1;
+    auto k = gemv_tma_kernel<KIND, MT, P, R>;
+    static bool configured[64] = {};  // per instantiation and device
+    int dev = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
+    if (!configured[dev]) {
+        Q35CU_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        configured[dev] = true;
     }
-    return v;
+    return launch_pdl(k, grid, dim3(a.cons + 32), smem, st, a);
 }
 
-template <int KIND, int CONV>
-int launch_rs(const Args &a, uint32_t threads, dim3 grid, int mt, cudaStream_t st)
+// (MT, P) with MT * P <= 4 registers of activation per thread-slice; R rows
+// per stage from P (about 20 KB per stage)
+template <int KIND>
+int dispatch_tma(const Args &a, dim3 grid, size_t smem, int mt, int P, cudaStream_t st)
 {
-    if (mt == 1) return launch_pdl(gemv_rs_kernel<KIND, CONV, 1, 8>, grid, dim3(threads), st, a);
-    if (mt == 2) return launch_pdl(gemv_rs_kernel<KIND, CONV, 2, 8>, grid, dim3(threads), st, a);
-    return launch_pdl(gemv_rs_kernel<KIND, CONV, 4, 4>, grid, dim3(threads), st, a);
+    if (P == 1) {
+        if (mt == 1) return launch_tma<KIND, 1, 1, 4>(a, grid, smem, st);
+        if (mt == 2) return launch_tma<KIND, 2, 1, 4>(a, grid, smem, st);
+        return launch_tma<KIND, 4, 1, 4>(a, grid, smem, st);
+    }
+    if (P == 2) {
+        if (mt == 1) return launch_tma<KIND, 1, 2, 2>(a, grid, smem, st);
+        return launch_tma<KIND, 2, 2, 2>(a, grid, smem, st);
+    }
+    if (P == 3) return launch_tma<KIND, 1, 3, 1>(a, grid, smem, st);
+    return launch_tma<KIND, 1, 4, 1>(a, grid, smem, st);
 }
 
 }  // namespace
 
-// threads and passes of the row-stream kernel: a function of K only
+// consumer threads and passes of the streaming kernel: a function of K only
 void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes)
 {
     const uint32_t epv = kind == 0 ? 16 : 8;
     const uint32_t nvec = (K + epv - 1) / epv;
-    const uint32_t P = (nvec + kMaxThreads - 1) / kMaxThreads;
+    const uint32_t P = (nvec + kMaxCons - 1) / kMaxCons;
     uint32_t T = (nvec + P - 1) / P;
     T = (T + 31) / 32 * 32;
     *threads = T;
@@ -459,6 +505,7 @@ int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint
     a.kblocks = (K + 127) / 128;
     a.nseg = nseg;
     const uint32_t epv = kind == 0 ? 16 : 8;
+    const uint32_t esz = kind == 0 ? 1 : 2;
     bool vec_ok = (K % epv == 0) && (ldx % 4 == 0) && ((uintptr_t)X % 16 == 0);
     uint32_t vb = 0;
     for (int s = 0; s < nseg; ++s) {
@@ -469,24 +516,33 @@ int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint
     }
     a.total_rows = vb;
     if (vb == 0) return Q35CU_OK;
+    uint32_t T = 0, P = 0;
+    gemv_geometry(kind, K, &T, &P);
+    if (P > 4) vec_ok = false;
     if (vec_ok) {
-        uint32_t T, P;
-        gemv_geometry(kind, K, &T, &P);
-        a.passes = P;
-        const int mt = m == 1 ? 1 : (m == 2 ? 2 : 4);
+        a.cons = T;
+        const int R = P == 1 ? 4 : (P == 2 ? 2 : 1);
+        a.slot_bytes = (uint32_t)R * K * esz;
+        uint32_t stages = kRingBudget / a.slot_bytes;
+        stages = stages < 2 ? 2 : (stages > kMaxStages ? kMaxStages : stages);
+        a.stages = stages;
+        const size_t smem = (size_t)stages * a.slot_bytes + 2 * kMaxStages * 8 + kMaxWarps * 32 * 4;
+        const int mt_max = (int)(4 / P);
+        int mt = m == 1 ? 1 : (m == 2 ? 2 : 4);
+        if (mt > mt_max) mt = mt_max;
         const uint32_t sms = (uint32_t)device_sms();
         const uint32_t gx = vb < sms ? vb : sms;
         const uint32_t gy = (m + mt - 1) / mt;
         if (gy > 65535) return set_error(Q35CU_ERR_ARG, "gemv: too many tokens (%u)", m);
         const dim3 grid(gx, gy);
-        if (kind == 1) return launch_rs<1, 1>(a, T, grid, mt, st);
-        return conv_variant() == 0 ? launch_rs<0, 0>(a, T, grid, mt, st) : launch_rs<0, 1>(a, T, grid, mt, st);
+        return kind == 0 ? dispatch_tma<0>(a, grid, smem, mt, (int)P, st)
+                         : dispatch_tma<1>(a, grid, smem, mt, (int)P, st);
     }
     const uint64_t items = (uint64_t)vb * m;
     const uint64_t blocks = (items + 7) / 8;
     if (blocks > 0x7FFFFFFFull) return set_error(Q35CU_ERR_ARG, "gemv: shape too large for the generic kernel");
-    if (kind == 0) return launch_pdl(gemv_any_kernel<0>, dim3((unsigned)blocks), dim3(256), st, a);
-    return launch_pdl(gemv_any_kernel<1>, dim3((unsigned)blocks), dim3(256), st, a);
+    if (kind == 0) return launch_pdl(gemv_any_kernel<0>, dim3((unsigned)blocks), dim3(256), 0, st, a);
+    return launch_pdl(gemv_any_kernel<1>, dim3((unsigned)blocks), dim3(256), 0, st, a);
 }
 
 int launch_swiglu(const float *g, const float *u, float *o, size_t n, cudaStream_t st)
@@ -518,6 +574,16 @@ int scan_nan_codes(const uint8_t *W, size_t bytes, uint32_t *d_flag, cudaStream_
     Q35CU_CUDA(cudaMemcpyAsync(&h, d_flag, 4, cudaMemcpyDeviceToHost, st));
     Q35CU_CUDA(cudaStreamSynchronize(st));
     *has_nan = h != 0;
+    return Q35CU_OK;
+}
+
+int device_status(uint32_t *status, bool clear)
+{
+    Q35CU_CUDA(cudaMemcpyFromSymbol(status, g_device_status, 4));
+    if (clear) {
+        const uint32_t z = 0;
+        Q35CU_CUDA(cudaMemcpyToSymbol(g_device_status, &z, 4));
+    }
     return Q35CU_OK;
 }
 

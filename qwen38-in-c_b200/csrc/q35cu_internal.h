@@ -54,6 +54,7 @@ int launch_gemv(int kind, const GemvSeg *segs, int nseg, const float *X,
                 uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st);
 int launch_swiglu(const float *g, const float *u, float *o, size_t n, cudaStream_t st);
 void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes);
+int device_status(uint32_t *status, bool clear);
 int scan_nan_codes(const uint8_t *W, size_t bytes, uint32_t *d_flag, cudaStream_t st, bool *has_nan);
 
 int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y,

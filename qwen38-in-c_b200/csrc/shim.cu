@@ -674,6 +674,14 @@ Q35_API const char *q35cu_build_info(void)
 
 Q35_API uint64_t q35cu_launch_count(void) { return g_launches.load(); }
 
+Q35_API int q35cu_device_status(uint32_t *status, int clear)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!status) return set_error(Q35CU_ERR_ARG, "status is NULL");
+    if (!dev_state()) return t_err;
+    return device_status(status, clear != 0);
+}
+
 // ------------------------------------------------------------------------
 // q35_mm.h: the reference-facing entry points
 // ------------------------------------------------------------------------
@@ -711,6 +719,16 @@ Q35_API const char *q35_mm_impl_fp8(void) { return "sm_100a"; }
 
 namespace {
 
+// a bounded device-side wait that gave up leaves a code in the status word
+int check_device_status()
+{
+    uint32_t st = 0;
+    int rc = device_status(&st, true);
+    if (rc) return rc;
+    if (st) return set_error((int)st, "a device-side wait gave up (status %u)", st);
+    return Q35CU_OK;
+}
+
 // stage X in, run `fn` (which launches on d->stream into the device output
 // region), stage Y out.  in_bytes / out_bytes are exact byte counts.
 template <class F>
@@ -729,6 +747,8 @@ int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
     if (rc) return rc;
     Q35CU_CUDA(cudaMemcpyAsync(h + in_al, dv + in_al, out_bytes, cudaMemcpyDeviceToHost, d->stream));
     Q35CU_CUDA(cudaStreamSynchronize(d->stream));
+    rc = check_device_status();
+    if (rc) return rc;
     memcpy(Y, h + in_al, out_bytes);
     return Q35CU_OK;
 }
@@ -832,6 +852,7 @@ Q35_API void q35_mm_fp8_multi4(const uint8_t *W[4], const uint16_t *sc[4], uint3
                     if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
                     if (e != cudaSuccess) rc = cuda_error(e, "copy-out");
                 }
+                if (!rc) rc = check_device_status();
                 if (!rc) {
                     off = 0;
                     for (int s = 0; s < 4; ++s) {

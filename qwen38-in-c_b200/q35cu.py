@@ -89,6 +89,7 @@ _SIGS = [
     ("q35cu_allgather_f32", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_build_info", C.c_char_p, []),
     ("q35cu_launch_count", C.c_uint64, []),
+    ("q35cu_device_status", C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
 ]
 
 _lib = None

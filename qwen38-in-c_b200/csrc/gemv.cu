@@ -201,8 +201,8 @@ struct Walk {
     bool ok;
 };
 
-template <int BR>
-__device__ __forceinline__ Walk walk_block(const Args &a, uint32_t vr, uint32_t vr1)
+template <int BR, class A>
+__device__ __forceinline__ Walk walk_block(const A &a, uint32_t vr, uint32_t vr1)
 {
     Walk w;
     w.ok = vr < vr1;
@@ -363,6 +363,238 @@ __global__ void __launch_bounds__(kMaxCons + 32, 1) gemv_tma_kernel(const __grid
     }
 }
 
+// ---- FP8 decode GEMV on per-warp tensor-core MMAs ----------------------------
+//
+// The CUDA-core form above spends ~5 issued instructions per weight byte
+// (decode, widen, pack, multiply), which caps it far below HBM speed.  Here
+// the multiply-accumulate runs on mma.sync.m16n8k16 (f16 x f16 -> f32):
+//   A = 16 weight rows x 16 k, decoded e4m3 -> f16 by the hardware unpack
+//       (exact, one instruction per two bytes, NaN codes stay NaN);
+//   B = the activation, split exactly per 128-column block into
+//       x * 2^e = hi + lo with hi, lo in f16 (~23 significant bits, the
+//       power of two e chosen per token and block so that max |x*2^e| < 2^15),
+//       hi and lo as separate columns, up to 4 tokens per n8 MMA;
+//   C = f32.  Each 128-column block's partial of each row is scaled once:
+//       acc += (s[r/128, kb] * 2^-e) * C.
+// The k order inside each MMA is permuted consistently for A and B (lane
+// (g, t) holds bytes 4t..4t+3 of a 16-byte step), so every operand comes
+// from one 32-bit (A) or 64-bit (B) shared-memory load.  About 0.03 issued
+// instructions per weight byte remain.
+//
+// Layout: a producer warp streams stages of [16 rows x 1024 k] bytes into a
+// shared-memory ring (16 row copies per stage, rows padded by 16 bytes so
+// the A loads of a warp hit 32 distinct banks); warp w of 8 consumers owns
+// the 128-column block w of every 1024-column chunk.  After the last chunk
+// of a 16-row block the 8 warps' partials are added in warp order through
+// shared memory.  Results depend only on (row, token, K): batch, multi and
+// single calls agree bit for bit and repeat exactly.
+constexpr int kMmaWarps = 8;
+constexpr uint32_t kChunk = 1024;
+constexpr uint32_t kRowPitch = kChunk + 16;
+constexpr uint32_t kStageBytes = 16 * kRowPitch;
+
+// shared-memory layout of gemv_mma_kernel (byte offsets, 16-byte aligned)
+struct MmaSmem {
+    uint32_t xs, xmul, bar, red, total;
+};
+__host__ __device__ __forceinline__ MmaSmem mma_smem_layout(uint32_t stages, uint32_t mt, uint32_t xcol_bytes,
+                                                           uint32_t kblocks)
+{
+    MmaSmem L;
+    L.xs = stages * kStageBytes;
+    L.xmul = L.xs + 2 * mt * xcol_bytes;
+    L.bar = (L.xmul + mt * kblocks * 4 + 15) & ~15u;
+    L.red = L.bar + 2 * kMaxStages * 8;
+    L.total = L.red + kMmaWarps * 32 * 16;
+    return L;
+}
+
+struct MArgs {
+    Seg seg[4];
+    const float *X;
+    uint32_t K, ldx, m, kblocks, total_rows, nchunks;
+    uint32_t stages;      // ring slots
+    uint32_t xcol_bytes;  // bytes of one f16 activation column in shared memory (2K + 32)
+    int nseg;
+};
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint16_t f16_bits(float v)
+{
+    uint16_t h;
+    asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(v));
+    return h;
+}
+
+template <int MT>
+__global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ MArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *ring = smem;
+    const MmaSmem L = mma_smem_layout(a.stages, MT, a.xcol_bytes, a.kblocks);
+    uint8_t *xs = smem + L.xs;                                 // [2*MT][xcol_bytes] f16 hi/lo columns
+    float *xmul = reinterpret_cast<float *>(smem + L.xmul);    // [MT][kblocks] 2^-e
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
+    uint64_t *empty = full + kMaxStages;
+    float4 *red = reinterpret_cast<float4 *>(smem + L.red);    // [8 warps][32 lanes]
+    __shared__ uint32_t abort_flag;
+
+    constexpr uint32_t ncons = kMmaWarps * 32;
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const uint32_t K = a.K, S = a.stages;
+    const uint32_t vr0 = (uint32_t)(((uint64_t)blockIdx.x * a.total_rows) / gridDim.x);
+    const uint32_t vr1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.total_rows) / gridDim.x);
+    const uint32_t tok0 = blockIdx.y * MT;
+
+    griddep_launch();
+    if (t == 0) {
+        for (uint32_t i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kMmaWarps);
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (t >= ncons) {
+        // ---------------- producer warp --------------------------------------
+        if (lane != 0) return;
+        uint32_t issued = 0;
+        bool ok = true;
+        for (Walk w = walk_block<16>(a, vr0, vr1); w.ok && ok;) {
+            const Seg &sg = a.seg[w.s];
+            const uint32_t nrows = w.b1 - w.b0;
+            for (uint32_t c = 0; c < a.nchunks && ok; ++c) {
+                const uint32_t slot = issued % S;
+                if (issued >= S) {
+                    ok = mbar_wait(&empty[slot], ((issued / S) - 1) & 1);
+                    if (!ok || abort_flag) { abort_flag = 1; ok = false; break; }
+                }
+                const uint32_t kc = c * kChunk;
+                const uint32_t bytes = (K - kc) < kChunk ? (K - kc) : kChunk;
+                uint8_t *dst = ring + (size_t)slot * kStageBytes;
+                const uint8_t *src = sg.W + (size_t)(w.b0 - sg.vbegin) * K + kc;
+                mbar_expect_tx(&full[slot], nrows * bytes);
+                for (uint32_t r = 0; r < nrows; ++r) bulk_g2s(dst + r * kRowPitch, src + (size_t)r * K, bytes, &full[slot]);
+                ++issued;
+            }
+            w = walk_block<16>(a, w.b1, vr1);
+        }
+        for (uint32_t i = (issued > S ? issued - S : 0); i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
+        return;
+    }
+
+    // ---------------- consumers: the activation in f16 hi/lo -----------------
+    griddep_wait();
+    for (uint32_t idx = warp; idx < MT * a.kblocks; idx += kMmaWarps) {
+        const uint32_t tt = idx / a.kblocks, kb = idx % a.kblocks;
+        const uint32_t k = kb * 128 + lane * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tok0 + tt < a.m && k < K) v = __ldg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + k));
+        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        // 2^e with max|x * 2^e| < 2^15; e in [-126, 127] keeps 2^e and 2^-e representable
+        int e = 0;
+        if (mx > 0.f && mx == mx && mx != __int_as_float(0x7f800000)) {
+            const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;
+            e = 14 - E;
+            e = e > 126 ? 126 : (e < -126 ? -126 : e);
+        }
+        const float up = __uint_as_float((uint32_t)(e + 127) << 23), down = __uint_as_float((uint32_t)(127 - e) << 23);
+        const float xv[4] = {v.x * up, v.y * up, v.z * up, v.w * up};
+        uint16_t hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            hi[j] = f16_bits(xv[j]);
+            lo[j] = f16_bits(xv[j] - __half2float(__ushort_as_half(hi[j])));
+        }
+        uint2 ph, pl;
+        ph.x = hi[0] | ((uint32_t)hi[1] << 16);
+        ph.y = hi[2] | ((uint32_t)hi[3] << 16);
+        pl.x = lo[0] | ((uint32_t)lo[1] << 16);
+        pl.y = lo[2] | ((uint32_t)lo[3] << 16);
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) = ph;
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) = pl;
+        if (lane == 0) xmul[tt * a.kblocks + kb] = down;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
+
+    // ---------------- consumers: the row blocks --------------------------------
+    const uint32_t g = lane >> 2, tq = lane & 3;
+    const bool bcol = g < 2 * MT;  // this lane feeds a live B column
+    const uint8_t *xcol = xs + (size_t)(bcol ? g : 0) * a.xcol_bytes + tq * 8;
+    uint32_t consumed = 0;
+    bool ok = true;
+    for (Walk w = walk_block<16>(a, vr0, vr1); w.ok && ok;
+         w = walk_block<16>(a, w.b1, vr1)) {
+        const Seg &sg = a.seg[w.s];
+        const uint32_t rlast = sg.rows - 1;
+        uint32_t r_g = w.b0 + g - sg.vbegin, r_g8 = r_g + 8;
+        r_g = r_g < rlast ? r_g : rlast;
+        r_g8 = r_g8 < rlast ? r_g8 : rlast;
+        const float *s_g = sg.S + (size_t)(r_g >> 7) * a.kblocks;
+        const float *s_g8 = sg.S + (size_t)(r_g8 >> 7) * a.kblocks;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (uint32_t c = 0; c < a.nchunks; ++c) {
+            const uint32_t slot = consumed % S;
+            ok = mbar_wait(&full[slot], (consumed / S) & 1);
+            if (!ok) { abort_flag = 1; break; }
+            const uint32_t kb = c * 8 + warp;
+            if (kb < a.kblocks) {
+                const uint8_t *st = ring + (size_t)slot * kStageBytes + warp * 128 + tq * 4;
+                const uint8_t *xb = xcol + (size_t)kb * 256;
+                float cz[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int s = 0; s < 8; ++s) {
+                    const uint32_t A0 = *reinterpret_cast<const uint32_t *>(st + g * kRowPitch + s * 16);
+                    const uint32_t A1 = *reinterpret_cast<const uint32_t *>(st + (g + 8) * kRowPitch + s * 16);
+                    uint32_t a0, a2, a1, a3;
+                    hw_f16x2(A0, a0, a2);
+                    hw_f16x2(A1, a1, a3);
+                    uint2 b = make_uint2(0u, 0u);
+                    if (bcol) b = *reinterpret_cast<const uint2 *>(xb + s * 32);
+                    mma16816(cz, a0, a1, a2, a3, b.x, b.y);
+                }
+                const float xm = tq < MT ? xmul[tq * a.kblocks + kb] : 0.f;
+                const float f0 = __ldg(s_g + kb) * xm, f1 = __ldg(s_g8 + kb) * xm;
+                acc[0] = fmaf(f0, cz[0], acc[0]);
+                acc[1] = fmaf(f0, cz[1], acc[1]);
+                acc[2] = fmaf(f1, cz[2], acc[2]);
+                acc[3] = fmaf(f1, cz[3], acc[3]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            ++consumed;
+        }
+        if (!ok) break;
+        red[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
+        if (t < 16 * MT) {
+            const uint32_t i = t / MT, tt = t % MT;  // row in block, token
+            const uint32_t src_lane = (i & 7) * 4 + tt;
+            float y = 0.f;
+#pragma unroll
+            for (int q = 0; q < kMmaWarps; ++q) {
+                const float4 r4 = red[q * 32 + src_lane];
+                y += i < 8 ? r4.x + r4.y : r4.z + r4.w;
+            }
+            const uint32_t vr = w.b0 + i;
+            if (vr < w.b1 && tok0 + tt < a.m) sg.Y[(size_t)(tok0 + tt) * sg.ldy + (vr - sg.vbegin)] = y;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
+    }
+}
+
 // Any shape, any alignment: one warp per (row, token), lanes over k, one
 // value per lane per step.  Used only when cols is not a multiple of the
 // 16-byte vector, an activation row is not 16-byte aligned, or K needs more
@@ -461,6 +693,67 @@ int launch_tma(const Args &a, dim3 grid, size_t smem, cudaStream_t st)
     return launch_pdl(k, grid, dim3(a.cons + 32), smem, st, a);
 }
 
+template <int MT>
+int launch_mma(const MArgs &a, dim3 grid, size_t smem, cudaStream_t st)
+{
+    auto k = gemv_mma_kernel<MT>;
+    static bool configured[64] = {};
+    int dev = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
+    if (!configured[dev]) {
+        Q35CU_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        configured[dev] = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3((kMmaWarps + 1) * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q35CU_CUDA(cudaLaunchKernelEx(&cfg, k, a));
+    count_launch();
+    return Q35CU_OK;
+}
+
+// FP8 weights with cols % 128 == 0: the tensor-core decode GEMV
+int launch_gemv_mma(const Args &a0, cudaStream_t st)
+{
+    MArgs a{};
+    for (int s = 0; s < 4; ++s) a.seg[s] = a0.seg[s];
+    a.X = a0.X;
+    a.K = a0.K;
+    a.ldx = a0.ldx;
+    a.m = a0.m;
+    a.kblocks = a0.kblocks;
+    a.total_rows = a0.total_rows;
+    a.nseg = a0.nseg;
+    a.nchunks = (a0.K + kChunk - 1) / kChunk;
+    a.xcol_bytes = 2 * a0.K + 32;
+    const uint32_t budget = 220 * 1024;
+    int mt = a0.m >= 3 ? 4 : (int)a0.m;
+    while (mt > 1 && mma_smem_layout(2, mt, a.xcol_bytes, a.kblocks).total > budget) mt /= 2;
+    if (mma_smem_layout(2, mt, a.xcol_bytes, a.kblocks).total > budget)
+        return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: cols %u too large for the shared-memory activation", a0.K);
+    uint32_t stages = 6;
+    while (stages > 2 && mma_smem_layout(stages, mt, a.xcol_bytes, a.kblocks).total > budget) --stages;
+    a.stages = stages;
+    const size_t smem = mma_smem_layout(stages, mt, a.xcol_bytes, a.kblocks).total;
+    const uint32_t sms = (uint32_t)device_sms();
+    const uint32_t blocks16 = (a.total_rows + 15) / 16;
+    const uint32_t gx = blocks16 < sms ? blocks16 : sms;
+    const uint32_t gy = (a0.m + mt - 1) / mt;
+    if (gy > 65535) return set_error(Q35CU_ERR_ARG, "gemv: too many tokens (%u)", a0.m);
+    const dim3 grid(gx, gy);
+    if (mt == 1) return launch_mma<1>(a, grid, smem, st);
+    if (mt == 2) return launch_mma<2>(a, grid, smem, st);
+    return launch_mma<4>(a, grid, smem, st);
+}
+
 // (MT, P) with MT * P <= 4 registers of activation per thread-slice; R rows
 // per stage from P (about 20 KB per stage)
 template <int KIND>
@@ -516,6 +809,7 @@ int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint
     }
     a.total_rows = vb;
     if (vb == 0) return Q35CU_OK;
+    if (vec_ok && kind == 0 && K % 128 == 0 && getenv("Q35CU_GEMV_SIMT") == nullptr) return launch_gemv_mma(a, st);
     uint32_t T = 0, P = 0;
     gemv_geometry(kind, K, &T, &P);
     if (P > 4) vec_ok = false;

@@ -702,7 +702,7 @@ int launch_mma(const MArgs &a, dim3 grid, size_t smem, cudaStream_t st)
     Q35CU_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
     if (!configured[dev]) {
-        Q35CU_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        Q35CU_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
         configured[dev] = true;
     }
     cudaLaunchConfig_t cfg{};

@@ -90,6 +90,16 @@ __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.
 
 __device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// 16-byte streaming load of read-only data (no L1 allocation, 256-byte L2 prefetch)
+__device__ __forceinline__ uint4 ld_stream(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count)
 {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count));
@@ -365,58 +375,63 @@ __global__ void __launch_bounds__(kMaxCons + 32, 1) gemv_tma_kernel(const __grid
 
 // ---- FP8 decode GEMV on per-warp tensor-core MMAs ----------------------------
 //
-// The CUDA-core form above spends ~5 issued instructions per weight byte
-// (decode, widen, pack, multiply), which caps it far below HBM speed.  Here
-// the multiply-accumulate runs on mma.sync.m16n8k16 (f16 x f16 -> f32):
+// The CUDA-core form spends ~5 issued instructions per weight byte (decode,
+// widen, pack, multiply), which caps it far below HBM speed.  Here the
+// multiply-accumulate runs on mma.sync.m16n8k16 (f16 x f16 -> f32):
 //   A = 16 weight rows x 16 k, decoded e4m3 -> f16 by the hardware unpack
 //       (exact, one instruction per two bytes, NaN codes stay NaN);
 //   B = the activation, split exactly per 128-column block into
-//       x * 2^e = hi + lo with hi, lo in f16 (~23 significant bits, the
-//       power of two e chosen per token and block so that max |x*2^e| < 2^15),
+//       x * 2^e = hi + lo with hi, lo in f16 (~23 significant bits; the power
+//       of two e is chosen per token and block so that max |x*2^e| < 2^15),
 //       hi and lo as separate columns, up to 4 tokens per n8 MMA;
-//   C = f32.  Each 128-column block's partial of each row is scaled once:
+//   C = f32.  Each 128-column block's partial of a row is scaled once:
 //       acc += (s[r/128, kb] * 2^-e) * C.
-// The k order inside each MMA is permuted consistently for A and B (lane
-// (g, t) holds bytes 4t..4t+3 of a 16-byte step), so every operand comes
-// from one 32-bit (A) or 64-bit (B) shared-memory load.  About 0.03 issued
+// Weights go straight from HBM into A fragments: lane (g, t) loads 16 bytes
+// of rows g and g+8 at column 16t of a 64-column group, and byte quad j of
+// that vector is its A operand for k-step j of the group (the k order inside
+// the group is permuted; B is read with the same permutation from the f16
+// activation columns in shared memory).  Each warp-load touches 16 rows x 64
+// contiguous bytes, two full 32-byte sectors per row.  About 0.03 issued
 // instructions per weight byte remain.
 //
-// Layout: a producer warp streams stages of [16 rows x 1024 k] bytes into a
-// shared-memory ring (16 row copies per stage, rows padded by 16 bytes so
-// the A loads of a warp hit 32 distinct banks); warp w of 8 consumers owns
-// the 128-column block w of every 1024-column chunk.  After the last chunk
-// of a 16-row block the 8 warps' partials are added in warp order through
-// shared memory.  Results depend only on (row, token, K): batch, multi and
-// single calls agree bit for bit and repeat exactly.
-constexpr int kMmaWarps = 8;
-constexpr uint32_t kChunk = 1024;
-constexpr uint32_t kRowPitch = kChunk + 16;
-constexpr uint32_t kStageBytes = 16 * kRowPitch;
-
-// shared-memory layout of gemv_mma_kernel (byte offsets, 16-byte aligned)
-struct MmaSmem {
-    uint32_t xs, xmul, bar, red, total;
-};
-__host__ __device__ __forceinline__ MmaSmem mma_smem_layout(uint32_t stages, uint32_t mt, uint32_t xcol_bytes,
-                                                           uint32_t kblocks)
-{
-    MmaSmem L;
-    L.xs = stages * kStageBytes;
-    L.xmul = L.xs + 2 * mt * xcol_bytes;
-    L.bar = (L.xmul + mt * kblocks * 4 + 15) & ~15u;
-    L.red = L.bar + 2 * kMaxStages * 8;
-    L.total = L.red + kMmaWarps * 32 * 16;
-    return L;
-}
+// Work: CTA c owns the contiguous rows [c*R/G, (c+1)*R/G) of the launch
+// (R rows of all segments, G = grid <= SMs), cut into 16-row blocks (never
+// crossing a segment).  An item is (16-row block, 256 columns = 2 blocks of
+// 128); the 16 warps take items round-robin with the next item's loads in
+// flight while the current one multiplies, and write one partial per item.
+// After a round of row blocks, the partials of each output are added in
+// column order.  Results depend only on (row, token, K): batch, multi and
+// single calls agree bit for bit, and repeat exactly.
+constexpr int kM2Warps = 16;
+constexpr int kM2Threads = kM2Warps * 32;
+constexpr uint32_t kItemCols = 256;            // columns per work item
+constexpr uint32_t kMaxRowBlocks = 1024;       // row blocks per CTA (table in shared memory)
 
 struct MArgs {
     Seg seg[4];
     const float *X;
-    uint32_t K, ldx, m, kblocks, total_rows, nchunks;
-    uint32_t stages;      // ring slots
+    uint32_t K, ldx, m, kblocks, total_rows;
     uint32_t xcol_bytes;  // bytes of one f16 activation column in shared memory (2K + 32)
+    uint32_t ipr;         // items per row block = ceil(K / 256)
+    uint32_t rb_round;    // row blocks per round (partials buffer)
     int nseg;
 };
+
+// shared-memory layout (byte offsets, 16-byte aligned)
+struct MmaSmem {
+    uint32_t xs, xmul, rbt, part, total;
+};
+__host__ __device__ __forceinline__ MmaSmem mma_smem_layout(uint32_t mt, uint32_t xcol_bytes, uint32_t kblocks,
+                                                           uint32_t items_round)
+{
+    MmaSmem L;
+    L.xs = 0;
+    L.xmul = 2 * mt * xcol_bytes;
+    L.rbt = (L.xmul + mt * kblocks * 4 + 15) & ~15u;
+    L.part = L.rbt + kMaxRowBlocks * 8;
+    L.total = L.part + items_round * 32 * 16;
+    return L;
+}
 
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1)
@@ -434,78 +449,81 @@ __device__ __forceinline__ uint16_t f16_bits(float v)
     return h;
 }
 
+// one item's weights for this lane: rows g, g+8 x 4 groups of 64 columns
+struct ItemLoad {
+    uint4 v[8];  // [group][row half]
+};
+
 template <int MT>
-__global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ MArgs a)
+__global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_constant__ MArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t *ring = smem;
-    const MmaSmem L = mma_smem_layout(a.stages, MT, a.xcol_bytes, a.kblocks);
-    uint8_t *xs = smem + L.xs;                                 // [2*MT][xcol_bytes] f16 hi/lo columns
-    float *xmul = reinterpret_cast<float *>(smem + L.xmul);    // [MT][kblocks] 2^-e
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
-    uint64_t *empty = full + kMaxStages;
-    float4 *red = reinterpret_cast<float4 *>(smem + L.red);    // [8 warps][32 lanes]
-    __shared__ uint32_t abort_flag;
+    const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * a.ipr);
+    uint8_t *xs = smem + L.xs;                                   // [2*MT][xcol_bytes] f16 columns
+    float *xmul = reinterpret_cast<float *>(smem + L.xmul);      // [MT][kblocks] 2^-e
+    uint2 *rbt = reinterpret_cast<uint2 *>(smem + L.rbt);        // row blocks: (first virtual row, rows | seg << 8)
+    float4 *part = reinterpret_cast<float4 *>(smem + L.part);    // [items in round][32 lanes]
+    __shared__ uint32_t nrb_s;
 
-    constexpr uint32_t ncons = kMmaWarps * 32;
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const uint32_t K = a.K, S = a.stages;
+    const uint32_t g = lane >> 2, tq = lane & 3;
+    const uint32_t K = a.K, ipr = a.ipr;
     const uint32_t vr0 = (uint32_t)(((uint64_t)blockIdx.x * a.total_rows) / gridDim.x);
     const uint32_t vr1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.total_rows) / gridDim.x);
     const uint32_t tok0 = blockIdx.y * MT;
 
     griddep_launch();
-    if (t == 0) {
-        for (uint32_t i = 0; i < S; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kMmaWarps);
+    if (t == 0) {  // the CTA's 16-row blocks, cut at segment boundaries
+        uint32_t n = 0;
+        for (uint32_t vr = vr0; vr < vr1 && n < kMaxRowBlocks;) {
+            int s = 0;
+            for (int i = 1; i < a.nseg; ++i)
+                if (vr >= a.seg[i].vbegin) s = i;
+            uint32_t e = vr + 16;
+            const uint32_t send = a.seg[s].vbegin + a.seg[s].rows;
+            e = e < vr1 ? e : vr1;
+            e = e < send ? e : send;
+            rbt[n++] = make_uint2(vr, (e - vr) | ((uint32_t)s << 8));
+            vr = e;
         }
-        abort_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        nrb_s = n;
     }
     __syncthreads();
+    const uint32_t nrb = nrb_s;
 
-    if (t >= ncons) {
-        // ---------------- producer warp --------------------------------------
-        if (lane != 0) return;
-        uint32_t issued = 0;
-        bool ok = true;
-        for (Walk w = walk_block<16>(a, vr0, vr1); w.ok && ok;) {
-            const Seg &sg = a.seg[w.s];
-            const uint32_t nrows = w.b1 - w.b0;
-            for (uint32_t c = 0; c < a.nchunks && ok; ++c) {
-                const uint32_t slot = issued % S;
-                if (issued >= S) {
-                    ok = mbar_wait(&empty[slot], ((issued / S) - 1) & 1);
-                    if (!ok || abort_flag) { abort_flag = 1; ok = false; break; }
-                }
-                const uint32_t kc = c * kChunk;
-                const uint32_t bytes = (K - kc) < kChunk ? (K - kc) : kChunk;
-                uint8_t *dst = ring + (size_t)slot * kStageBytes;
-                const uint8_t *src = sg.W + (size_t)(w.b0 - sg.vbegin) * K + kc;
-                mbar_expect_tx(&full[slot], nrows * bytes);
-                for (uint32_t r = 0; r < nrows; ++r) bulk_g2s(dst + r * kRowPitch, src + (size_t)r * K, bytes, &full[slot]);
-                ++issued;
-            }
-            w = walk_block<16>(a, w.b1, vr1);
+    // item -> this lane's weight addresses
+    auto issue = [&](ItemLoad &ld, uint32_t item) {
+        const uint2 rb = rbt[item / ipr];
+        const uint32_t c0 = (item % ipr) * kItemCols;
+        const Seg &sg = a.seg[rb.y >> 8];
+        const uint32_t nrows = rb.y & 0xFF;
+        const uint32_t r = rb.x - sg.vbegin;
+        const uint8_t *w0 = sg.W + (size_t)(r + g) * K + c0 + tq * 16;
+        const uint8_t *w1 = w0 + (size_t)8 * K;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const bool kv = c0 + q * 64 < K;
+            ld.v[2 * q] = (kv && g < nrows) ? ld_stream(w0 + q * 64) : make_uint4(0, 0, 0, 0);
+            ld.v[2 * q + 1] = (kv && g + 8 < nrows) ? ld_stream(w1 + q * 64) : make_uint4(0, 0, 0, 0);
         }
-        for (uint32_t i = (issued > S ? issued - S : 0); i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
-        return;
-    }
+    };
 
-    // ---------------- consumers: the activation in f16 hi/lo -----------------
+    // prefetch this warp's first item (weights only) before waiting on the previous kernel
+    ItemLoad cur, nxt;
+    const uint32_t first_round_items = (nrb < a.rb_round ? nrb : a.rb_round) * ipr;
+    if (warp < first_round_items) issue(cur, warp);
+
     griddep_wait();
-    for (uint32_t idx = warp; idx < MT * a.kblocks; idx += kMmaWarps) {
+    for (uint32_t idx = warp; idx < MT * a.kblocks; idx += kM2Warps) {
         const uint32_t tt = idx / a.kblocks, kb = idx % a.kblocks;
         const uint32_t k = kb * 128 + lane * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (tok0 + tt < a.m && k < K) v = __ldg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + k));
+        if (tok0 + tt < a.m) v = __ldg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + k));
         float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-        // 2^e with max|x * 2^e| < 2^15; e in [-126, 127] keeps 2^e and 2^-e representable
-        int e = 0;
-        if (mx > 0.f && mx == mx && mx != __int_as_float(0x7f800000)) {
+        int e = 0;  // 2^e with max |x*2^e| < 2^15; |e| <= 126 keeps 2^e and 2^-e normal
+        if (mx > 0.f && mx <= 3.402823466e38f) {
             const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;
             e = 14 - E;
             e = e > 126 ? 126 : (e < -126 ? -126 : e);
@@ -518,80 +536,92 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 1) gemv_mma_kernel(const
             hi[j] = f16_bits(xv[j]);
             lo[j] = f16_bits(xv[j] - __half2float(__ushort_as_half(hi[j])));
         }
-        uint2 ph, pl;
-        ph.x = hi[0] | ((uint32_t)hi[1] << 16);
-        ph.y = hi[2] | ((uint32_t)hi[3] << 16);
-        pl.x = lo[0] | ((uint32_t)lo[1] << 16);
-        pl.y = lo[2] | ((uint32_t)lo[3] << 16);
-        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) = ph;
-        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) = pl;
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) =
+            make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) =
+            make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
         if (lane == 0) xmul[tt * a.kblocks + kb] = down;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
+    __syncthreads();
 
-    // ---------------- consumers: the row blocks --------------------------------
-    const uint32_t g = lane >> 2, tq = lane & 3;
     const bool bcol = g < 2 * MT;  // this lane feeds a live B column
-    const uint8_t *xcol = xs + (size_t)(bcol ? g : 0) * a.xcol_bytes + tq * 8;
-    uint32_t consumed = 0;
-    bool ok = true;
-    for (Walk w = walk_block<16>(a, vr0, vr1); w.ok && ok;
-         w = walk_block<16>(a, w.b1, vr1)) {
-        const Seg &sg = a.seg[w.s];
-        const uint32_t rlast = sg.rows - 1;
-        uint32_t r_g = w.b0 + g - sg.vbegin, r_g8 = r_g + 8;
-        r_g = r_g < rlast ? r_g : rlast;
-        r_g8 = r_g8 < rlast ? r_g8 : rlast;
-        const float *s_g = sg.S + (size_t)(r_g >> 7) * a.kblocks;
-        const float *s_g8 = sg.S + (size_t)(r_g8 >> 7) * a.kblocks;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (uint32_t c = 0; c < a.nchunks; ++c) {
-            const uint32_t slot = consumed % S;
-            ok = mbar_wait(&full[slot], (consumed / S) & 1);
-            if (!ok) { abort_flag = 1; break; }
-            const uint32_t kb = c * 8 + warp;
-            if (kb < a.kblocks) {
-                const uint8_t *st = ring + (size_t)slot * kStageBytes + warp * 128 + tq * 4;
-                const uint8_t *xb = xcol + (size_t)kb * 256;
-                float cz[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint8_t *xcol = xs + (size_t)(bcol ? g : 0) * a.xcol_bytes;
+    for (uint32_t rb0 = 0; rb0 < nrb; rb0 += a.rb_round) {
+        const uint32_t nrb_r = (nrb - rb0) < a.rb_round ? (nrb - rb0) : a.rb_round;
+        const uint32_t items = nrb_r * ipr;
+        for (uint32_t it = warp; it < items; it += kM2Warps) {
+            const uint32_t item = rb0 * ipr + it;
+            const uint32_t nit = it + kM2Warps;
+            // next item of this warp: later in this round, or its first item of the next round
+            const uint32_t nrb_next = rb0 + a.rb_round < nrb ? ((nrb - rb0 - a.rb_round) < a.rb_round
+                                                                   ? (nrb - rb0 - a.rb_round)
+                                                                   : a.rb_round)
+                                                              : 0;
+            if (nit < items) issue(nxt, rb0 * ipr + nit);
+            else if (warp < nrb_next * ipr) issue(nxt, (rb0 + a.rb_round) * ipr + warp);
+            // multiply the current item: 2 blocks of 128 columns = 2 x 2 groups x 4 k-steps
+            const uint2 rb = rbt[item / ipr];
+            const Seg &sg = a.seg[rb.y >> 8];
+            const uint32_t rlast = sg.rows - 1;
+            uint32_t r_g = rb.x - sg.vbegin + g, r_g8 = r_g + 8;
+            r_g = r_g < rlast ? r_g : rlast;
+            r_g8 = r_g8 < rlast ? r_g8 : rlast;
+            const uint32_t c0 = (item % ipr) * kItemCols;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const uint32_t A0 = *reinterpret_cast<const uint32_t *>(st + g * kRowPitch + s * 16);
-                    const uint32_t A1 = *reinterpret_cast<const uint32_t *>(st + (g + 8) * kRowPitch + s * 16);
-                    uint32_t a0, a2, a1, a3;
-                    hw_f16x2(A0, a0, a2);
-                    hw_f16x2(A1, a1, a3);
-                    uint2 b = make_uint2(0u, 0u);
-                    if (bcol) b = *reinterpret_cast<const uint2 *>(xb + s * 32);
-                    mma16816(cz, a0, a1, a2, a3, b.x, b.y);
+            for (int hb = 0; hb < 2; ++hb) {
+                const uint32_t kb = (c0 >> 7) + hb;
+                if (kb < a.kblocks) {
+                    float cz[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const uint4 A0 = cur.v[2 * (2 * hb + q)], A1 = cur.v[2 * (2 * hb + q) + 1];
+                        const uint32_t w0[4] = {A0.x, A0.y, A0.z, A0.w}, w1[4] = {A1.x, A1.y, A1.z, A1.w};
+                        // B: f16 of columns c0 + 128hb + 64q + 16tq + 4j .. +3 for step j
+                        const uint8_t *xb = xcol + (size_t)(c0 + hb * 128 + q * 64 + tq * 16) * 2;
+                        uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
+                        if (bcol) {
+                            b01 = *reinterpret_cast<const uint4 *>(xb);
+                            b23 = *reinterpret_cast<const uint4 *>(xb + 16);
+                        }
+                        const uint32_t bw[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint32_t a0, a2, a1, a3;
+                            hw_f16x2(w0[j], a0, a2);
+                            hw_f16x2(w1[j], a1, a3);
+                            mma16816(cz, a0, a1, a2, a3, bw[2 * j], bw[2 * j + 1]);
+                        }
+                    }
+                    const float xm = tq < MT ? xmul[tq * a.kblocks + kb] : 0.f;
+                    const float f0 = __ldg(sg.S + (size_t)(r_g >> 7) * a.kblocks + kb) * xm;
+                    const float f1 = __ldg(sg.S + (size_t)(r_g8 >> 7) * a.kblocks + kb) * xm;
+                    acc[0] = fmaf(f0, cz[0], acc[0]);
+                    acc[1] = fmaf(f0, cz[1], acc[1]);
+                    acc[2] = fmaf(f1, cz[2], acc[2]);
+                    acc[3] = fmaf(f1, cz[3], acc[3]);
                 }
-                const float xm = tq < MT ? xmul[tq * a.kblocks + kb] : 0.f;
-                const float f0 = __ldg(s_g + kb) * xm, f1 = __ldg(s_g8 + kb) * xm;
-                acc[0] = fmaf(f0, cz[0], acc[0]);
-                acc[1] = fmaf(f0, cz[1], acc[1]);
-                acc[2] = fmaf(f1, cz[2], acc[2]);
-                acc[3] = fmaf(f1, cz[3], acc[3]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            ++consumed;
+            part[(size_t)it * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            cur = nxt;
         }
-        if (!ok) break;
-        red[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
-        if (t < 16 * MT) {
-            const uint32_t i = t / MT, tt = t % MT;  // row in block, token
-            const uint32_t src_lane = (i & 7) * 4 + tt;
+        __syncthreads();
+        // combine: output (row i of block, token tt) = sum over items of the block, in column order
+        for (uint32_t o = t; o < nrb_r * 16 * MT; o += kM2Threads) {
+            const uint32_t rbl = o / (16 * MT), i = (o / MT) % 16, tt = o % MT;
+            const uint2 rb = rbt[rb0 + rbl];
+            const uint32_t nrows = rb.y & 0xFF;
+            if (i >= nrows || tok0 + tt >= a.m) continue;
+            const uint32_t src = (i & 7) * 4 + tt;
             float y = 0.f;
-#pragma unroll
-            for (int q = 0; q < kMmaWarps; ++q) {
-                const float4 r4 = red[q * 32 + src_lane];
-                y += i < 8 ? r4.x + r4.y : r4.z + r4.w;
+            for (uint32_t s = 0; s < ipr; ++s) {
+                const float4 p4 = part[(size_t)(rbl * ipr + s) * 32 + src];
+                y += i < 8 ? p4.x + p4.y : p4.z + p4.w;
             }
-            const uint32_t vr = w.b0 + i;
-            if (vr < w.b1 && tok0 + tt < a.m) sg.Y[(size_t)(tok0 + tt) * sg.ldy + (vr - sg.vbegin)] = y;
+            const Seg &sg = a.seg[rb.y >> 8];
+            sg.Y[(size_t)(tok0 + tt) * sg.ldy + (rb.x - sg.vbegin + i)] = y;
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(ncons) : "memory");
+        __syncthreads();
     }
 }
 
@@ -707,7 +737,7 @@ int launch_mma(const MArgs &a, dim3 grid, size_t smem, cudaStream_t st)
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3((kMmaWarps + 1) * 32);
+    cfg.blockDim = dim3(kM2Threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -732,20 +762,25 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st)
     a.kblocks = a0.kblocks;
     a.total_rows = a0.total_rows;
     a.nseg = a0.nseg;
-    a.nchunks = (a0.K + kChunk - 1) / kChunk;
     a.xcol_bytes = 2 * a0.K + 32;
-    const uint32_t budget = 220 * 1024;
-    int mt = a0.m >= 3 ? 4 : (int)a0.m;
-    while (mt > 1 && mma_smem_layout(2, mt, a.xcol_bytes, a.kblocks).total > budget) mt /= 2;
-    if (mma_smem_layout(2, mt, a.xcol_bytes, a.kblocks).total > budget)
-        return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: cols %u too large for the shared-memory activation", a0.K);
-    uint32_t stages = 6;
-    while (stages > 2 && mma_smem_layout(stages, mt, a.xcol_bytes, a.kblocks).total > budget) --stages;
-    a.stages = stages;
-    const size_t smem = mma_smem_layout(stages, mt, a.xcol_bytes, a.kblocks).total;
+    a.ipr = (a0.K + kItemCols - 1) / kItemCols;
+    const uint32_t budget = 216 * 1024;
     const uint32_t sms = (uint32_t)device_sms();
-    const uint32_t blocks16 = (a.total_rows + 15) / 16;
-    const uint32_t gx = blocks16 < sms ? blocks16 : sms;
+    const uint32_t gx = ((a.total_rows + 15) / 16) < sms ? (a.total_rows + 15) / 16 : sms;
+    const uint32_t rows_cta = (a.total_rows + gx - 1) / gx;
+    const uint32_t nrb_max = (rows_cta + 15) / 16 + 2 * (uint32_t)a.nseg;
+    if (nrb_max > kMaxRowBlocks) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: %u rows per CTA", rows_cta);
+    int mt = a0.m >= 3 ? 4 : (int)a0.m;
+    auto fits = [&](int mtt, uint32_t rbr) {
+        return mma_smem_layout(mtt, a.xcol_bytes, a.kblocks, rbr * a.ipr).total <= budget;
+    };
+    while (mt > 1 && !fits(mt, 1)) mt /= 2;
+    if (!fits(mt, 1)) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: cols %u too large", a0.K);
+    // row blocks per round: all of the CTA's if they fit, else as many as fit
+    uint32_t rbr = nrb_max;
+    while (rbr > 1 && !fits(mt, rbr)) --rbr;
+    a.rb_round = rbr;
+    const size_t smem = mma_smem_layout(mt, a.xcol_bytes, a.kblocks, rbr * a.ipr).total;
     const uint32_t gy = (a0.m + mt - 1) / mt;
     if (gy > 65535) return set_error(Q35CU_ERR_ARG, "gemv: too many tokens (%u)", a0.m);
     const dim3 grid(gx, gy);

@@ -404,8 +404,8 @@ __global__ void __launch_bounds__(kMaxCons + 32, 1) gemv_tma_kernel(const __grid
 // single calls agree bit for bit, and repeat exactly.
 constexpr int kM2Warps = 16;
 constexpr int kM2Threads = kM2Warps * 32;
-constexpr uint32_t kItemCols = 256;            // columns per work item
-constexpr uint32_t kMaxRowBlocks = 1024;       // row blocks per CTA (table in shared memory)
+constexpr uint32_t kItemCols = 256;   // columns per work item
+constexpr uint32_t kMaxRowBlocks = 256;
 
 struct MArgs {
     Seg seg[4];
@@ -415,6 +415,14 @@ struct MArgs {
     uint32_t ipr;         // items per row block = ceil(K / 256)
     uint32_t rb_round;    // row blocks per round (partials buffer)
     int nseg;
+};
+
+// one 16-row block of the CTA, resolved once: weight row pointer, the
+// segment's scale grid, first row in the segment, valid rows, segment
+struct RowBlock {
+    const uint8_t *w;
+    const float *s;
+    uint32_t r, nrows_seg;  // nrows_seg = valid rows | segment << 8
 };
 
 // shared-memory layout (byte offsets, 16-byte aligned)
@@ -428,7 +436,7 @@ __host__ __device__ __forceinline__ MmaSmem mma_smem_layout(uint32_t mt, uint32_
     L.xs = 0;
     L.xmul = 2 * mt * xcol_bytes;
     L.rbt = (L.xmul + mt * kblocks * 4 + 15) & ~15u;
-    L.part = L.rbt + kMaxRowBlocks * 8;
+    L.part = L.rbt + kMaxRowBlocks * (uint32_t)sizeof(RowBlock);
     L.total = L.part + items_round * 32 * 16;
     return L;
 }
@@ -449,25 +457,20 @@ __device__ __forceinline__ uint16_t f16_bits(float v)
     return h;
 }
 
-// one item's weights for this lane: rows g, g+8 x 4 groups of 64 columns
-struct ItemLoad {
-    uint4 v[8];  // [group][row half]
-};
-
 template <int MT>
 __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_constant__ MArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * a.ipr);
-    uint8_t *xs = smem + L.xs;                                   // [2*MT][xcol_bytes] f16 columns
-    float *xmul = reinterpret_cast<float *>(smem + L.xmul);      // [MT][kblocks] 2^-e
-    uint2 *rbt = reinterpret_cast<uint2 *>(smem + L.rbt);        // row blocks: (first virtual row, rows | seg << 8)
-    float4 *part = reinterpret_cast<float4 *>(smem + L.part);    // [items in round][32 lanes]
+    uint8_t *xs = smem + L.xs;                                    // [2*MT][xcol_bytes] f16 columns
+    float *xmul = reinterpret_cast<float *>(smem + L.xmul);       // [MT][kblocks] 2^-e
+    RowBlock *rbt = reinterpret_cast<RowBlock *>(smem + L.rbt);   // the CTA's row blocks
+    float4 *part = reinterpret_cast<float4 *>(smem + L.part);     // [items in round][32 lanes]
     __shared__ uint32_t nrb_s;
 
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t g = lane >> 2, tq = lane & 3;
-    const uint32_t K = a.K, ipr = a.ipr;
+    const uint32_t K = a.K, ipr = a.ipr, kbn = a.kblocks;
     const uint32_t vr0 = (uint32_t)(((uint64_t)blockIdx.x * a.total_rows) / gridDim.x);
     const uint32_t vr1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.total_rows) / gridDim.x);
     const uint32_t tok0 = blockIdx.y * MT;
@@ -479,11 +482,17 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
             int s = 0;
             for (int i = 1; i < a.nseg; ++i)
                 if (vr >= a.seg[i].vbegin) s = i;
+            const Seg &sg = a.seg[s];
             uint32_t e = vr + 16;
-            const uint32_t send = a.seg[s].vbegin + a.seg[s].rows;
+            const uint32_t send = sg.vbegin + sg.rows;
             e = e < vr1 ? e : vr1;
             e = e < send ? e : send;
-            rbt[n++] = make_uint2(vr, (e - vr) | ((uint32_t)s << 8));
+            RowBlock rb;
+            rb.r = vr - sg.vbegin;
+            rb.w = sg.W + (size_t)rb.r * K;
+            rb.s = sg.S;
+            rb.nrows_seg = (e - vr) | ((uint32_t)s << 8);
+            rbt[n++] = rb;
             vr = e;
         }
         nrb_s = n;
@@ -491,31 +500,85 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     __syncthreads();
     const uint32_t nrb = nrb_s;
 
-    // item -> this lane's weight addresses
-    auto issue = [&](ItemLoad &ld, uint32_t item) {
-        const uint2 rb = rbt[item / ipr];
-        const uint32_t c0 = (item % ipr) * kItemCols;
-        const Seg &sg = a.seg[rb.y >> 8];
-        const uint32_t nrows = rb.y & 0xFF;
-        const uint32_t r = rb.x - sg.vbegin;
-        const uint8_t *w0 = sg.W + (size_t)(r + g) * K + c0 + tq * 16;
+    // this lane's 8 loads of an item: rows g, g+8 x 4 groups of 64 columns
+    auto issue = [&](uint4 (&v)[8], uint32_t rbi, uint32_t sp) {
+        const RowBlock rb = rbt[rbi];
+        const uint32_t nrows = rb.nrows_seg & 0xFF, c0 = sp * kItemCols;
+        const uint8_t *w0 = rb.w + (size_t)g * K + c0 + tq * 16;
         const uint8_t *w1 = w0 + (size_t)8 * K;
+        const bool r0v = g < nrows, r1v = g + 8 < nrows;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const bool kv = c0 + q * 64 < K;
-            ld.v[2 * q] = (kv && g < nrows) ? ld_stream(w0 + q * 64) : make_uint4(0, 0, 0, 0);
-            ld.v[2 * q + 1] = (kv && g + 8 < nrows) ? ld_stream(w1 + q * 64) : make_uint4(0, 0, 0, 0);
+            v[2 * q] = (kv && r0v) ? ld_stream(w0 + q * 64) : make_uint4(0, 0, 0, 0);
+            v[2 * q + 1] = (kv && r1v) ? ld_stream(w1 + q * 64) : make_uint4(0, 0, 0, 0);
         }
     };
 
-    // prefetch this warp's first item (weights only) before waiting on the previous kernel
-    ItemLoad cur, nxt;
-    const uint32_t first_round_items = (nrb < a.rb_round ? nrb : a.rb_round) * ipr;
-    if (warp < first_round_items) issue(cur, warp);
+    // multiply one item (2 blocks of 128 columns) held in v; write its partial
+    const bool bcol = g < 2 * MT;  // this lane feeds a live B column
+    const uint8_t *xcol = xs + (size_t)(bcol ? g : 0) * a.xcol_bytes + tq * 32;
+    auto compute = [&](const uint4 (&v)[8], uint32_t rbi, uint32_t sp, uint32_t slot) {
+        const RowBlock rb = rbt[rbi];
+        const uint32_t c0 = sp * kItemCols;
+        // scale rows of g and g+8 (clamped into the segment)
+        const uint32_t rlast = a.seg[rb.nrows_seg >> 8].rows - 1;
+        uint32_t r_g = rb.r + g, r_g8 = r_g + 8;
+        r_g = r_g < rlast ? r_g : rlast;
+        r_g8 = r_g8 < rlast ? r_g8 : rlast;
+        const float *s0 = rb.s + (size_t)(r_g >> 7) * kbn, *s1 = rb.s + (size_t)(r_g8 >> 7) * kbn;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+            const uint32_t kb = (c0 >> 7) + hb;
+            if (kb < kbn) {
+                const float f0s = __ldg(s0 + kb), f1s = __ldg(s1 + kb);
+                float cz[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const uint4 A0 = v[2 * (2 * hb + q)], A1 = v[2 * (2 * hb + q) + 1];
+                    const uint32_t w0[4] = {A0.x, A0.y, A0.z, A0.w}, w1[4] = {A1.x, A1.y, A1.z, A1.w};
+                    uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
+                    if (bcol) {
+                        const uint8_t *xb = xcol + (size_t)(c0 + hb * 128 + q * 64) * 2;
+                        b01 = *reinterpret_cast<const uint4 *>(xb);
+                        b23 = *reinterpret_cast<const uint4 *>(xb + 16);
+                    }
+                    const uint32_t bw[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t a0, a2, a1, a3;
+                        hw_f16x2(w0[j], a0, a2);
+                        hw_f16x2(w1[j], a1, a3);
+                        mma16816(cz, a0, a1, a2, a3, bw[2 * j], bw[2 * j + 1]);
+                    }
+                }
+                const float xm = tq < MT ? xmul[tq * kbn + kb] : 0.f;
+                const float f0 = f0s * xm, f1 = f1s * xm;
+                acc[0] = fmaf(f0, cz[0], acc[0]);
+                acc[1] = fmaf(f0, cz[1], acc[1]);
+                acc[2] = fmaf(f1, cz[2], acc[2]);
+                acc[3] = fmaf(f1, cz[3], acc[3]);
+            }
+        }
+        part[(size_t)slot * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    };
+
+    // items of this warp in round order: (row block, split) advanced by 16 items
+    const uint32_t nitems = nrb * ipr;
+    uint32_t it = warp, rbi = warp / ipr, sp = warp % ipr;
+    auto advance = [&]() {
+        it += kM2Warps;
+        sp += kM2Warps;
+        while (sp >= ipr) { sp -= ipr; ++rbi; }
+    };
+
+    uint4 va[8], vb[8];
+    if (it < nitems) issue(va, rbi, sp);  // weights only: before waiting on the previous kernel
 
     griddep_wait();
-    for (uint32_t idx = warp; idx < MT * a.kblocks; idx += kM2Warps) {
-        const uint32_t tt = idx / a.kblocks, kb = idx % a.kblocks;
+    for (uint32_t idx = warp; idx < MT * kbn; idx += kM2Warps) {
+        const uint32_t tt = idx / kbn, kb = idx % kbn;
         const uint32_t k = kb * 128 + lane * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (tok0 + tt < a.m) v = __ldg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + k));
@@ -540,86 +603,43 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
             make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
         *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) =
             make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
-        if (lane == 0) xmul[tt * a.kblocks + kb] = down;
+        if (lane == 0) xmul[tt * kbn + kb] = down;
     }
     __syncthreads();
 
-    const bool bcol = g < 2 * MT;  // this lane feeds a live B column
-    const uint8_t *xcol = xs + (size_t)(bcol ? g : 0) * a.xcol_bytes;
     for (uint32_t rb0 = 0; rb0 < nrb; rb0 += a.rb_round) {
         const uint32_t nrb_r = (nrb - rb0) < a.rb_round ? (nrb - rb0) : a.rb_round;
-        const uint32_t items = nrb_r * ipr;
-        for (uint32_t it = warp; it < items; it += kM2Warps) {
-            const uint32_t item = rb0 * ipr + it;
-            const uint32_t nit = it + kM2Warps;
-            // next item of this warp: later in this round, or its first item of the next round
-            const uint32_t nrb_next = rb0 + a.rb_round < nrb ? ((nrb - rb0 - a.rb_round) < a.rb_round
-                                                                   ? (nrb - rb0 - a.rb_round)
-                                                                   : a.rb_round)
-                                                              : 0;
-            if (nit < items) issue(nxt, rb0 * ipr + nit);
-            else if (warp < nrb_next * ipr) issue(nxt, (rb0 + a.rb_round) * ipr + warp);
-            // multiply the current item: 2 blocks of 128 columns = 2 x 2 groups x 4 k-steps
-            const uint2 rb = rbt[item / ipr];
-            const Seg &sg = a.seg[rb.y >> 8];
-            const uint32_t rlast = sg.rows - 1;
-            uint32_t r_g = rb.x - sg.vbegin + g, r_g8 = r_g + 8;
-            r_g = r_g < rlast ? r_g : rlast;
-            r_g8 = r_g8 < rlast ? r_g8 : rlast;
-            const uint32_t c0 = (item % ipr) * kItemCols;
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int hb = 0; hb < 2; ++hb) {
-                const uint32_t kb = (c0 >> 7) + hb;
-                if (kb < a.kblocks) {
-                    float cz[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const uint4 A0 = cur.v[2 * (2 * hb + q)], A1 = cur.v[2 * (2 * hb + q) + 1];
-                        const uint32_t w0[4] = {A0.x, A0.y, A0.z, A0.w}, w1[4] = {A1.x, A1.y, A1.z, A1.w};
-                        // B: f16 of columns c0 + 128hb + 64q + 16tq + 4j .. +3 for step j
-                        const uint8_t *xb = xcol + (size_t)(c0 + hb * 128 + q * 64 + tq * 16) * 2;
-                        uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
-                        if (bcol) {
-                            b01 = *reinterpret_cast<const uint4 *>(xb);
-                            b23 = *reinterpret_cast<const uint4 *>(xb + 16);
-                        }
-                        const uint32_t bw[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            uint32_t a0, a2, a1, a3;
-                            hw_f16x2(w0[j], a0, a2);
-                            hw_f16x2(w1[j], a1, a3);
-                            mma16816(cz, a0, a1, a2, a3, bw[2 * j], bw[2 * j + 1]);
-                        }
-                    }
-                    const float xm = tq < MT ? xmul[tq * a.kblocks + kb] : 0.f;
-                    const float f0 = __ldg(sg.S + (size_t)(r_g >> 7) * a.kblocks + kb) * xm;
-                    const float f1 = __ldg(sg.S + (size_t)(r_g8 >> 7) * a.kblocks + kb) * xm;
-                    acc[0] = fmaf(f0, cz[0], acc[0]);
-                    acc[1] = fmaf(f0, cz[1], acc[1]);
-                    acc[2] = fmaf(f1, cz[2], acc[2]);
-                    acc[3] = fmaf(f1, cz[3], acc[3]);
-                }
+        const uint32_t iend = (rb0 + nrb_r) * ipr;  // items of this round: [rb0 * ipr, iend)
+        // ping-pong: the other buffer's item is in flight while this one multiplies
+        while (it < iend) {
+            uint32_t c_it = it, c_rb = rbi, c_sp = sp;
+            advance();
+            if (it < nitems) issue(vb, rbi, sp);
+            compute(va, c_rb, c_sp, c_it - rb0 * ipr);
+            if (it >= iend) {
+                // next item (if any) sits in vb and belongs to the next round
+                for (int q = 0; q < 8; ++q) va[q] = vb[q];
+                break;
             }
-            part[(size_t)it * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            cur = nxt;
+            c_it = it; c_rb = rbi; c_sp = sp;
+            advance();
+            if (it < nitems) issue(va, rbi, sp);
+            compute(vb, c_rb, c_sp, c_it - rb0 * ipr);
         }
         __syncthreads();
-        // combine: output (row i of block, token tt) = sum over items of the block, in column order
+        // combine: output (row i of block, token tt) = sum over the block's items, in column order
         for (uint32_t o = t; o < nrb_r * 16 * MT; o += kM2Threads) {
             const uint32_t rbl = o / (16 * MT), i = (o / MT) % 16, tt = o % MT;
-            const uint2 rb = rbt[rb0 + rbl];
-            const uint32_t nrows = rb.y & 0xFF;
-            if (i >= nrows || tok0 + tt >= a.m) continue;
+            const RowBlock rb = rbt[rb0 + rbl];
+            if (i >= (rb.nrows_seg & 0xFF) || tok0 + tt >= a.m) continue;
             const uint32_t src = (i & 7) * 4 + tt;
             float y = 0.f;
             for (uint32_t s = 0; s < ipr; ++s) {
                 const float4 p4 = part[(size_t)(rbl * ipr + s) * 32 + src];
                 y += i < 8 ? p4.x + p4.y : p4.z + p4.w;
             }
-            const Seg &sg = a.seg[rb.y >> 8];
-            sg.Y[(size_t)(tok0 + tt) * sg.ldy + (rb.x - sg.vbegin + i)] = y;
+            const Seg &sg = a.seg[rb.nrows_seg >> 8];
+            sg.Y[(size_t)(tok0 + tt) * sg.ldy + rb.r + i] = y;
         }
         __syncthreads();
     }

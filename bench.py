@@ -254,12 +254,16 @@ def kernel_roofline(q35cu, torch, st, hbm_peak, reps=3):
     collectives), on the stream they run on; sum of algorithmic bytes / sum of
     launch durations."""
     stream = torch.cuda.current_stream()
-    launches = []
+    launches, labels = [], []
     for L in st.layers:
         launches.append(("multi", [p.w for p in L.col_in]))
+        labels.append("qkv+z" if L.kind == "dn" else "q+k+v")
         launches.append(("gemv", L.attn_out.w))
+        labels.append("out" if L.kind == "dn" else "o")
         launches.append(("multi", [L.gate.w, L.up.w]))
+        labels.append("gate+up")
         launches.append(("gemv", L.down.w))
+        labels.append("down")
     total_bytes = 0
     for kind, w in launches:
         ws = w if kind == "multi" else [w]
@@ -268,6 +272,7 @@ def kernel_roofline(q35cu, torch, st, hbm_peak, reps=3):
     xs = torch.randn((stack_max_cols(st),), device="cuda")
     ybuf = torch.empty((40000,), device="cuda")
     durs = []
+    per = {}
     for _ in range(reps):
         evs = []
         for kind, w in launches:
@@ -284,10 +289,20 @@ def kernel_roofline(q35cu, torch, st, hbm_peak, reps=3):
             b.record(stream)
             evs.append((a, b))
         torch.cuda.synchronize()
-        durs.append(sum(a.elapsed_time(b) for a, b in evs) * 1e-3)
+        ts = [a.elapsed_time(b) * 1e-3 for a, b in evs]
+        durs.append(sum(ts))
+        for (kind, w), lab, dt in zip(launches, labels, ts):
+            ws = w if kind == "multi" else [w]
+            by = sum(gemv_bytes(ww.rows, ww.cols) for ww in ws)
+            e = per.setdefault(lab, [0, 0.0, 0])
+            e[0] += by
+            e[1] += dt
+            e[2] += 1
     t = statistics.median(durs)
     ach = total_bytes / t / 1e9
-    return ach, total_bytes / len(launches), t / len(launches), len(launches)
+    breakdown = {lab: {"launches_per_step": e[2] // reps, "us": round(e[1] / e[2] * 1e6, 2),
+                       "GBps": round(e[0] / e[1] / 1e9, 1)} for lab, e in per.items()}
+    return ach, total_bytes / len(launches), t / len(launches), len(launches), breakdown
 
 
 def stack_max_cols(st):
@@ -474,7 +489,7 @@ def run_ours(args):
                "path": "pinned H2D of the 64 layer inputs + graphed TP step + D2H of the 64 layer outputs"}
 
     # live roofline of the dominant kernel (the decode GEMV), this rank
-    ach, bytes_per_launch, s_per_launch, nl = kernel_roofline(q35cu, torch, st, hbm_peak)
+    ach, bytes_per_launch, s_per_launch, nl, breakdown = kernel_roofline(q35cu, torch, st, hbm_peak)
     ach = max_over_ranks(-ach) * -1 if world > 1 else ach  # slowest rank
     traffic = None
     tp = os.path.join(REPO, "profiles", "traffic.json")
@@ -515,10 +530,10 @@ def run_ours(args):
             "gpu_launches": main["kernels_per_step"] * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "traffic": traffic,
-                         "kernel": "gemv_rs_kernel (decode GEMV, row stream), all launches of one step",
+                         "kernel": "gemv_mma_kernel (decode GEMV), all launches of one step",
                          "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
                          "launches_timed": nl, "algorithmic_bytes_per_launch": round(bytes_per_launch),
-                         "us_per_launch": round(s_per_launch * 1e6, 2)},
+                         "us_per_launch": round(s_per_launch * 1e6, 2), "by_projection": breakdown},
             "clocks": main["clocks"],
             "e2e": e2e,
         }

@@ -500,50 +500,53 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     __syncthreads();
     const uint32_t nrb = nrb_s;
 
-    // this lane's 8 loads of an item: rows g, g+8 x 4 groups of 64 columns
-    auto issue = [&](uint4 (&v)[8], uint32_t rbi, uint32_t sp) {
+    // this lane's loads of an item: rows g, g+8 x 4 groups of 64 columns, and
+    // the block scales of both rows.  Out-of-range rows and columns read a
+    // clamped in-range address instead of being predicated off: their
+    // products land only in rows / blocks that are never stored.
+    auto issue = [&](uint4 (&v)[8], float (&sc)[4], uint32_t rbi, uint32_t sp) {
         const RowBlock rb = rbt[rbi];
         const uint32_t nrows = rb.nrows_seg & 0xFF, c0 = sp * kItemCols;
-        const uint8_t *w0 = rb.w + (size_t)g * K + c0 + tq * 16;
-        const uint8_t *w1 = w0 + (size_t)8 * K;
-        const bool r0v = g < nrows, r1v = g + 8 < nrows;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const bool kv = c0 + q * 64 < K;
-            v[2 * q] = (kv && r0v) ? ld_stream(w0 + q * 64) : make_uint4(0, 0, 0, 0);
-            v[2 * q + 1] = (kv && r1v) ? ld_stream(w1 + q * 64) : make_uint4(0, 0, 0, 0);
-        }
+        const uint32_t g0 = g < nrows ? g : nrows - 1, g1 = g + 8 < nrows ? g + 8 : nrows - 1;
+        const uint8_t *w0 = rb.w + (size_t)g0 * K + c0 + tq * 16;
+        const uint8_t *w1 = rb.w + (size_t)g1 * K + c0 + tq * 16;
+        const uint32_t c1 = c0 + 128 < K ? 128u : 0u;  // second block of the item (re-read if past K)
+        v[0] = ld_stream(w0);
+        v[1] = ld_stream(w1);
+        v[2] = ld_stream(w0 + 64);
+        v[3] = ld_stream(w1 + 64);
+        v[4] = ld_stream(w0 + c1);
+        v[5] = ld_stream(w1 + c1);
+        v[6] = ld_stream(w0 + c1 + 64);
+        v[7] = ld_stream(w1 + c1 + 64);
+        const float *s0 = rb.s + (size_t)((rb.r + g0) >> 7) * kbn + (c0 >> 7);
+        const float *s1 = rb.s + (size_t)((rb.r + g1) >> 7) * kbn + (c0 >> 7);
+        const uint32_t d1 = c1 >> 7;
+        sc[0] = __ldg(s0);
+        sc[1] = __ldg(s1);
+        sc[2] = __ldg(s0 + d1);
+        sc[3] = __ldg(s1 + d1);
     };
 
-    // multiply one item (2 blocks of 128 columns) held in v; write its partial
-    const bool bcol = g < 2 * MT;  // this lane feeds a live B column
-    const uint8_t *xcol = xs + (size_t)(bcol ? g : 0) * a.xcol_bytes + tq * 32;
-    auto compute = [&](const uint4 (&v)[8], uint32_t rbi, uint32_t sp, uint32_t slot) {
-        const RowBlock rb = rbt[rbi];
+    // multiply one item (2 blocks of 128 columns) held in v; write its partial.
+    // Lanes with g >= 2*MT feed B columns no output reads: they load a live
+    // column (finite data) rather than zeros, as MMA output columns never mix.
+    const uint8_t *xcol = xs + (size_t)(g % (2 * MT)) * a.xcol_bytes + tq * 32;
+    auto compute = [&](const uint4 (&v)[8], const float (&sc)[4], uint32_t sp, uint32_t slot) {
         const uint32_t c0 = sp * kItemCols;
-        // scale rows of g and g+8 (clamped into the segment)
-        const uint32_t rlast = a.seg[rb.nrows_seg >> 8].rows - 1;
-        uint32_t r_g = rb.r + g, r_g8 = r_g + 8;
-        r_g = r_g < rlast ? r_g : rlast;
-        r_g8 = r_g8 < rlast ? r_g8 : rlast;
-        const float *s0 = rb.s + (size_t)(r_g >> 7) * kbn, *s1 = rb.s + (size_t)(r_g8 >> 7) * kbn;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
             const uint32_t kb = (c0 >> 7) + hb;
             if (kb < kbn) {
-                const float f0s = __ldg(s0 + kb), f1s = __ldg(s1 + kb);
                 float cz[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
                     const uint4 A0 = v[2 * (2 * hb + q)], A1 = v[2 * (2 * hb + q) + 1];
                     const uint32_t w0[4] = {A0.x, A0.y, A0.z, A0.w}, w1[4] = {A1.x, A1.y, A1.z, A1.w};
-                    uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
-                    if (bcol) {
-                        const uint8_t *xb = xcol + (size_t)(c0 + hb * 128 + q * 64) * 2;
-                        b01 = *reinterpret_cast<const uint4 *>(xb);
-                        b23 = *reinterpret_cast<const uint4 *>(xb + 16);
-                    }
+                    const uint8_t *xb = xcol + (size_t)(c0 + hb * 128 + q * 64) * 2;
+                    const uint4 b01 = *reinterpret_cast<const uint4 *>(xb);
+                    const uint4 b23 = *reinterpret_cast<const uint4 *>(xb + 16);
                     const uint32_t bw[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
@@ -553,8 +556,8 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
                         mma16816(cz, a0, a1, a2, a3, bw[2 * j], bw[2 * j + 1]);
                     }
                 }
-                const float xm = tq < MT ? xmul[tq * kbn + kb] : 0.f;
-                const float f0 = f0s * xm, f1 = f1s * xm;
+                const float xm = xmul[(tq < MT ? tq : 0) * kbn + kb];
+                const float f0 = sc[2 * hb] * xm, f1 = sc[2 * hb + 1] * xm;
                 acc[0] = fmaf(f0, cz[0], acc[0]);
                 acc[1] = fmaf(f0, cz[1], acc[1]);
                 acc[2] = fmaf(f1, cz[2], acc[2]);
@@ -574,7 +577,8 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     };
 
     uint4 va[8], vb[8];
-    if (it < nitems) issue(va, rbi, sp);  // weights only: before waiting on the previous kernel
+    float sa[4], sb[4];
+    if (it < nitems) issue(va, sa, rbi, sp);  // weights only: before waiting on the previous kernel
 
     griddep_wait();
     for (uint32_t idx = warp; idx < MT * kbn; idx += kM2Warps) {
@@ -612,19 +616,21 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
         const uint32_t iend = (rb0 + nrb_r) * ipr;  // items of this round: [rb0 * ipr, iend)
         // ping-pong: the other buffer's item is in flight while this one multiplies
         while (it < iend) {
-            uint32_t c_it = it, c_rb = rbi, c_sp = sp;
+            uint32_t c_it = it, c_sp = sp;
             advance();
-            if (it < nitems) issue(vb, rbi, sp);
-            compute(va, c_rb, c_sp, c_it - rb0 * ipr);
+            if (it < nitems) issue(vb, sb, rbi, sp);
+            compute(va, sa, c_sp, c_it - rb0 * ipr);
             if (it >= iend) {
-                // next item (if any) sits in vb and belongs to the next round
+                // the next item (if any) sits in vb and belongs to the next round
                 for (int q = 0; q < 8; ++q) va[q] = vb[q];
+                for (int q = 0; q < 4; ++q) sa[q] = sb[q];
                 break;
             }
-            c_it = it; c_rb = rbi; c_sp = sp;
+            c_it = it;
+            c_sp = sp;
             advance();
-            if (it < nitems) issue(va, rbi, sp);
-            compute(vb, c_rb, c_sp, c_it - rb0 * ipr);
+            if (it < nitems) issue(va, sa, rbi, sp);
+            compute(vb, sb, c_sp, c_it - rb0 * ipr);
         }
         __syncthreads();
         // combine: output (row i of block, token tt) = sum over the block's items, in column order

@@ -437,7 +437,7 @@ __host__ __device__ __forceinline__ MmaSmem mma_smem_layout(uint32_t mt, uint32_
     L.xmul = 2 * mt * xcol_bytes;
     L.rbt = (L.xmul + mt * kblocks * 4 + 15) & ~15u;
     L.part = L.rbt + kMaxRowBlocks * (uint32_t)sizeof(RowBlock);
-    L.total = L.part + items_round * 32 * 16;
+    L.total = L.part + items_round * 16 * mt * 4;
     return L;
 }
 
@@ -465,7 +465,7 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     uint8_t *xs = smem + L.xs;                                    // [2*MT][xcol_bytes] f16 columns
     float *xmul = reinterpret_cast<float *>(smem + L.xmul);       // [MT][kblocks] 2^-e
     RowBlock *rbt = reinterpret_cast<RowBlock *>(smem + L.rbt);   // the CTA's row blocks
-    float4 *part = reinterpret_cast<float4 *>(smem + L.part);     // [items in round][32 lanes]
+    float *part = reinterpret_cast<float *>(smem + L.part);       // [items in round][16 rows][MT]
     __shared__ uint32_t nrb_s;
 
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -564,7 +564,11 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
                 acc[3] = fmaf(f1, cz[3], acc[3]);
             }
         }
-        part[(size_t)slot * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        // lane (g, tq) holds token tq of rows g and g+8 as (hi, lo) column pairs
+        if (tq < MT) {
+            part[((size_t)slot * 16 + g) * MT + tq] = acc[0] + acc[1];
+            part[((size_t)slot * 16 + g + 8) * MT + tq] = acc[2] + acc[3];
+        }
     };
 
     // items of this warp in round order: (row block, split) advanced by 16 items
@@ -638,12 +642,8 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
             const uint32_t rbl = o / (16 * MT), i = (o / MT) % 16, tt = o % MT;
             const RowBlock rb = rbt[rb0 + rbl];
             if (i >= (rb.nrows_seg & 0xFF) || tok0 + tt >= a.m) continue;
-            const uint32_t src = (i & 7) * 4 + tt;
             float y = 0.f;
-            for (uint32_t s = 0; s < ipr; ++s) {
-                const float4 p4 = part[(size_t)(rbl * ipr + s) * 32 + src];
-                y += i < 8 ? p4.x + p4.y : p4.z + p4.w;
-            }
+            for (uint32_t s = 0; s < ipr; ++s) y += part[((size_t)(rbl * ipr + s) * 16 + i) * MT + tt];
             const Seg &sg = a.seg[rb.nrows_seg >> 8];
             sg.Y[(size_t)(tok0 + tt) * sg.ldy + rb.r + i] = y;
         }

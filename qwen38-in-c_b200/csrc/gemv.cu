@@ -585,33 +585,49 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     if (it < nitems) issue(va, sa, rbi, sp);  // weights only: before waiting on the previous kernel
 
     griddep_wait();
-    for (uint32_t idx = warp; idx < MT * kbn; idx += kM2Warps) {
-        const uint32_t tt = idx / kbn, kb = idx % kbn;
-        const uint32_t k = kb * 128 + lane * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (tok0 + tt < a.m) v = __ldg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + k));
-        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    // activation -> f16 hi/lo columns: one warp per (token, 128-column block);
+    // a warp's blocks are loaded four at a time so their L2 round trips overlap
+    for (uint32_t base = warp; base < MT * kbn; base += 4 * kM2Warps) {
+        float4 xv4[4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-        int e = 0;  // 2^e with max |x*2^e| < 2^15; |e| <= 126 keeps 2^e and 2^-e normal
-        if (mx > 0.f && mx <= 3.402823466e38f) {
-            const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;
-            e = 14 - E;
-            e = e > 126 ? 126 : (e < -126 ? -126 : e);
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t idx = base + u * kM2Warps;
+            const uint32_t tt = idx / kbn, kb = idx % kbn;
+            xv4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (idx < MT * kbn && tok0 + tt < a.m)
+                xv4[u] = __ldg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + kb * 128 + lane * 4));
         }
-        const float up = __uint_as_float((uint32_t)(e + 127) << 23), down = __uint_as_float((uint32_t)(127 - e) << 23);
-        const float xv[4] = {v.x * up, v.y * up, v.z * up, v.w * up};
-        uint16_t hi[4], lo[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            hi[j] = f16_bits(xv[j]);
-            lo[j] = f16_bits(xv[j] - __half2float(__ushort_as_half(hi[j])));
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t idx = base + u * kM2Warps;
+            if (idx >= MT * kbn) break;
+            const uint32_t tt = idx / kbn, kb = idx % kbn;
+            const uint32_t k = kb * 128 + lane * 4;
+            const float4 v = xv4[u];
+            float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+            int e = 0;  // 2^e with max |x*2^e| < 2^15; |e| <= 126 keeps 2^e and 2^-e normal
+            if (mx > 0.f && mx <= 3.402823466e38f) {
+                const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;
+                e = 14 - E;
+                e = e > 126 ? 126 : (e < -126 ? -126 : e);
+            }
+            const float up = __uint_as_float((uint32_t)(e + 127) << 23);
+            const float down = __uint_as_float((uint32_t)(127 - e) << 23);
+            const float xv[4] = {v.x * up, v.y * up, v.z * up, v.w * up};
+            uint16_t hi[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                hi[j] = f16_bits(xv[j]);
+                lo[j] = f16_bits(xv[j] - __half2float(__ushort_as_half(hi[j])));
+            }
+            *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) =
+                make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
+            *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) =
+                make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
+            if (lane == 0) xmul[tt * kbn + kb] = down;
         }
-        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) =
-            make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
-        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) =
-            make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
-        if (lane == 0) xmul[tt * kbn + kb] = down;
     }
     __syncthreads();
 

@@ -955,6 +955,10 @@ int device_status(uint32_t *status, bool clear)
         const uint32_t z = 0;
         Q35CU_CUDA(cudaMemcpyToSymbol(g_device_status, &z, 4));
     }
+    uint32_t g = 0;
+    const int rc = gemm_status(&g, clear);
+    if (rc) return rc;
+    if (!*status) *status = g;
     return Q35CU_OK;
 }
 

@@ -60,6 +60,8 @@ int scan_nan_codes(const uint8_t *W, size_t bytes, uint32_t *d_flag, cudaStream_
 int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y,
                     cudaStream_t st);
 int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
+int launch_round_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
+int gemm_status(uint32_t *status, bool clear);
 int launch_bf16_to_f32_scales(const uint16_t *src, float *dst, size_t n, cudaStream_t st);
 int launch_f32_to_bf16_scales(const float *src, uint16_t *dst, size_t n, cudaStream_t st);
 int launch_synth_fp8(uint64_t seed, float stddev, uint32_t grows, uint32_t gcols,

@@ -88,6 +88,8 @@ struct DevState {
     size_t h_cap = 0;
     void *d_stage = nullptr;  // device, in + out
     size_t d_cap = 0;
+    void *d_xbf = nullptr;    // device bf16 copy of a prefill activation batch
+    size_t xbf_cap = 0;
     uint32_t *d_flag = nullptr;  // 4-byte scratch word for upload scans
 };
 
@@ -719,6 +721,18 @@ Q35_API const char *q35_mm_impl_fp8(void) { return "sm_100a"; }
 
 namespace {
 
+// batches of at least this many tokens take the tensor-core GEMM
+// (Q35CU_GEMM_MIN_TOKENS overrides; the default keeps M <= 64 on the fp32 GEMV)
+uint32_t gemm_min_tokens()
+{
+    static uint32_t v = 0;
+    if (!v) {
+        const char *e = getenv("Q35CU_GEMM_MIN_TOKENS");
+        v = (e && atoi(e) > 0) ? (uint32_t)atoi(e) : 128u;
+    }
+    return v;
+}
+
 // a bounded device-side wait that gave up leaves a code in the status word
 int check_device_status()
 {
@@ -787,7 +801,28 @@ Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint
     if (!W || !scale_bf16 || !X) rc = set_error(Q35CU_ERR_ARG, "q35_mm_fp8_batch: NULL input");
     q35cu_weight *w = rc ? nullptr : cached_weight(0, W, scale_bf16, rows, cols);
     if (!rc && !w) rc = t_err;
-    if (!rc)
+    // prefill-sized batches run the tensor-core GEMM on bf16-rounded activations
+    const bool tc = n >= gemm_min_tokens() && cols % 16 == 0;
+    if (!rc && tc) {
+        DevState *d = dev_state();
+        const size_t xb = (size_t)n * cols * 2;
+        if (xb > d->xbf_cap) {
+            if (d->d_xbf) dev_free(d->d_xbf, d->xbf_cap);
+            d->d_xbf = nullptr;
+            d->xbf_cap = 0;
+            rc = dev_alloc(&d->d_xbf, xb);
+            if (!rc) d->xbf_cap = xb;
+        }
+    }
+    if (!rc && tc)
+        rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
+            DevState *d = dev_state();
+            uint16_t *xbf = static_cast<uint16_t *>(d->d_xbf);
+            int r = launch_round_bf16(dx, xbf, (size_t)n * cols, st);
+            if (r) return r;
+            return launch_gemm_fp8(w, xbf, n, dy, st);
+        });
+    else if (!rc)
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
             GemvSeg g = seg_of(w, dy, rows);
             // token tiles of at most 64 per launch keep the grid's y extent small

@@ -282,7 +282,8 @@ def multi(ws, X, Ys, m: int = 1, stream=None) -> None:
 
 
 def gemm(w: Weight, Xb, Y, stream=None) -> None:
-    """Tensor-core GEMM: Y[m, rows] fp32 = Xb[m, cols] (bf16 as int16/bfloat16 tensor) (W.s)^T."""
+    """Tensor-core GEMM: Y[m, rows] fp32 = Xb[m, cols] (bf16 bits, any 2-byte dtype) (W.s)^T."""
+    assert Xb.element_size() == 2 and Xb.is_contiguous() and Y.is_contiguous()
     check(load().q35cu_gemm_fp8(w.h, _ptr(Xb), Xb.shape[0], _ptr(Y), _stream(stream)))
 
 

@@ -305,6 +305,46 @@ def kernel_roofline(q35cu, torch, st, hbm_peak, reps=3):
     return ach, total_bytes / len(launches), t / len(launches), len(launches), breakdown
 
 
+C2_SHAPES = [("qkv", 10240, 5120), ("z", 6144, 5120), ("out", 5120, 6144), ("q", 12288, 5120),
+             ("k", 1024, 5120), ("v", 1024, 5120), ("o", 5120, 6144), ("gate", 17408, 5120),
+             ("up", 17408, 5120), ("down", 5120, 17408)]
+
+
+def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
+    """Configuration 2: one decoder layer's projections at M=2048 tokens through
+    the tensor-core GEMM (device API, bf16-rounded activations resident in HBM)."""
+    ws = [(n, q35cu.Weight.synth_fp8(9000 + i, r, c)) for i, (n, r, c) in enumerate(C2_SHAPES)]
+    try:
+        kmax = max(w.cols for _, w in ws)
+        X = torch.randn((m, kmax), device="cuda").to(torch.bfloat16)
+        xs = {w.cols: X[:, : w.cols].contiguous() for _, w in ws}
+        per, tot_f, tot_t = {}, 0.0, 0.0
+        for n, w in ws:
+            yv = torch.empty((m, w.rows), device="cuda")
+            q35cu.gemm(w, xs[w.cols].view(torch.int16), yv)  # warm-up
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                q35cu.gemm(w, xs[w.cols].view(torch.int16), yv)
+            e1.record()
+            torch.cuda.synchronize()
+            dt = e0.elapsed_time(e1) * 1e-3 / reps
+            fl = 2.0 * m * w.rows * w.cols
+            per[n] = {"rows": w.rows, "cols": w.cols, "us": round(dt * 1e6, 1), "TFLOPs": round(fl / dt / 1e12, 1)}
+            tot_f += fl
+            tot_t += dt
+    finally:
+        for _, w in ws:
+            w.free()
+    ach = tot_f / tot_t / 1e12
+    return {"m": m, "flops": tot_f, "ms": round(tot_t * 1e3, 3), "TFLOPs": round(ach, 1),
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": bf16_peak, "unit": "TFLOP/s",
+                         "frac": round(ach / bf16_peak, 4), "kernel": "gemm_fp8_tc_kernel",
+                         "peak_source": "measured bf16_tflops (burst, MEASURED_PEAKS.json)"},
+            "by_projection": per}
+
+
 def stack_max_cols(st):
     return max(max(p.w.cols for p in L.col_in + [L.attn_out, L.gate, L.up, L.down]) for L in st.layers)
 
@@ -507,6 +547,7 @@ def run_ours(args):
             for m in (1, 4, 16, 64):
                 sweep.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10))
         extras["config1_sweep"] = sweep
+        extras["config2_prefill"] = time_prefill_c2(q35cu, torch, bf16_peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_extras:

@@ -120,6 +120,23 @@ int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint32_t ldx
  * promotion.  Needs cols % 16 == 0. */
 int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m,
                    float *Y, void *stream);
+/* The prefill GEMM of q35cu_gemm_fp8 on fp32 activations, for callers that
+ * may not have the library allocate device memory: a serving process that
+ * reserved its HBM budget up front, or a loop that cannot absorb the device
+ * synchronisation a cudaMalloc / cudaFree can bring.  No counterpart in the
+ * reference (its matmuls run on host memory).
+ *   X [m, cols] fp32 and Y [m, rows] fp32 are device memory owned by the
+ *   caller; X is rounded to bf16 (the prefill contract) into a fixed 16 MiB
+ *   array compiled into the library -- every GPU that loads the library
+ *   holds it until exit -- so m * cols may be at most
+ *   Q35CU_NOALLOC_MAX_ACTS; larger calls fail with Q35CU_ERR_ARG.
+ *   All calls share that array: calls that overlap on the GPU race.
+ *   The first call on a device looks up the array's address and configures
+ *   the kernel; make it before any stream capture.  stream NULL = the
+ *   legacy default stream.  Allocates nothing. */
+#define Q35CU_NOALLOC_MAX_ACTS (8u << 20)
+int q35cu_gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m,
+                               float *Y, void *stream);
 /* fp32 -> bf16 (nearest even) conversion of n values. */
 int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream);
 /* y[rows] = W x for a bf16 weight (q35_mm_bf16). */

@@ -133,9 +133,6 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar)
                  : "memory");
 }
 
-#define Q35CU_R32(p) p[0], p[1], p[2], p[3], p[4], p[5], p[6], p[7], p[8], p[9], p[10], p[11], p[12], p[13], \
-                     p[14], p[15], p[16], p[17], p[18], p[19], p[20], p[21], p[22], p[23], p[24], p[25], p[26], \
-                     p[27], p[28], p[29], p[30], p[31]
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
 {
     asm volatile(
@@ -420,6 +417,82 @@ int launch_round_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st)
     return Q35CU_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Prefill GEMM for callers that must not allocate device memory.
+//
+// q35cu_gemm_fp8 takes bf16 activations; a caller holding fp32 activations
+// needs a bf16 copy first, and the host entry point q35_mm_fp8_batch keeps
+// that copy in a buffer it allocates.  Some callers cannot let the library
+// call cudaMalloc at that point: a serving process that reserved its whole
+// HBM budget up front, or a decode/prefill loop that cannot afford the
+// device-wide synchronisation a cudaMalloc/cudaFree may imply.  For them the
+// bf16 copy lives in a fixed array compiled into this file instead.
+//
+//   * the array holds kNoAllocMaxActs bf16 values (16 MiB); every GPU that
+//     loads the library keeps it until the process exits;
+//   * a call with m * cols > kNoAllocMaxActs is rejected with Q35CU_ERR_ARG;
+//   * every call reuses the same array: two calls whose work overlaps on the
+//     GPU (different streams, no ordering) race on it;
+//   * each call overwrites exactly the m * cols values it reads, so nothing
+//     needs clearing between calls;
+//   * the first call on a device looks up the array's device address
+//     (cudaGetSymbolAddress) and sets the GEMM's shared-memory limit; make
+//     that first call before any stream capture.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocMaxActs = (size_t)8 << 20;
+static __device__ __align__(256) uint16_t g_noalloc_acts[kNoAllocMaxActs];
+
+namespace {
+
+__global__ void round_bf16_noalloc(const float *x, uint16_t *y, size_t n)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __bfloat16_as_ushort(__float2bfloat16_rn(x[i]));
+}
+
+// the array's device address, looked up once per device with that device current
+int noalloc_scratch(uint16_t **out)
+{
+    static uint16_t *addr[64] = {};
+    int dev = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_acts);
+        if (e != cudaSuccess || !p) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_acts)");
+        addr[dev] = static_cast<uint16_t *>(p);
+    }
+    *out = addr[dev];
+    return Q35CU_OK;
+}
+
+}  // namespace
+
+int gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m, float *Y, cudaStream_t st)
+{
+    if (!w || w->kind != 0 || !X || !Y) return set_error(Q35CU_ERR_ARG, "gemm_fp8_f32_noalloc: bad arguments");
+    if (!m) return Q35CU_OK;
+    const size_t n = (size_t)m * w->cols;
+    if (n > kNoAllocMaxActs)
+        return set_error(Q35CU_ERR_ARG,
+                         "gemm_fp8_f32_noalloc: %u tokens x %u cols = %zu activations exceed the fixed %zu-value "
+                         "scratch; split the batch",
+                         m, w->cols, n, kNoAllocMaxActs);
+    uint16_t *xbf = nullptr;
+    int rc = noalloc_scratch(&xbf);
+    if (rc) return rc;
+    int dev = 0, sms = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    Q35CU_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    size_t blocks = (n + 255) / 256;
+    if (blocks > (size_t)sms * 16) blocks = (size_t)sms * 16;
+    round_bf16_noalloc<<<(unsigned)blocks, 256, 0, st>>>(X, xbf, n);
+    count_launch();
+    Q35CU_CUDA(cudaGetLastError());
+    return launch_gemm_fp8(w, xbf, m, Y, st);
+}
+
 int gemm_status(uint32_t *status, bool clear)
 {
     Q35CU_CUDA(cudaMemcpyFromSymbol(status, g_gemm_status, 4));
@@ -431,3 +504,12 @@ int gemm_status(uint32_t *status, bool clear)
 }
 
 }  // namespace q35cu
+
+// The allocation-free prefill entry point (see gemm_fp8_f32_noalloc above).
+// `stream` NULL means the legacy default stream.
+extern "C" __attribute__((visibility("default"))) int q35cu_gemm_fp8_f32_noalloc(const q35cu_weight *w,
+                                                                               const float *X, uint32_t m,
+                                                                               float *Y, void *stream)
+{
+    return q35cu::gemm_fp8_f32_noalloc(w, X, m, Y, static_cast<cudaStream_t>(stream));
+}

@@ -75,6 +75,7 @@ _SIGS = [
     ("q35cu_gemv_fp8", C.c_int, [_vp, _vp, _u32, _u32, _vp, _u32, _vp]),
     ("q35cu_multi_fp8", C.c_int, [C.POINTER(_vp), _vp, _u32, _u32, C.POINTER(_vp), _vp]),
     ("q35cu_gemm_fp8", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
+    ("q35cu_gemm_fp8_f32_noalloc", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
     ("q35cu_f32_to_bf16", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_swiglu", C.c_int, [_vp, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemv_bf16", C.c_int, [_vp, _vp, _vp, _vp]),

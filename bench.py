@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the C0/C1 sweep, e2e and CPU baseline")
     ap.add_argument("--profile-c0", action="store_true",
                     help="only the isolated configuration-0 GEMV (a small command for ncu captures)")
+    ap.add_argument("--profile-c2", action="store_true",
+                    help="only the configuration-2 gate projection at M=2048 through the GEMM (for ncu captures)")
     return ap.parse_args()
 
 
@@ -612,10 +614,32 @@ def run_profile_c0(args):
     return 0
 
 
+def run_profile_c2(args):
+    import torch
+
+    import q35cu
+
+    torch.cuda.set_device(0)
+    q35cu.check(q35cu.load().q35cu_set_device(0))
+    w = q35cu.Weight.synth_fp8(9007, 17408, 5120)
+    try:
+        X = torch.randn((2048, 5120), device="cuda").to(torch.bfloat16)
+        Y = torch.empty((2048, 17408), device="cuda")
+        for _ in range(max(1, args.steps)):
+            q35cu.gemm(w, X.view(torch.int16), Y)
+        torch.cuda.synchronize()
+    finally:
+        w.free()
+    print(json.dumps({"config2_gate_gemm": "ok", "launches": max(1, args.steps)}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.profile_c0:
         return run_profile_c0(args)
+    if args.profile_c2:
+        return run_profile_c2(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -533,13 +533,15 @@ def run_ours(args):
     # live roofline of the dominant kernel (the decode GEMV), this rank
     ach, bytes_per_launch, s_per_launch, nl, breakdown = kernel_roofline(q35cu, torch, st, hbm_peak)
     ach = max_over_ranks(-ach) * -1 if world > 1 else ach  # slowest rank
+    # DRAM bytes (read + write) per algorithmic byte of the decode GEMV from the
+    # committed ncu capture (profiles/gemv_fp8_c0.md), scaled to this step's mean launch
     traffic = None
-    tp = os.path.join(REPO, "profiles", "traffic.json")
+    tp = os.path.join(REPO, "profiles", "gemv_fp8_c0.md")
     if os.path.exists(tp):
         with open(tp) as f:
-            tj = json.load(f)
-        if "gemv_c3_bytes_per_algorithmic_byte" in tj:
-            traffic = round(tj["gemv_c3_bytes_per_algorithmic_byte"] * bytes_per_launch)
+            for line in f:
+                if line.startswith("| traffic / algorithmic bytes |"):
+                    traffic = round(float(line.split("|")[2].split()[0]) * bytes_per_launch)
 
     extras = {}
     if rank == 0 and world == 1 and not args.no_extras:

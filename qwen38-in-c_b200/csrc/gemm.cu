@@ -12,14 +12,14 @@
 //               [128 rows x 128 B] and the bf16 activation tile [128 tokens x
 //               128 cols] (two 64-column boxes), both 128B-swizzled, into a
 //               3-stage ring (mbarrier complete_tx);
-//   warps 2-5   converters: thread r turns row r of the fp8 tile into bf16 --
+//   warps 2-9   converters: two threads per row turn the fp8 tile into bf16 --
 //               exact (e4m3 -> f16 -> f32 -> bf16 loses nothing) -- written in
 //               the canonical K-major 128B-swizzle layout the MMA reads
 //               (two 64-column atoms), double-buffered, then a proxy fence;
 //   warp 1      one elected thread issues tcgen05.mma kind::f16 (A = the
 //               bf16 weight tile, M = 128; B = the activation tile, N = 128;
 //               8 steps of K = 16) into a fresh TMEM partial P[kb % 2];
-//   warps 6-9   epilogue: each thread owns one weight row (a TMEM lane) and
+//   warps 10-13 epilogue: each thread owns one weight row (a TMEM lane) and
 //               promotes  ACC += s[n/128, kb] * P  for its 128 token columns
 //               (ACC also in TMEM), then stores Y from the last block.
 // TMEM: P0 | P1 | ACC = 384 of 512 columns.  The per-128-K promotion keeps
@@ -50,7 +50,8 @@ constexpr uint32_t kWTile = kBM * kBK;      // 16 KB fp8
 constexpr uint32_t kATile = kBM * kBK * 2;  // 32 KB bf16
 constexpr uint32_t kAtom = 128 * 128;       // one 64-column swizzle atom of 128 rows
 constexpr uint32_t kSpin = 1u << 22;
-constexpr int kThreads = 320;
+constexpr int kConvWarps = 8;   // fp8 -> bf16 converters (two threads per weight row)
+constexpr int kThreads = (2 + kConvWarps + 4) * 32;
 
 struct GemmArgs {
     const float *S;  // scales [ceil(N/128), kblocks]
@@ -197,10 +198,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (t == 32) {
         for (int i = 0; i < kStages; ++i) {
             bar_init(&full[i], 1);
-            bar_init(&empty[i], 4 + 1);
+            bar_init(&empty[i], kConvWarps + 1);
         }
         for (int i = 0; i < 2; ++i) {
-            bar_init(&a_full[i], 4);
+            bar_init(&a_full[i], kConvWarps);
             bar_init(&a_empty[i], 1);
             bar_init(&p_full[i], 1);
             bar_init(&p_empty[i], 4);
@@ -253,9 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the last partial must have landed before the CTA can free TMEM
             if (ok && nkb) bar_wait(&p_full[(nkb - 1) % 2], ((nkb - 1) / 2) & 1);
         }
-    } else if (warp < 6) {
+    } else if (warp < 2 + kConvWarps) {
         // ---------------- converters: fp8 -> bf16, swizzled -----------------
-        const uint32_t r = t - 64;  // weight row of the tile
+        const uint32_t r = (t - 64) >> 1;        // weight row of the tile
+        const int c0 = ((t - 64) & 1) * 4;       // this thread's four 16-byte chunks
         bool ok = true;
         for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
             const int s = kb % kStages, j = kb % 2;
@@ -265,7 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint8_t *wrow = sm + Smem::w(s) + r * 128;
             uint8_t *arow = sm + Smem::a(j) + r * 128;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
+            for (int cc = 0; cc < 4; ++cc) {
+                const int c = c0 + cc;
                 const uint4 v = *reinterpret_cast<const uint4 *>(wrow + ((c ^ (r & 7)) << 4));
                 const uint2 b0 = e4m3x4_to_bf16x4(v.x), b1 = e4m3x4_to_bf16x4(v.y);
                 const uint2 b2 = e4m3x4_to_bf16x4(v.z), b3 = e4m3x4_to_bf16x4(v.w);

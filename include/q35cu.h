@@ -117,20 +117,26 @@ int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint32_t ldx
                     float *const Y[4], void *stream);
 /* Tensor-core GEMM for prefill: Y [m, rows] fp32 = Xb [m, cols] bf16 times
  * the dequantised weight, fp32 accumulation with per-128-K block-scale
- * promotion.  Needs cols % 16 == 0. */
+ * promotion.  Needs cols % 16 == 0.  The caller provides a device workspace
+ * of at least q35cu_gemm_fp8_workspace_bytes(m, cols) bytes (16-byte
+ * aligned) for the prepared activations (f16 with a per-token power-of-two
+ * scale, which carries every bf16 value exactly); calls on different streams
+ * need different workspaces.  The library allocates nothing here. */
+size_t q35cu_gemm_fp8_workspace_bytes(uint32_t m, uint32_t cols);
 int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m,
-                   float *Y, void *stream);
+                   float *Y, void *workspace, size_t workspace_bytes, void *stream);
 /* The prefill GEMM of q35cu_gemm_fp8 on fp32 activations, for callers that
- * may not have the library allocate device memory: a serving process that
- * reserved its HBM budget up front, or a loop that cannot absorb the device
- * synchronisation a cudaMalloc / cudaFree can bring.  No counterpart in the
- * reference (its matmuls run on host memory).
+ * may not have the library allocate device memory and hold no workspace: a
+ * serving process that reserved its HBM budget up front, or a loop that
+ * cannot absorb the device synchronisation a cudaMalloc / cudaFree can
+ * bring.  No counterpart in the reference (its matmuls run on host memory).
  *   X [m, cols] fp32 and Y [m, rows] fp32 are device memory owned by the
- *   caller; X is rounded to bf16 (the prefill contract) into a fixed 16 MiB
- *   array compiled into the library -- every GPU that loads the library
- *   holds it until exit -- so m * cols may be at most
- *   Q35CU_NOALLOC_MAX_ACTS; larger calls fail with Q35CU_ERR_ARG.
- *   All calls share that array: calls that overlap on the GPU race.
+ *   caller; X is rounded to bf16 (the prefill contract) and prepared into
+ *   fixed arrays compiled into the library (16 MiB of activations, 2 MiB of
+ *   per-token scales) -- every GPU that loads the library holds them until
+ *   exit -- so m * cols may be at most Q35CU_NOALLOC_MAX_ACTS; larger calls
+ *   fail with Q35CU_ERR_ARG.
+ *   All calls share those arrays: calls that overlap on the GPU race.
  *   The first call on a device looks up the array's address and configures
  *   the kernel; make it before any stream capture.  stream NULL = the
  *   legacy default stream.  Allocates nothing. */

@@ -1,34 +1,56 @@
 // Tensor-core prefill GEMM (M >= 128 tokens), sm_100a: TMA + tcgen05 + TMEM.
 //
 // Replaces the CPU loop of q35_mm_fp8_batch (qwen35-c/src/q35_mm.c:158-172)
-// for prefill-sized batches.  Y[t, n] = sum_k Xb[t, k] * e4m3(W[n, k]) * s[n/128, k/128]
-// with the activations Xb rounded to bf16 (the prefill contract: relative
-// L2 error <= 5e-3 against the reference on the same bf16-valued X).
+// for prefill-sized batches.  Y[t, n] = sum_k xb[t, k] * e4m3(W[n, k]) * s[n/128, k/128]
+// with xb = bf16(X) (the prefill contract: relative L2 error <= 5e-3 against
+// the reference on the same bf16-valued activations).
 //
 // Roofline: tensor cores.  2*M*N*K flops per launch.
 //
-// One CTA computes a 128 (weight rows) x 128 (tokens) tile over all of K:
-//   warp 0      TMA producer: per 128-column block kb, the fp8 weight tile
-//               [128 rows x 128 B] and the bf16 activation tile [128 tokens x
-//               128 cols] (two 64-column boxes), both 128B-swizzled, into a
-//               3-stage ring (mbarrier complete_tx);
-//   warps 2-9   converters: two threads per row turn the fp8 tile into bf16 --
-//               exact (e4m3 -> f16 -> f32 -> bf16 loses nothing) -- written in
-//               the canonical K-major 128B-swizzle layout the MMA reads
-//               (two 64-column atoms), double-buffered, then a proxy fence;
-//   warp 1      one elected thread issues tcgen05.mma kind::f16 (A = the
-//               bf16 weight tile, M = 128; B = the activation tile, N = 128;
-//               8 steps of K = 16) into a fresh TMEM partial P[kb % 2];
-//   warps 10-13 epilogue: each thread owns one weight row (a TMEM lane) and
-//               promotes  ACC += s[n/128, kb] * P  for its 128 token columns
-//               (ACC also in TMEM), then stores Y from the last block.
-// TMEM: P0 | P1 | ACC = 384 of 512 columns.  The per-128-K promotion keeps
-// the block scale out of the MMA operands, so the weight operand stays
-// exact and the scale is applied once per block in fp32.
+// Operands are f16 on the tensor cores (kind::f16, both operands f16):
+//   * every e4m3 value is an f16 value, so a weight tile converts exactly with
+//     one cvt.rn.f16x2.e4m3x2 per two elements (bf16 would need four
+//     instructions per two: e4m3 -> f16 -> f32 -> bf16);
+//   * the activations are prepared once per call (gemm_prep_kernel): each
+//     token row is rounded to bf16 and multiplied by 2^-e_t, the power of two
+//     that puts its largest magnitude in [2^14, 2^15).  bf16 carries 8
+//     significant bits and f16 11, so every element down to 2^-28 of the
+//     row's largest converts exactly.  The epilogue multiplies by 2^e_t.
+//     Scaling by a power of two commutes with every fp32 rounding in the MMA
+//     and in the promotion, so Y equals the bf16 x bf16 computation.
+//
+// Persistent CTAs (one per SM) walk 128 (weight rows) x 128 (tokens) tiles,
+// token tile fastest: the CTAs running together share a few weight row
+// blocks (each read from HBM about once) and the activations (L2-resident).
+//
+// Shared-memory bandwidth is the scarce resource at this tile shape (an
+// M = N = 128 MMA reading both operands from shared memory takes its whole
+// bandwidth), so the converted weight operand never touches shared memory:
+// the converters write it into TMEM and the MMA reads A from TMEM.  Per
+// 128-column block the shared-memory traffic is the TMA fill (48 KB), the
+// converters' fp8 read (16 KB) and the MMA's activation read (32 KB).
+//
+// Roles (480 threads):
+//   warp 0      TMA producer of the activation tile [128 tokens x 128 cols]
+//               f16 (two 64-column boxes, 128B swizzle), 5-stage ring
+//               released by the MMA;
+//   warp 1      one thread issues tcgen05.mma kind::f16 (A = the weight tile
+//               from TMEM, M = 128; B = the activation tile from shared
+//               memory, N = 128; 8 steps of K = 16) into TMEM partial P[g % 2];
+//   warp 2      TMA producer of the fp8 weight tile [128 rows x 128 B],
+//               3-stage ring released by the converters;
+//   warps 3-6   converters: thread = weight row = TMEM lane; converts its
+//               row to f16 and stores it with tcgen05.st into A[g % 4]
+//               (64 TMEM columns, two f16 per column along K);
+//   warps 7-14  epilogue: warp w owns TMEM lanes 32*(w%4).. (one weight row
+//               per thread) and 64 of the 128 token columns; it keeps the
+//               tile's accumulator in registers, ACC += s[n/128, kb] * P per
+//               128-column block (the block scale stays out of the MMA
+//               operands, which stay exact), and stores Y after the last block.
 //
 // Every mbarrier wait is bounded; a wait that gives up records
 // Q35CU_ERR_TIMEOUT in the GEMM's device status word and the CTA winds down
-// (the producer waits, bounded, for its copies in flight; TMEM is freed).
+// (the producers wait, bounded, for their copies in flight; TMEM is freed).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -44,26 +66,35 @@ namespace {
 constexpr int kBM = 128;   // weight rows per tile (MMA M)
 constexpr int kBN = 128;   // tokens per tile (MMA N)
 constexpr int kBK = 128;   // columns per block (one scale block)
-constexpr int kStages = 3;
-constexpr uint32_t kXTile = kBN * kBK * 2;  // 32 KB bf16
+constexpr int kXStages = 5;
+constexpr int kWStages = 3;
+constexpr int kABufs = 4;                   // converted weight tiles in TMEM
+constexpr uint32_t kXTile = kBN * kBK * 2;  // 32 KB f16
 constexpr uint32_t kWTile = kBM * kBK;      // 16 KB fp8
-constexpr uint32_t kATile = kBM * kBK * 2;  // 32 KB bf16
 constexpr uint32_t kAtom = 128 * 128;       // one 64-column swizzle atom of 128 rows
 constexpr uint32_t kSpin = 1u << 22;
-constexpr int kConvWarps = 8;   // fp8 -> bf16 converters (two threads per weight row)
-constexpr int kThreads = (2 + kConvWarps + 4) * 32;
+constexpr int kWarpX = 0, kWarpMma = 1, kWarpW = 2, kWarpConv = 3;
+constexpr int kConvWarps = 4;                       // one thread per weight row
+constexpr int kWarpEpi = kWarpConv + kConvWarps;    // 7
+constexpr int kEpiWarps = 8;                        // 4 lane quadrants x 2 column halves
+constexpr int kThreads = (kWarpEpi + kEpiWarps) * 32;
+// TMEM columns: P0 | P1 (fp32 partials, 128 each) | A0..A3 (64 each: 128 f16 per lane)
+constexpr uint32_t kTmemA = 2 * kBN;
+constexpr uint32_t kACols = kBK / 2;
+constexpr uint32_t kTmemCols = 512;
+static_assert(kTmemA + kABufs * kACols <= kTmemCols, "TMEM budget");
 
 struct GemmArgs {
-    const float *S;  // scales [ceil(N/128), kblocks]
-    float *Y;        // [m, N] token-major
-    uint32_t N, K, m, kblocks;
+    const float *S;       // weight scales [ceil(N/128), kblocks]
+    const float *tscale;  // per token 2^e_t [m]
+    float *Y;             // [m, N] token-major
+    uint32_t N, K, m, kblocks, mtiles, ntiles;
 };
 
 struct Smem {  // offsets from the 1024-aligned base
-    static constexpr uint32_t x(int s) { return s * (kXTile + kWTile); }
-    static constexpr uint32_t w(int s) { return s * (kXTile + kWTile) + kXTile; }
-    static constexpr uint32_t a(int j) { return kStages * (kXTile + kWTile) + j * kATile; }
-    static constexpr uint32_t bars = kStages * (kXTile + kWTile) + 2 * kATile;
+    static constexpr uint32_t x(int s) { return s * kXTile; }
+    static constexpr uint32_t w(int s) { return kXStages * kXTile + s * kWTile; }
+    static constexpr uint32_t bars = kXStages * kXTile + kWStages * kWTile;
     static constexpr uint32_t total = bars + 256;
 };
 
@@ -73,9 +104,17 @@ __device__ __forceinline__ void bar_init(uint64_t *b, uint32_t n)
 {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(b)), "r"(n));
 }
-__device__ __forceinline__ void bar_expect(uint64_t *b, uint32_t bytes)
+// The producer and MMA roles run with their whole warp converged (so the
+// tensor-map, descriptor and TMEM operands are warp-uniform values the
+// compiler keeps in uniform registers); the single-thread instructions are
+// predicated on `leader` inside the asm rather than branched around.
+__device__ __forceinline__ void bar_expect(uint64_t *b, uint32_t bytes, uint32_t leader)
 {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(b)), "r"(bytes) : "memory");
+    asm volatile(
+        "{\n\t.reg .pred e;\n\tsetp.ne.b32 e, %2, 0;\n\t"
+        "@e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(sa(b)),
+        "r"(bytes), "r"(leader)
+        : "memory");
 }
 __device__ __forceinline__ void bar_arrive(uint64_t *b)
 {
@@ -96,12 +135,22 @@ __device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity)
     return false;
 }
 
-__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar)
+__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar,
+                                       uint32_t leader)
 {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(sa(dst)), "l"(map), "r"(c0), "r"(c1), "r"(sa(bar))
+        "{\n\t.reg .pred e;\n\tsetp.ne.b32 e, %5, 0;\n\t"
+        "@e cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        "\n\t}" ::"r"(sa(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(sa(bar)), "r"(leader)
         : "memory");
+}
+
+// wait (bounded) until the last min(issued, stages) copies of a ring have landed
+__device__ __forceinline__ void drain(uint64_t *full, int stages, uint32_t issued)
+{
+    for (uint32_t i = issued > (uint32_t)stages ? issued - stages : 0; i < issued; ++i)
+        bar_wait(&full[i % stages], (i / stages) & 1);
 }
 
 // UMMA shared-memory descriptor: K-major, 128B swizzle, 8-row core groups 1024 B apart
@@ -116,22 +165,27 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
     return d;
 }
 
-// kind::f16 instruction descriptor: D f32, A bf16, B bf16, both K-major, M = 128, N = 128
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
+// kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B f16 (bits
+// 7-9 and 10-12 = 0), both K-major, N = 128 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16)
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc)
+// D[tmem] (+)= A[tmem] * B[smem descriptor], issued by the leader lane
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t acc,
+                                           uint32_t leader)
 {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+        "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 e, %5, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(kIdesc), "r"(acc), "r"(leader)
         : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint64_t *bar)
+__device__ __forceinline__ void mma_commit(uint64_t *bar, uint32_t leader)
 {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(bar))
-                 : "memory");
+    asm volatile(
+        "{\n\t.reg .pred e;\n\tsetp.ne.b32 e, %1, 0;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(sa(bar)),
+        "r"(leader)
+        : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
@@ -145,6 +199,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
 {
     asm volatile(
@@ -157,20 +212,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
-// four e4m3 bytes -> four bf16, exact (e4m3 -> f16 -> f32 -> bf16 only widens)
-__device__ __forceinline__ uint2 e4m3x4_to_bf16x4(uint32_t w)
+// four e4m3 bytes (byte 0 first) -> two f16x2 words, exact
+__device__ __forceinline__ void e4m3x4_to_f16x4(uint32_t w, uint32_t &lo, uint32_t &hi)
 {
-    uint32_t h01, h23;
     asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
         "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
-        : "=r"(h01), "=r"(h23)
+        : "=r"(lo), "=r"(hi)
         : "r"(w));
-    const float2 f01 = __half22float2(*reinterpret_cast<__half2 *>(&h01));
-    const float2 f23 = __half22float2(*reinterpret_cast<__half2 *>(&h23));
-    uint2 r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r.x) : "f"(f01.y), "f"(f01.x));
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r.y) : "f"(f23.y), "f"(f23.x));
-    return r;
+}
+
+// ACC[i] (+)= s * P[i] for 32 columns; the first block starts the accumulator
+__device__ __forceinline__ void promote32(float *acc, const uint32_t (&p)[32], float s, bool first)
+{
+    if (first) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = s * __uint_as_float(p[i]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = fmaf(s, __uint_as_float(p[i]), acc[i]);
+    }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -179,32 +239,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + Smem::bars);  // [3] TMA -> converters, MMA
-    uint64_t *empty = full + kStages;                                 // [3] converters + MMA -> TMA
-    uint64_t *a_full = empty + kStages;                               // [2] converters -> MMA
-    uint64_t *a_empty = a_full + 2;                                   // [2] MMA -> converters
-    uint64_t *p_full = a_empty + 2;                                   // [2] MMA -> epilogue
-    uint64_t *p_empty = p_full + 2;                                   // [2] epilogue -> MMA
+    uint64_t *x_full = reinterpret_cast<uint64_t *>(sm + Smem::bars);  // [3] TMA -> MMA
+    uint64_t *x_empty = x_full + kXStages;                              // [3] MMA -> TMA
+    uint64_t *w_full = x_empty + kXStages;                              // [3] TMA -> converters
+    uint64_t *w_empty = w_full + kWStages;                              // [3] converters -> TMA
+    uint64_t *a_full = w_empty + kWStages;                              // [4] converters -> MMA
+    uint64_t *a_empty = a_full + kABufs;                                // [4] MMA -> converters
+    uint64_t *p_full = a_empty + kABufs;                                // [2] MMA -> epilogue
+    uint64_t *p_empty = p_full + 2;                                     // [2] epilogue -> MMA
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(p_empty + 2);
 
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const uint32_t n0 = blockIdx.x * kBM, m0 = blockIdx.y * kBN;
     const uint32_t nkb = a.kblocks;
 
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(sa(tmem_slot)));
+    if (warp == kWarpX) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(tmem_slot)),
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (t == 32) {
-        for (int i = 0; i < kStages; ++i) {
-            bar_init(&full[i], 1);
-            bar_init(&empty[i], kConvWarps + 1);
+        for (int i = 0; i < kXStages; ++i) {
+            bar_init(&x_full[i], 1);
+            bar_init(&x_empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kWStages; ++i) {
+            bar_init(&w_full[i], 1);
+            bar_init(&w_empty[i], kConvWarps);
+        }
+        for (int i = 0; i < kABufs; ++i) {
             bar_init(&a_full[i], kConvWarps);
             bar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             bar_init(&p_full[i], 1);
-            bar_init(&p_empty[i], 4);
+            bar_init(&p_empty[i], kEpiWarps);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -213,135 +281,214 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        // ---------------- TMA producer -------------------------------------
-        if (lane == 0) {
-            uint32_t issued = 0;
-            bool ok = true;
-            for (uint32_t kb = 0; kb < nkb && ok; ++kb, ++issued) {
-                const int s = kb % kStages;
-                if (kb >= kStages) ok = bar_wait(&empty[s], ((kb / kStages) - 1) & 1);
+    const uint32_t leader = lane == 0;
+    if (warp == kWarpX) {
+        // ---------------- activation producer (whole warp) -----------------
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+            const int m0 = (int)((tile % a.mtiles) * kBN);
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                const int s = g % kXStages;
+                if (g >= (uint32_t)kXStages) ok = __all_sync(0xffffffffu, bar_wait(&x_empty[s], ((g / kXStages) - 1) & 1));
                 if (!ok) break;
-                bar_expect(&full[s], kXTile + kWTile);
-                tma_2d(sm + Smem::x(s), &map_x, (int)(kb * kBK), (int)m0, &full[s]);
-                tma_2d(sm + Smem::x(s) + kAtom, &map_x, (int)(kb * kBK + 64), (int)m0, &full[s]);
-                tma_2d(sm + Smem::w(s), &map_w, (int)(kb * kBK), (int)n0, &full[s]);
+                bar_expect(&x_full[s], kXTile, leader);
+                tma_2d(sm + Smem::x(s), &map_x, (int)(kb * kBK), m0, &x_full[s], leader);
+                tma_2d(sm + Smem::x(s) + kAtom, &map_x, (int)(kb * kBK + 64), m0, &x_full[s], leader);
             }
-            for (uint32_t i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
-                bar_wait(&full[i % kStages], (i / kStages) & 1);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ---------------------------------------
-        if (lane == 0) {
-            bool ok = true;
-            for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
-                const int s = kb % kStages, j = kb % 2;
-                ok = bar_wait(&full[s], (kb / kStages) & 1) && bar_wait(&a_full[j], (kb / 2) & 1);
-                if (ok && kb >= 2) ok = bar_wait(&p_empty[j], ((kb / 2) - 1) & 1);
+        drain(x_full, kXStages, g);
+    } else if (warp == kWarpW) {
+        // ---------------- weight producer (whole warp) ---------------------
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+            const int n0 = (int)((tile / a.mtiles) * kBM);
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                const int s = g % kWStages;
+                if (g >= (uint32_t)kWStages) ok = __all_sync(0xffffffffu, bar_wait(&w_empty[s], ((g / kWStages) - 1) & 1));
+                if (!ok) break;
+                bar_expect(&w_full[s], kWTile, leader);
+                tma_2d(sm + Smem::w(s), &map_w, (int)(kb * kBK), n0, &w_full[s], leader);
+            }
+        }
+        drain(w_full, kWStages, g);
+    } else if (warp == kWarpMma) {
+        // ---------------- MMA issuer (whole warp, lane 0 issues) ------------
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                const int s = g % kXStages, ja = g % kABufs, j = g & 1;
+                bool w = bar_wait(&x_full[s], (g / kXStages) & 1) && bar_wait(&a_full[ja], (g / kABufs) & 1);
+                if (w && g >= 2) w = bar_wait(&p_empty[j], ((g >> 1) - 1) & 1);
+                ok = __all_sync(0xffffffffu, w);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t abase = sa(sm + Smem::a(j)), xbase = sa(sm + Smem::x(s));
-                const uint32_t d = tmem + j * kBN;
+                const uint32_t xbase = sa(sm + Smem::x(s));
+                const uint32_t d = tmem + j * kBN, acol = tmem + kTmemA + ja * kACols;
 #pragma unroll
                 for (int ks = 0; ks < kBK / 16; ++ks) {
                     const uint32_t off = (ks >> 2) * kAtom + (ks & 3) * 32;
-                    mma_bf16(d, sw128_desc(abase + off), sw128_desc(xbase + off), ks > 0);
+                    mma_f16_ts(d, acol + ks * 8, sw128_desc(xbase + off), ks > 0, leader);
                 }
-                mma_commit(&p_full[j]);
-                mma_commit(&empty[s]);
-                mma_commit(&a_empty[j]);
+                mma_commit(&p_full[j], leader);
+                mma_commit(&x_empty[s], leader);
+                mma_commit(&a_empty[ja], leader);
             }
-            // the last partial must have landed before the CTA can free TMEM
-            if (ok && nkb) bar_wait(&p_full[(nkb - 1) % 2], ((nkb - 1) / 2) & 1);
         }
-    } else if (warp < 2 + kConvWarps) {
-        // ---------------- converters: fp8 -> bf16, swizzled -----------------
-        const uint32_t r = (t - 64) >> 1;        // weight row of the tile
-        const int c0 = ((t - 64) & 1) * 4;       // this thread's four 16-byte chunks
+        // the last partial must have landed before the CTA can free TMEM
+        if (ok && g) bar_wait(&p_full[(g - 1) & 1], ((g - 1) >> 1) & 1);
+    } else if (warp < kWarpEpi) {
+        // ---------------- converters: fp8 -> f16 into TMEM -------------------
+        // Thread = weight row = TMEM lane (warp w may access lanes 32*(w%4)..).
+        // The 8 lanes of one shared-memory phase (16-byte loads) hold 8
+        // consecutive rows, so the swizzled chunk positions (c ^ (r & 7))
+        // differ: no bank conflicts.  Column i of A holds K elements 2i, 2i+1.
+        const uint32_t quad = warp & 3;
+        const uint32_t r = quad * 32 + lane;
+        const uint32_t sw = r & 7;
+        const uint32_t lane_base = tmem + ((quad * 32) << 16) + kTmemA;
+        uint32_t g = 0;
         bool ok = true;
-        for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
-            const int s = kb % kStages, j = kb % 2;
-            ok = bar_wait(&full[s], (kb / kStages) & 1);
-            if (ok && kb >= 2) ok = bar_wait(&a_empty[j], ((kb / 2) - 1) & 1);
-            if (!ok) break;
-            const uint8_t *wrow = sm + Smem::w(s) + r * 128;
-            uint8_t *arow = sm + Smem::a(j) + r * 128;
+        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                const int s = g % kWStages, ja = g % kABufs;
+                ok = bar_wait(&w_full[s], (g / kWStages) & 1);
+                if (ok && g >= (uint32_t)kABufs) ok = bar_wait(&a_empty[ja], ((g / kABufs) - 1) & 1);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint8_t *wrow = sm + Smem::w(s) + r * 128;
+                uint4 v[8];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const int c = c0 + cc;
-                const uint4 v = *reinterpret_cast<const uint4 *>(wrow + ((c ^ (r & 7)) << 4));
-                const uint2 b0 = e4m3x4_to_bf16x4(v.x), b1 = e4m3x4_to_bf16x4(v.y);
-                const uint2 b2 = e4m3x4_to_bf16x4(v.z), b3 = e4m3x4_to_bf16x4(v.w);
-                // bf16 chunks 2c and 2c+1 of the 16 in this row: atom (2c)/8, chunk (2c)%8
-                const uint32_t q0 = 2 * c, q1 = 2 * c + 1;
-                *reinterpret_cast<uint4 *>(arow + (q0 >> 3) * kAtom + (((q0 & 7) ^ (r & 7)) << 4)) =
-                    make_uint4(b0.x, b0.y, b1.x, b1.y);
-                *reinterpret_cast<uint4 *>(arow + (q1 >> 3) * kAtom + (((q1 & 7) ^ (r & 7)) << 4)) =
-                    make_uint4(b2.x, b2.y, b3.x, b3.y);
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                bar_arrive(&a_full[j]);
-                bar_arrive(&empty[s]);
+                for (uint32_t c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4 *>(wrow + ((c ^ sw) << 4));
+                __syncwarp();
+                if (lane == 0) bar_arrive(&w_empty[s]);  // the fp8 tile is in registers
+#pragma unroll
+                for (int hlf = 0; hlf < 2; ++hlf) {
+                    uint32_t h[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 q = v[hlf * 4 + c];
+                        e4m3x4_to_f16x4(q.x, h[8 * c + 0], h[8 * c + 1]);
+                        e4m3x4_to_f16x4(q.y, h[8 * c + 2], h[8 * c + 3]);
+                        e4m3x4_to_f16x4(q.z, h[8 * c + 4], h[8 * c + 5]);
+                        e4m3x4_to_f16x4(q.w, h[8 * c + 6], h[8 * c + 7]);
+                    }
+                    tmem_st32(lane_base + ja * kACols + hlf * 32, h);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(&a_full[ja]);
             }
         }
     } else {
         // ---------------- epilogue: promotion and store -----------------------
-        const uint32_t quad = warp & 3;                 // TMEM lanes this warp may touch
-        const uint32_t row = quad * 32 + lane;          // weight row of the tile
-        const uint32_t n = n0 + row;
-        const uint32_t sb = (n0 / 128 < (a.N + 127) / 128) ? n0 / 128 : 0;
-        const float *srow = a.S + (size_t)sb * nkb;
-        const uint32_t lane_base = tmem + ((quad * 32) << 16);
+        const uint32_t quad = warp & 3;                         // TMEM lanes this warp may touch
+        const uint32_t half = (warp - kWarpEpi) >> 2;           // token columns 64*half ..
+        const uint32_t tbase = tmem + ((quad * 32) << 16) + half * 64;
+        uint32_t g = 0;
         bool ok = true;
-        for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
-            const int j = kb % 2;
-            ok = bar_wait(&p_full[j], (kb / 2) & 1);
-            if (!ok) break;
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const float sc = __ldg(srow + kb);
-            const bool last = kb + 1 == nkb;
-#pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t p[32], q[32];
-                tmem_ld32(lane_base + j * kBN + c * 32, p);
-                if (kb) tmem_ld32(lane_base + 2 * kBN + c * 32, q);
+        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+            const uint32_t rb = tile / a.mtiles;
+            const uint32_t n = rb * kBM + quad * 32 + lane;               // weight row
+            const uint32_t t0 = (tile % a.mtiles) * kBN + half * 64;      // first token
+            const float *srow = a.S + (size_t)rb * nkb;
+            float acc[64];
+            float sc = __ldg(srow);
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                const int j = g & 1;
+                const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
+                ok = bar_wait(&p_full[j], (g >> 1) & 1);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                uint32_t p[32];
+                tmem_ld32(tbase + j * kBN, p);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                promote32(acc, p, sc, kb == 0);
+                tmem_ld32(tbase + j * kBN + 32, p);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                promote32(acc + 32, p, sc, kb == 0);
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(&p_empty[j]);
+                sc = sc_next;
+            }
+            if (ok && n < a.N) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float acc = kb ? fmaf(sc, __uint_as_float(p[i]), __uint_as_float(q[i]))
-                                         : sc * __uint_as_float(p[i]);
-                    q[i] = __float_as_uint(acc);
-                }
-                if (!last) {
-                    tmem_st32(lane_base + 2 * kBN + c * 32, q);
-                } else if (n < a.N) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const uint32_t mm = m0 + c * 32 + i;
-                        if (mm < a.m) a.Y[(size_t)mm * a.N + n] = __uint_as_float(q[i]);
-                    }
+                for (int i = 0; i < 64; ++i) {
+                    const uint32_t tok = t0 + i;
+                    if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
                 }
             }
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) bar_arrive(&p_empty[j]);
         }
     }
 
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    if (warp == kWarpX)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
-// bf16 rounding of fp32 activations (nearest even)
-__global__ void f32_to_bf16_rows(const float *x, uint16_t *y, size_t n)
+// ---------------------------------------------------------------------------
+// Activation preparation: one CTA per token row.  xb = bf16(x) (nearest
+// even); e = floor(log2(max |xb|)) - 14, so max |xb| * 2^-e lies in
+// [2^14, 2^15) below the f16 limit 65504; Xh = f16(xb * 2^-e), exact for
+// every |xb| >= 2^(e-14); tscale = 2^e.  A row of zeros takes e = 0; a row
+// whose largest magnitude is infinite or NaN takes e = 0 (the NaN or
+// infinity reaches Y as it would in fp32).  e is kept >= -112 so both 2^e
+// and 2^-e are normal floats.
+// ---------------------------------------------------------------------------
+constexpr int kPrepThreads = 256;
+
+template <bool F32>
+__device__ __forceinline__ float4 prep_load(const void *x, size_t i4)
 {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        y[i] = __bfloat16_as_ushort(__float2bfloat16_rn(x[i]));
+    if (F32) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i4);
+        return make_float4(__bfloat162float(__float2bfloat16_rn(v.x)), __bfloat162float(__float2bfloat16_rn(v.y)),
+                           __bfloat162float(__float2bfloat16_rn(v.z)), __bfloat162float(__float2bfloat16_rn(v.w)));
+    }
+    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(x) + i4);
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u), __uint_as_float(v.y << 16),
+                       __uint_as_float(v.y & 0xFFFF0000u));
+}
+
+template <bool F32>
+__global__ void __launch_bounds__(kPrepThreads) gemm_prep_kernel(const void *X, uint32_t K, uint16_t *Xh,
+                                                                 float *tscale)
+{
+    __shared__ float red[kPrepThreads / 32];
+    const size_t row = blockIdx.x;
+    const uint32_t k4 = K / 4;  // K % 16 == 0
+    const size_t base4 = row * k4;
+    float mx = 0.f;
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = prep_load<F32>(X, base4 + i);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < kPrepThreads / 32; ++i) mx = fmaxf(mx, red[i]);
+    const int eb = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+    int e = 0;
+    if (eb == 0 && mx > 0.f) e = -112;         // subnormal maximum
+    else if (eb > 0 && eb < 255) e = max(eb - 127 - 14, -112);
+    const float down = __uint_as_float((uint32_t)(127 - e) << 23);
+    uint2 *out = reinterpret_cast<uint2 *>(Xh) + base4;
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = prep_load<F32>(X, base4 + i);
+        const __half2 h01 = __floats2half2_rn(v.x * down, v.y * down);
+        const __half2 h23 = __floats2half2_rn(v.z * down, v.w * down);
+        out[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
+    }
+    if (threadIdx.x == 0) tscale[row] = __uint_as_float((uint32_t)(127 + e) << 23);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -377,44 +524,66 @@ int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_
     return Q35CU_OK;
 }
 
+// SM count of the current device, looked up once per device
+int sm_count_of(int dev, int *out)
+{
+    static int sms[64] = {};
+    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
+    if (!sms[dev]) Q35CU_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    *out = sms[dev];
+    return Q35CU_OK;
+}
+
 }  // namespace
 
-int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y, cudaStream_t st)
+size_t gemm_workspace_bytes(uint32_t m, uint32_t K)
 {
-    const uint32_t N = w->rows, K = w->cols;
+    return (((size_t)m * K * 2 + 255) & ~(size_t)255) + (size_t)m * 4;
+}
+
+int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *Xh, float *tscale,
+                     cudaStream_t st)
+{
+    if (!m) return Q35CU_OK;
     if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
-    if (((uintptr_t)Xb % 16) || ((uintptr_t)w->d_w % 16)) return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned operand");
-    if ((N + kBM - 1) / kBM > 0x7FFFFFFFu || (m + kBN - 1) / kBN > 65535u)
-        return set_error(Q35CU_ERR_ARG, "gemm_fp8: shape too large");
-    CUtensorMap mx, mw;
-    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, Xb, K, m, (uint64_t)K * 2, 64, kBN);
-    if (rc) return rc;
-    rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
-    if (rc) return rc;
-    GemmArgs a{w->d_s, Y, N, K, m, (K + kBK - 1) / kBK};
-    static bool configured[64] = {};
-    int dev = 0;
-    Q35CU_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
-    const size_t smem = Smem::total + 1024;
-    if (!configured[dev]) {
-        Q35CU_CUDA(cudaFuncSetAttribute(gemm_fp8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        configured[dev] = true;
-    }
-    const dim3 grid((N + kBM - 1) / kBM, (m + kBN - 1) / kBN);
-    gemm_fp8_tc_kernel<<<grid, kThreads, smem, st>>>(mx, mw, a);
+    if ((uintptr_t)X % 16 || (uintptr_t)Xh % 16 || (uintptr_t)tscale % 4)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned activations or workspace");
+    if (f32)
+        gemm_prep_kernel<true><<<m, kPrepThreads, 0, st>>>(X, K, Xh, tscale);
+    else
+        gemm_prep_kernel<false><<<m, kPrepThreads, 0, st>>>(X, K, Xh, tscale);
     count_launch();
     Q35CU_CUDA(cudaGetLastError());
     return Q35CU_OK;
 }
 
-int launch_round_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st)
+int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
+                    cudaStream_t st)
 {
-    if (!n) return Q35CU_OK;
-    size_t blocks = (n + 255) / 256;
-    const size_t cap = (size_t)device_sms() * 16;
-    if (blocks > cap) blocks = cap;
-    f32_to_bf16_rows<<<(unsigned)blocks, 256, 0, st>>>(x, y, n);
+    const uint32_t N = w->rows, K = w->cols;
+    if (!m) return Q35CU_OK;
+    if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
+    if (((uintptr_t)Xh % 16) || ((uintptr_t)w->d_w % 16)) return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned operand");
+    const uint64_t mtiles = (m + kBN - 1) / kBN, ntiles = mtiles * ((N + kBM - 1) / kBM);
+    if (ntiles > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: shape too large");
+    CUtensorMap mx, mw;
+    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xh, K, m, (uint64_t)K * 2, 64, kBN);
+    if (rc) return rc;
+    rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
+    if (rc) return rc;
+    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles};
+    static bool configured[64] = {};
+    int dev = 0, sms = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    rc = sm_count_of(dev, &sms);
+    if (rc) return rc;
+    const size_t smem = Smem::total + 1024;
+    if (!configured[dev]) {
+        Q35CU_CUDA(cudaFuncSetAttribute(gemm_fp8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured[dev] = true;
+    }
+    const uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
+    gemm_fp8_tc_kernel<<<grid, kThreads, smem, st>>>(mx, mw, a);
     count_launch();
     Q35CU_CUDA(cudaGetLastError());
     return Q35CU_OK;
@@ -423,50 +592,51 @@ int launch_round_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st)
 // ---------------------------------------------------------------------------
 // Prefill GEMM for callers that must not allocate device memory.
 //
-// q35cu_gemm_fp8 takes bf16 activations; a caller holding fp32 activations
-// needs a bf16 copy first, and the host entry point q35_mm_fp8_batch keeps
-// that copy in a buffer it allocates.  Some callers cannot let the library
-// call cudaMalloc at that point: a serving process that reserved its whole
+// q35cu_gemm_fp8 takes a caller-provided workspace for the prepared (f16,
+// per-token scaled) copy of the activations, and the host entry point
+// q35_mm_fp8_batch keeps that copy in a buffer it allocates.  Some callers
+// can do neither at that point: a serving process that reserved its whole
 // HBM budget up front, or a decode/prefill loop that cannot afford the
 // device-wide synchronisation a cudaMalloc/cudaFree may imply.  For them the
-// bf16 copy lives in a fixed array compiled into this file instead.
+// prepared copy lives in fixed arrays compiled into this file instead.
 //
-//   * the array holds kNoAllocMaxActs bf16 values (16 MiB); every GPU that
-//     loads the library keeps it until the process exits;
+//   * the arrays hold kNoAllocMaxActs f16 values (16 MiB) and one scale per
+//     token (2 MiB: cols is a multiple of 16, so m <= kNoAllocMaxActs / 16);
+//     every GPU that loads the library keeps them until the process exits;
 //   * a call with m * cols > kNoAllocMaxActs is rejected with Q35CU_ERR_ARG;
-//   * every call reuses the same array: two calls whose work overlaps on the
-//     GPU (different streams, no ordering) race on it;
-//   * each call overwrites exactly the m * cols values it reads, so nothing
-//     needs clearing between calls;
-//   * the first call on a device looks up the array's device address
+//   * every call reuses the same arrays: two calls whose work overlaps on the
+//     GPU (different streams, no ordering) race on them;
+//   * each call overwrites exactly the m * cols values and m scales it reads,
+//     so nothing needs clearing between calls;
+//   * the first call on a device looks up the arrays' device addresses
 //     (cudaGetSymbolAddress) and sets the GEMM's shared-memory limit; make
 //     that first call before any stream capture.
 // ---------------------------------------------------------------------------
 constexpr size_t kNoAllocMaxActs = (size_t)8 << 20;
 static __device__ __align__(256) uint16_t g_noalloc_acts[kNoAllocMaxActs];
+static __device__ __align__(256) float g_noalloc_tscale[kNoAllocMaxActs / 16];
 
 namespace {
 
-__global__ void round_bf16_noalloc(const float *x, uint16_t *y, size_t n)
+// the arrays' device addresses, looked up once per device with that device current
+int noalloc_scratch(uint16_t **acts, float **tscale)
 {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        y[i] = __bfloat16_as_ushort(__float2bfloat16_rn(x[i]));
-}
-
-// the array's device address, looked up once per device with that device current
-int noalloc_scratch(uint16_t **out)
-{
-    static uint16_t *addr[64] = {};
+    static uint16_t *a_addr[64] = {};
+    static float *s_addr[64] = {};
     int dev = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
-    if (!addr[dev]) {
-        void *p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_acts);
+    if (!a_addr[dev]) {
+        void *p = nullptr, *q = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_acts);
         if (e != cudaSuccess || !p) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_acts)");
-        addr[dev] = static_cast<uint16_t *>(p);
+        e = cudaGetSymbolAddress(&q, g_noalloc_tscale);
+        if (e != cudaSuccess || !q) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_tscale)");
+        s_addr[dev] = static_cast<float *>(q);
+        a_addr[dev] = static_cast<uint16_t *>(p);
     }
-    *out = addr[dev];
+    *acts = a_addr[dev];
+    *tscale = s_addr[dev];
     return Q35CU_OK;
 }
 
@@ -482,18 +652,13 @@ int gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m, floa
                          "gemm_fp8_f32_noalloc: %u tokens x %u cols = %zu activations exceed the fixed %zu-value "
                          "scratch; split the batch",
                          m, w->cols, n, kNoAllocMaxActs);
-    uint16_t *xbf = nullptr;
-    int rc = noalloc_scratch(&xbf);
+    uint16_t *xh = nullptr;
+    float *ts = nullptr;
+    int rc = noalloc_scratch(&xh, &ts);
     if (rc) return rc;
-    int dev = 0, sms = 0;
-    Q35CU_CUDA(cudaGetDevice(&dev));
-    Q35CU_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    size_t blocks = (n + 255) / 256;
-    if (blocks > (size_t)sms * 16) blocks = (size_t)sms * 16;
-    round_bf16_noalloc<<<(unsigned)blocks, 256, 0, st>>>(X, xbf, n);
-    count_launch();
-    Q35CU_CUDA(cudaGetLastError());
-    return launch_gemm_fp8(w, xbf, m, Y, st);
+    rc = launch_gemm_prep(X, true, m, w->cols, xh, ts, st);
+    if (rc) return rc;
+    return launch_gemm_fp8(w, xh, ts, m, Y, st);
 }
 
 int gemm_status(uint32_t *status, bool clear)

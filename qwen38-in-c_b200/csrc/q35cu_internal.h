@@ -57,10 +57,15 @@ void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes);
 int device_status(uint32_t *status, bool clear);
 int scan_nan_codes(const uint8_t *W, size_t bytes, uint32_t *d_flag, cudaStream_t st, bool *has_nan);
 
-int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y,
+// prefill GEMM: activations prepared once per call (f16, per-token power-of-two
+// scale) into a workspace of gemm_workspace_bytes(m, K): Xh [m, K] f16 at
+// offset 0, tscale [m] fp32 after it (256-byte aligned)
+size_t gemm_workspace_bytes(uint32_t m, uint32_t K);
+int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *Xh, float *tscale,
+                     cudaStream_t st);
+int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
                     cudaStream_t st);
 int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
-int launch_round_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
 int gemm_status(uint32_t *status, bool clear);
 int launch_bf16_to_f32_scales(const uint16_t *src, float *dst, size_t n, cudaStream_t st);
 int launch_f32_to_bf16_scales(const float *src, uint16_t *dst, size_t n, cudaStream_t st);

@@ -88,7 +88,7 @@ struct DevState {
     size_t h_cap = 0;
     void *d_stage = nullptr;  // device, in + out
     size_t d_cap = 0;
-    void *d_xbf = nullptr;    // device bf16 copy of a prefill activation batch
+    void *d_xbf = nullptr;    // GEMM workspace: prepared (f16) copy of a prefill activation batch
     size_t xbf_cap = 0;
     uint32_t *d_flag = nullptr;  // 4-byte scratch word for upload scans
 };
@@ -643,11 +643,25 @@ Q35_API int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint
     return launch_gemv(0, segs, n, X, K, ldx, m, pick(stream));
 }
 
-Q35_API int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y, void *stream)
+Q35_API size_t q35cu_gemm_fp8_workspace_bytes(uint32_t m, uint32_t cols)
+{
+    return gemm_workspace_bytes(m, cols);
+}
+
+Q35_API int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m, float *Y, void *workspace,
+                           size_t workspace_bytes, void *stream)
 {
     if (!w || w->kind != 0 || !Xb || !Y) return set_error(Q35CU_ERR_ARG, "gemm_fp8: bad arguments");
     if (!m) return Q35CU_OK;
-    return launch_gemm_fp8(w, Xb, m, Y, pick(stream));
+    const size_t need = gemm_workspace_bytes(m, w->cols);
+    if (!workspace || workspace_bytes < need)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    uint16_t *xh = static_cast<uint16_t *>(workspace);
+    float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + need - (size_t)m * 4);
+    cudaStream_t st = pick(stream);
+    int rc = launch_gemm_prep(Xb, false, m, w->cols, xh, ts, st);
+    if (rc) return rc;
+    return launch_gemm_fp8(w, xh, ts, m, Y, st);
 }
 
 Q35_API int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream)
@@ -805,7 +819,7 @@ Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint
     const bool tc = n >= gemm_min_tokens() && cols % 16 == 0;
     if (!rc && tc) {
         DevState *d = dev_state();
-        const size_t xb = (size_t)n * cols * 2;
+        const size_t xb = gemm_workspace_bytes(n, cols);
         if (xb > d->xbf_cap) {
             if (d->d_xbf) dev_free(d->d_xbf, d->xbf_cap);
             d->d_xbf = nullptr;
@@ -817,10 +831,12 @@ Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint
     if (!rc && tc)
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
             DevState *d = dev_state();
-            uint16_t *xbf = static_cast<uint16_t *>(d->d_xbf);
-            int r = launch_round_bf16(dx, xbf, (size_t)n * cols, st);
+            uint16_t *xh = static_cast<uint16_t *>(d->d_xbf);
+            float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(d->d_xbf) + gemm_workspace_bytes(n, cols) -
+                                                  (size_t)n * 4);
+            int r = launch_gemm_prep(dx, true, n, cols, xh, ts, st);
             if (r) return r;
-            return launch_gemm_fp8(w, xbf, n, dy, st);
+            return launch_gemm_fp8(w, xh, ts, n, dy, st);
         });
     else if (!rc)
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {

@@ -74,7 +74,8 @@ _SIGS = [
     ("q35cu_weight_device_bytes", C.c_size_t, [_vp]),
     ("q35cu_gemv_fp8", C.c_int, [_vp, _vp, _u32, _u32, _vp, _u32, _vp]),
     ("q35cu_multi_fp8", C.c_int, [C.POINTER(_vp), _vp, _u32, _u32, C.POINTER(_vp), _vp]),
-    ("q35cu_gemm_fp8", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
+    ("q35cu_gemm_fp8_workspace_bytes", C.c_size_t, [_u32, _u32]),
+    ("q35cu_gemm_fp8", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8_f32_noalloc", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
     ("q35cu_f32_to_bf16", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_swiglu", C.c_int, [_vp, _vp, _vp, C.c_size_t, _vp]),
@@ -282,10 +283,24 @@ def multi(ws, X, Ys, m: int = 1, stream=None) -> None:
     check(load().q35cu_multi_fp8(wp, _ptr(X), ldx, m, yp, _stream(stream)))
 
 
-def gemm(w: Weight, Xb, Y, stream=None) -> None:
-    """Tensor-core GEMM: Y[m, rows] fp32 = Xb[m, cols] (bf16 bits, any 2-byte dtype) (W.s)^T."""
+def gemm_workspace_bytes(m: int, cols: int) -> int:
+    return int(load().q35cu_gemm_fp8_workspace_bytes(m, cols))
+
+
+def gemm(w: Weight, Xb, Y, workspace=None, stream=None) -> None:
+    """Tensor-core GEMM: Y[m, rows] fp32 = Xb[m, cols] (bf16 bits, any 2-byte dtype) (W.s)^T.
+
+    ``workspace``: a device uint8 tensor of at least gemm_workspace_bytes(m, cols)
+    bytes; allocated per call when omitted."""
     assert Xb.element_size() == 2 and Xb.is_contiguous() and Y.is_contiguous()
-    check(load().q35cu_gemm_fp8(w.h, _ptr(Xb), Xb.shape[0], _ptr(Y), _stream(stream)))
+    m = Xb.shape[0]
+    need = gemm_workspace_bytes(m, w.cols)
+    if workspace is None:
+        import torch
+        workspace = torch.empty(need, dtype=torch.uint8, device=Xb.device)
+    assert workspace.numel() * workspace.element_size() >= need
+    check(load().q35cu_gemm_fp8(w.h, _ptr(Xb), m, _ptr(Y), _ptr(workspace),
+                                workspace.numel() * workspace.element_size(), _stream(stream)))
 
 
 def f32_to_bf16(x, y, stream=None) -> None:

@@ -19,31 +19,36 @@
 //     Scaling by a power of two commutes with every fp32 rounding in the MMA
 //     and in the promotion, so Y equals the bf16 x bf16 computation.
 //
-// Persistent CTAs (one per SM) walk 128 (weight rows) x 128 (tokens) tiles,
+// Persistent CTAs (one per SM) walk 128 (weight rows) x 192 (tokens) tiles,
 // token tile fastest: the CTAs running together share a few weight row
 // blocks (each read from HBM about once) and the activations (L2-resident).
 //
-// Shared-memory bandwidth is the scarce resource at this tile shape (an
-// M = N = 128 MMA reading both operands from shared memory takes its whole
-// bandwidth), so the converted weight operand never touches shared memory:
-// the converters write it into TMEM and the MMA reads A from TMEM.  Per
-// 128-column block the shared-memory traffic is the TMA fill (48 KB), the
-// converters' fp8 read (16 KB) and the MMA's activation read (32 KB).
+// Three measured costs shape the kernel:
+//   * shared-memory bandwidth: an MMA that reads both operands from shared
+//     memory at N = 128 needs all of it, so the converted weight operand
+//     never touches shared memory -- the converters write it into TMEM and
+//     the MMA reads A from TMEM;
+//   * issue: one tcgen05.mma takes ~77 cycles to issue whatever its size,
+//     and an N = 128 MMA is only 64 cycles of tensor work, so the tile is
+//     N = 192 tokens (96 cycles per MMA) -- P0 | P1 | A0 | A1 then fill
+//     the 512 TMEM columns exactly;
+//   * barrier waits: a try_wait costs ~120 cycles even on a completed phase,
+//     so the MMA warp waits on one barrier per 128-column block (the TMA,
+//     the converters and the epilogue all arrive on it) and commits once.
 //
-// Roles (480 threads):
-//   warp 0      TMA producer of the activation tile [128 tokens x 128 cols]
-//               f16 (two 64-column boxes, 128B swizzle), 5-stage ring
-//               released by the MMA;
-//   warp 1      one thread issues tcgen05.mma kind::f16 (A = the weight tile
-//               from TMEM, M = 128; B = the activation tile from shared
-//               memory, N = 128; 8 steps of K = 16) into TMEM partial P[g % 2];
+// Roles (608 threads):
+//   warp 0      TMA producer of the activation tile [192 tokens x 128 cols]
+//               f16 (two 64-column boxes, 128B swizzle), 3 stages;
+//   warp 1      lane 0 issues tcgen05.mma kind::f16 (A = the weight tile from
+//               TMEM, M = 128; B = the activation tile from shared memory,
+//               N = 192; 8 steps of K = 16) into TMEM partial P[g % 2];
 //   warp 2      TMA producer of the fp8 weight tile [128 rows x 128 B],
-//               3-stage ring released by the converters;
+//               4 stages released by the converters;
 //   warps 3-6   converters: thread = weight row = TMEM lane; converts its
-//               row to f16 and stores it with tcgen05.st into A[g % 4]
+//               row to f16 and stores it with tcgen05.st into A[g % 2]
 //               (64 TMEM columns, two f16 per column along K);
-//   warps 7-14  epilogue: warp w owns TMEM lanes 32*(w%4).. (one weight row
-//               per thread) and 64 of the 128 token columns; it keeps the
+//   warps 7-18  epilogue: warp w owns TMEM lanes 32*(w%4).. (one weight row
+//               per thread) and 64 of the 192 token columns; it keeps the
 //               tile's accumulator in registers, ACC += s[n/128, kb] * P per
 //               128-column block (the block scale stays out of the MMA
 //               operands, which stay exact), and stores Y after the last block.
@@ -64,25 +69,29 @@ __device__ uint32_t g_gemm_status;
 namespace {
 
 constexpr int kBM = 128;   // weight rows per tile (MMA M)
-constexpr int kBN = 128;   // tokens per tile (MMA N)
+constexpr int kBN = 192;   // tokens per tile (MMA N)
 constexpr int kBK = 128;   // columns per block (one scale block)
-constexpr int kXStages = 5;
-constexpr int kWStages = 3;
-constexpr int kABufs = 4;                   // converted weight tiles in TMEM
-constexpr uint32_t kXTile = kBN * kBK * 2;  // 32 KB f16
+constexpr int kStages = 3;                  // activation stages (+ TMEM operand + partial slots)
+constexpr int kWStages = 4;                 // fp8 weight stages
+constexpr uint32_t kXTile = kBN * kBK * 2;  // 48 KB f16
 constexpr uint32_t kWTile = kBM * kBK;      // 16 KB fp8
-constexpr uint32_t kAtom = 128 * 128;       // one 64-column swizzle atom of 128 rows
+constexpr uint32_t kXAtom = kBN * 128;      // one 64-column swizzle atom of the activation tile
 constexpr uint32_t kSpin = 1u << 22;
 constexpr int kWarpX = 0, kWarpMma = 1, kWarpW = 2, kWarpConv = 3;
 constexpr int kConvWarps = 4;                       // one thread per weight row
 constexpr int kWarpEpi = kWarpConv + kConvWarps;    // 7
-constexpr int kEpiWarps = 8;                        // 4 lane quadrants x 2 column halves
+constexpr int kEpiGroups = kBN / 64;                // 64 token columns per epilogue warp
+constexpr int kEpiWarps = 4 * kEpiGroups;           // 4 lane quadrants x 3 column groups
 constexpr int kThreads = (kWarpEpi + kEpiWarps) * 32;
-// TMEM columns: P0 | P1 (fp32 partials, 128 each) | A0..A3 (64 each: 128 f16 per lane)
+// TMEM columns: P0 | P1 (fp32 partials, kBN each) | A0 | A1 (64 each: 128 f16 per lane)
 constexpr uint32_t kTmemA = 2 * kBN;
 constexpr uint32_t kACols = kBK / 2;
 constexpr uint32_t kTmemCols = 512;
-static_assert(kTmemA + kABufs * kACols <= kTmemCols, "TMEM budget");
+static_assert(kTmemA + 2 * kACols <= kTmemCols, "TMEM budget");
+// arrivals that complete stage g: the activation producer (with the copy's
+// bytes), the converter warps (A[g % 2] written) and the epilogue warps
+// (P[g % 2] drained of block g - 2)
+constexpr uint32_t kStageArrivals = 1 + kConvWarps + kEpiWarps;
 
 struct GemmArgs {
     const float *S;       // weight scales [ceil(N/128), kblocks]
@@ -93,8 +102,8 @@ struct GemmArgs {
 
 struct Smem {  // offsets from the 1024-aligned base
     static constexpr uint32_t x(int s) { return s * kXTile; }
-    static constexpr uint32_t w(int s) { return kXStages * kXTile + s * kWTile; }
-    static constexpr uint32_t bars = kXStages * kXTile + kWStages * kWTile;
+    static constexpr uint32_t w(int s) { return kStages * kXTile + s * kWTile; }
+    static constexpr uint32_t bars = kStages * kXTile + kWStages * kWTile;
     static constexpr uint32_t total = bars + 256;
 };
 
@@ -188,18 +197,6 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar, uint32_t leader)
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
-{
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
-        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
 {
     asm volatile(
@@ -221,15 +218,24 @@ __device__ __forceinline__ void e4m3x4_to_f16x4(uint32_t w, uint32_t &lo, uint32
         : "r"(w));
 }
 
-// ACC[i] (+)= s * P[i] for 32 columns; the first block starts the accumulator
-__device__ __forceinline__ void promote32(float *acc, const uint32_t (&p)[32], float s, bool first)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// ACC[i] (+)= s * P[i] for 16 columns; the first block starts the accumulator
+__device__ __forceinline__ void promote16(float *acc, const uint32_t (&p)[16], float s, bool first)
 {
     if (first) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = s * __uint_as_float(p[i]);
+        for (int i = 0; i < 16; ++i) acc[i] = s * __uint_as_float(p[i]);
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = fmaf(s, __uint_as_float(p[i]), acc[i]);
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(s, __uint_as_float(p[i]), acc[i]);
     }
 }
 
@@ -239,18 +245,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *x_full = reinterpret_cast<uint64_t *>(sm + Smem::bars);  // [3] TMA -> MMA
-    uint64_t *x_empty = x_full + kXStages;                              // [3] MMA -> TMA
-    uint64_t *w_full = x_empty + kXStages;                              // [3] TMA -> converters
-    uint64_t *w_empty = w_full + kWStages;                              // [3] converters -> TMA
-    uint64_t *a_full = w_empty + kWStages;                              // [4] converters -> MMA
-    uint64_t *a_empty = a_full + kABufs;                                // [4] MMA -> converters
-    uint64_t *p_full = a_empty + kABufs;                                // [2] MMA -> epilogue
-    uint64_t *p_empty = p_full + 2;                                     // [2] epilogue -> MMA
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(p_empty + 2);
+    // stage g uses slot g % kStages of both arrays:
+    //   ready[s]: activation tile landed + A[g % 2] converted + P[g % 2] free -> MMA
+    //   done[s]:  the MMA of block g completed (tcgen05.commit)          -> all
+    uint64_t *ready = reinterpret_cast<uint64_t *>(sm + Smem::bars);
+    uint64_t *done = ready + kStages;
+    uint64_t *w_full = done + kStages;      // [4] TMA -> converters
+    uint64_t *w_empty = w_full + kWStages;  // [4] converters -> TMA
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_empty + kWStages);
 
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const uint32_t nkb = a.kblocks;
+    const uint32_t leader = lane == 0;
 
     if (warp == kWarpX) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(tmem_slot)),
@@ -258,21 +264,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (t == 32) {
-        for (int i = 0; i < kXStages; ++i) {
-            bar_init(&x_full[i], 1);
-            bar_init(&x_empty[i], 1);
+        for (int i = 0; i < kStages; ++i) {
+            bar_init(&ready[i], kStageArrivals);
+            bar_init(&done[i], 1);
         }
         for (int i = 0; i < kWStages; ++i) {
             bar_init(&w_full[i], 1);
             bar_init(&w_empty[i], kConvWarps);
-        }
-        for (int i = 0; i < kABufs; ++i) {
-            bar_init(&a_full[i], kConvWarps);
-            bar_init(&a_empty[i], 1);
-        }
-        for (int i = 0; i < 2; ++i) {
-            bar_init(&p_full[i], 1);
-            bar_init(&p_empty[i], kEpiWarps);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -281,7 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    const uint32_t leader = lane == 0;
+    // Ordering argument for the shared slot rings (kStages >= 3): every
+    // arrival for block g on ready[g % 3] comes after done(g - 2) or
+    // done(g - 3), so the slot has finished its phase for block g - 3; and no
+    // waiter on done(h) can be overtaken by done(h + 3), which needs that
+    // waiter's own later arrival first.
     if (warp == kWarpX) {
         // ---------------- activation producer (whole warp) -----------------
         uint32_t g = 0;
@@ -289,15 +291,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             const int m0 = (int)((tile % a.mtiles) * kBN);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int s = g % kXStages;
-                if (g >= (uint32_t)kXStages) ok = __all_sync(0xffffffffu, bar_wait(&x_empty[s], ((g / kXStages) - 1) & 1));
+                const int s = g % kStages;
+                if (g >= (uint32_t)kStages) ok = __all_sync(0xffffffffu, bar_wait(&done[s], ((g / kStages) - 1) & 1));
                 if (!ok) break;
-                bar_expect(&x_full[s], kXTile, leader);
-                tma_2d(sm + Smem::x(s), &map_x, (int)(kb * kBK), m0, &x_full[s], leader);
-                tma_2d(sm + Smem::x(s) + kAtom, &map_x, (int)(kb * kBK + 64), m0, &x_full[s], leader);
+                bar_expect(&ready[s], kXTile, leader);
+                tma_2d(sm + Smem::x(s), &map_x, (int)(kb * kBK), m0, &ready[s], leader);
+                tma_2d(sm + Smem::x(s) + kXAtom, &map_x, (int)(kb * kBK + 64), m0, &ready[s], leader);
             }
         }
-        drain(x_full, kXStages, g);
+        // wait (bounded) for the copies still in flight
+        for (uint32_t i = g > (uint32_t)kStages ? g - kStages : 0; i < g; ++i)
+            bar_wait(&ready[i % kStages], (i / kStages) & 1);
     } else if (warp == kWarpW) {
         // ---------------- weight producer (whole warp) ---------------------
         uint32_t g = 0;
@@ -319,26 +323,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int s = g % kXStages, ja = g % kABufs, j = g & 1;
-                bool w = bar_wait(&x_full[s], (g / kXStages) & 1) && bar_wait(&a_full[ja], (g / kABufs) & 1);
-                if (w && g >= 2) w = bar_wait(&p_empty[j], ((g >> 1) - 1) & 1);
-                ok = __all_sync(0xffffffffu, w);
+                const int s = g % kStages, j = g & 1;
+                ok = __all_sync(0xffffffffu, bar_wait(&ready[s], (g / kStages) & 1));
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t xbase = sa(sm + Smem::x(s));
-                const uint32_t d = tmem + j * kBN, acol = tmem + kTmemA + ja * kACols;
+                const uint32_t d = tmem + j * kBN, acol = tmem + kTmemA + j * kACols;
 #pragma unroll
                 for (int ks = 0; ks < kBK / 16; ++ks) {
-                    const uint32_t off = (ks >> 2) * kAtom + (ks & 3) * 32;
+                    const uint32_t off = (ks >> 2) * kXAtom + (ks & 3) * 32;
                     mma_f16_ts(d, acol + ks * 8, sw128_desc(xbase + off), ks > 0, leader);
                 }
-                mma_commit(&p_full[j], leader);
-                mma_commit(&x_empty[s], leader);
-                mma_commit(&a_empty[ja], leader);
+                mma_commit(&done[s], leader);
             }
         }
-        // the last partial must have landed before the CTA can free TMEM
-        if (ok && g) bar_wait(&p_full[(g - 1) & 1], ((g - 1) >> 1) & 1);
+        // the last block must have completed before the CTA can free TMEM
+        if (ok && g) bar_wait(&done[(g - 1) % kStages], ((g - 1) / kStages) & 1);
     } else if (warp < kWarpEpi) {
         // ---------------- converters: fp8 -> f16 into TMEM -------------------
         // Thread = weight row = TMEM lane (warp w may access lanes 32*(w%4)..).
@@ -353,9 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int s = g % kWStages, ja = g % kABufs;
+                const int s = g % kWStages, j = g & 1;
                 ok = bar_wait(&w_full[s], (g / kWStages) & 1);
-                if (ok && g >= (uint32_t)kABufs) ok = bar_wait(&a_empty[ja], ((g / kABufs) - 1) & 1);
+                // A[g % 2] was last read by block g - 2
+                if (ok && g >= 2) ok = bar_wait(&done[(g - 2) % kStages], ((g - 2) / kStages) & 1);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint8_t *wrow = sm + Smem::w(s) + r * 128;
@@ -375,44 +376,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                         e4m3x4_to_f16x4(q.z, h[8 * c + 4], h[8 * c + 5]);
                         e4m3x4_to_f16x4(q.w, h[8 * c + 6], h[8 * c + 7]);
                     }
-                    tmem_st32(lane_base + ja * kACols + hlf * 32, h);
+                    tmem_st32(lane_base + j * kACols + hlf * 32, h);
                 }
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) bar_arrive(&a_full[ja]);
+                if (lane == 0) bar_arrive(&ready[g % kStages]);
             }
         }
     } else {
         // ---------------- epilogue: promotion and store -----------------------
         const uint32_t quad = warp & 3;                         // TMEM lanes this warp may touch
-        const uint32_t half = (warp - kWarpEpi) >> 2;           // token columns 64*half ..
-        const uint32_t tbase = tmem + ((quad * 32) << 16) + half * 64;
+        const uint32_t grp = (warp - kWarpEpi) >> 2;            // token columns 64*grp ..
+        const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * 64;
+        // P[0] and P[1] start out free for blocks 0 and 1
+        if (lane == 0) {
+            bar_arrive(&ready[0]);
+            bar_arrive(&ready[1]);
+        }
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             const uint32_t rb = tile / a.mtiles;
             const uint32_t n = rb * kBM + quad * 32 + lane;               // weight row
-            const uint32_t t0 = (tile % a.mtiles) * kBN + half * 64;      // first token
+            const uint32_t t0 = (tile % a.mtiles) * kBN + grp * 64;       // first token
             const float *srow = a.S + (size_t)rb * nkb;
             float acc[64];
             float sc = __ldg(srow);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int j = g & 1;
                 const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
-                ok = bar_wait(&p_full[j], (g >> 1) & 1);
+                ok = bar_wait(&done[g % kStages], (g / kStages) & 1);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                uint32_t p[32];
-                tmem_ld32(tbase + j * kBN, p);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                promote32(acc, p, sc, kb == 0);
-                tmem_ld32(tbase + j * kBN + 32, p);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                promote32(acc + 32, p, sc, kb == 0);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t p[16];
+                    tmem_ld16(tbase + j * kBN + c * 16, p);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    promote16(acc + 16 * c, p, sc, kb == 0);
+                }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) bar_arrive(&p_empty[j]);
+                if (lane == 0) bar_arrive(&ready[(g + 2) % kStages]);  // P[g % 2] is free for block g + 2
                 sc = sc_next;
             }
             if (ok && n < a.N) {

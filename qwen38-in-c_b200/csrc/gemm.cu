@@ -36,12 +36,13 @@
 //     so the MMA warp waits on one barrier per 128-column block (the TMA,
 //     the converters and the epilogue all arrive on it) and commits once.
 //
-// Roles (608 threads):
+// Roles (640 threads):
 //   warp 0      TMA producer of the activation tile [192 tokens x 128 cols]
 //               f16 (two 64-column boxes, 128B swizzle), 3 stages;
-//   warp 1      lane 0 issues tcgen05.mma kind::f16 (A = the weight tile from
+//   warps 1, 19 lane 0 issues tcgen05.mma kind::f16 (A = the weight tile from
 //               TMEM, M = 128; B = the activation tile from shared memory,
 //               N = 192; 8 steps of K = 16) into TMEM partial P[g % 2];
+//               warp 1 takes the even blocks, warp 19 the odd ones;
 //   warp 2      TMA producer of the fp8 weight tile [128 rows x 128 B],
 //               4 stages released by the converters;
 //   warps 3-6   converters: thread = weight row = TMEM lane; converts its
@@ -82,7 +83,8 @@ constexpr int kConvWarps = 4;                       // one thread per weight row
 constexpr int kWarpEpi = kWarpConv + kConvWarps;    // 7
 constexpr int kEpiGroups = kBN / 64;                // 64 token columns per epilogue warp
 constexpr int kEpiWarps = 4 * kEpiGroups;           // 4 lane quadrants x 3 column groups
-constexpr int kThreads = (kWarpEpi + kEpiWarps) * 32;
+constexpr int kWarpMma2 = kWarpEpi + kEpiWarps;     // 19: MMA issuer of the odd blocks
+constexpr int kThreads = (kWarpMma2 + 1) * 32;
 // TMEM columns: P0 | P1 (fp32 partials, kBN each) | A0 | A1 (64 each: 128 f16 per lane)
 constexpr uint32_t kTmemA = 2 * kBN;
 constexpr uint32_t kACols = kBK / 2;
@@ -317,12 +319,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         drain(w_full, kWStages, g);
-    } else if (warp == kWarpMma) {
-        // ---------------- MMA issuer (whole warp, lane 0 issues) ------------
-        uint32_t g = 0;
+    } else if (warp == kWarpMma || warp == kWarpMma2) {
+        // ---------------- MMA issuers (whole warp, lane 0 issues) -----------
+        // A thread issuing tcgen05.mma blocks until the tensor pipe takes the
+        // instruction, so its per-block wait and commit would leave the pipe
+        // idle; two warps take alternate blocks (each block has its own P, A
+        // and activation stage) and one warp's wait overlaps the other's MMAs.
+        const uint32_t parity = warp == kWarpMma ? 0u : 1u;
+        uint32_t g = 0, last = 0xFFFFFFFFu;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                if ((g & 1) != parity) continue;
                 const int s = g % kStages, j = g & 1;
                 ok = __all_sync(0xffffffffu, bar_wait(&ready[s], (g / kStages) & 1));
                 if (!ok) break;
@@ -335,10 +343,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_f16_ts(d, acol + ks * 8, sw128_desc(xbase + off), ks > 0, leader);
                 }
                 mma_commit(&done[s], leader);
+                last = g;
             }
         }
-        // the last block must have completed before the CTA can free TMEM
-        if (ok && g) bar_wait(&done[(g - 1) % kStages], ((g - 1) / kStages) & 1);
+        // this warp's last block must have completed before the CTA can free TMEM
+        if (ok && last != 0xFFFFFFFFu) bar_wait(&done[last % kStages], (last / kStages) & 1);
     } else if (warp < kWarpEpi) {
         // ---------------- converters: fp8 -> f16 into TMEM -------------------
         // Thread = weight row = TMEM lane (warp w may access lanes 32*(w%4)..).

@@ -449,6 +449,10 @@ def run_ours(args):
         uid = [q35cu.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0, group=cpu_group)
         q35cu.tp_init(rank, world, uid[0])
+        # the one-shot NVLink collectives: every rank's exchange-area handle
+        hs = [None] * world
+        dist.all_gather_object(hs, q35cu.p2p_handle(), group=cpu_group)
+        q35cu.p2p_open(rank, world, hs)
 
     hbm_peak, bf16_peak, bf16_sus, peak_src = peaks()
     st = stack.Stack(rank, world, n_layers=args.layers, scheme="literal")
@@ -469,8 +473,10 @@ def run_ours(args):
 
     results = {}
     graphs = []
-    for scheme in (["literal", "paired"] if world > 1 else ["literal"]):
-        st.scheme = scheme
+    variants = [("p2p", "literal"), ("p2p", "paired"), ("nccl", "literal"), ("nccl", "paired")] if world > 1 \
+        else [("nccl", "literal")]
+    for coll, scheme in variants:
+        st.scheme, st.coll = scheme, coll
         # eager warm-up, then capture one step in a CUDA graph
         for _ in range(2):
             st.step()
@@ -502,9 +508,9 @@ def run_ours(args):
         clocks = clk.stop()
         barrier()
         ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-        results[scheme] = {"ms": ms, "clocks": clocks, "kernels_per_step": kernels_per_step}
+        results[(coll, scheme)] = {"ms": ms, "clocks": clocks, "kernels_per_step": kernels_per_step}
 
-    main = results["literal"]
+    main = results[variants[0]]
     total_bytes = stack.weight_bytes(args.layers)
     value = total_bytes / (main["ms"] * 1e-3) / 1e9
 
@@ -517,7 +523,7 @@ def run_ours(args):
         hx = torch.randn(st.x.shape).pin_memory()
         hy = torch.empty(st.y.shape).pin_memory()
         g = graphs[0]
-        st.scheme = "literal"
+        st.coll, st.scheme = variants[0]
         for _ in range(2):
             st.x.copy_(hx, non_blocking=True)
             g.replay()
@@ -578,6 +584,7 @@ def run_ours(args):
                                    f"48 DeltaNet + 16 GQA layers",
                        "weight_bytes_per_step": total_bytes, "parallelism": f"tp{world}",
                        "tp_scheme": "literal (all-gather after column-parallel, all-reduce after row-parallel)",
+                       "collectives": ("one-shot NVLink peer-memory kernels (q35cu_p2p_*)" if world > 1 else "none"),
                        "l2": "inputs larger than L2 (weights per GPU per step >> 126 MB)", "cuda_graph": True},
             "gpu_launches": main["kernels_per_step"] * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -590,9 +597,12 @@ def run_ours(args):
             "e2e": e2e,
         }
         if world > 1:
-            line["paired"] = {"ms_per_step": round(results["paired"]["ms"], 4),
-                              "value": round(total_bytes / (results["paired"]["ms"] * 1e-3) / 1e9, 1),
-                              "note": "Megatron pairing: no all-gather, the row-parallel projection consumes the local shard"}
+            line["variants"] = {f"{c}_{sc}": {"ms_per_step": round(r["ms"], 4),
+                                              "value": round(total_bytes / (r["ms"] * 1e-3) / 1e9, 1)}
+                                for (c, sc), r in results.items()}
+            line["variants_note"] = ("p2p = libq35cuda one-shot NVLink collectives, nccl = NCCL; literal = all-gather "
+                                     "after column-parallel + all-reduce after row-parallel, paired = Megatron pairing "
+                                     "(no all-gather, the row-parallel projection consumes the local shard)")
             line["collectives_per_step"] = colls
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu.get(k) for k in ("value", "unit", "cores", "kind", "sample")}
@@ -605,6 +615,9 @@ def run_ours(args):
     graphs.clear()
     st.free()
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        q35cu.p2p_close()
         q35cu.tp_finalize()
         dist.barrier()
         dist.destroy_process_group()

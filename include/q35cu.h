@@ -164,6 +164,27 @@ int q35cu_tp_rank(void);
 int q35cu_tp_finalize(void);
 int q35cu_allreduce_f32(float *buf, size_t n, void *stream);
 int q35cu_allgather_f32(const float *send, float *recv, size_t n_per_rank, void *stream);
+/* One-shot collectives over NVLink peer memory for the small vectors a
+ * tensor-parallel decode step exchanges (no NCCL call; the reference has no
+ * counterpart).  Every rank owns an exchange area in its HBM:
+ *   1. q35cu_p2p_handle(h, cap): allocates this rank's area (on the current
+ *      device) and writes its CUDA IPC handle (Q35CU_P2P_HANDLE_BYTES bytes);
+ *   2. the caller gathers every rank's handle (rank order, any transport);
+ *   3. q35cu_p2p_open(rank, world, handles, Q35CU_P2P_HANDLE_BYTES) maps the
+ *      peers' areas (world <= 8, one process per GPU).
+ * The collectives are then asynchronous on `stream` and may be captured in a
+ * CUDA graph; every rank must issue the same sequence of them.  The sum is
+ * taken in rank order, so all ranks get the same bits, run after run.  At
+ * most q35cu_p2p_max_elems() values per rank per call (larger exchanges stay
+ * on NCCL).  in == out is allowed.  q35cu_p2p_close() unmaps and frees (call
+ * it on every rank once no collective is in flight). */
+#define Q35CU_P2P_HANDLE_BYTES 64
+int q35cu_p2p_handle(void *out, size_t cap);
+int q35cu_p2p_open(int rank, int world, const void *handles, size_t handle_bytes);
+int q35cu_p2p_close(void);
+size_t q35cu_p2p_max_elems(void);
+int q35cu_p2p_allreduce_f32(const float *in, float *out, size_t n, void *stream);
+int q35cu_p2p_allgather_f32(const float *send, float *recv, size_t n_per_rank, void *stream);
 
 /* ---- info --------------------------------------------------------------- */
 const char *q35cu_build_info(void);

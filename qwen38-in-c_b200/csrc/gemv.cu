@@ -955,10 +955,12 @@ int device_status(uint32_t *status, bool clear)
         const uint32_t z = 0;
         Q35CU_CUDA(cudaMemcpyToSymbol(g_device_status, &z, 4));
     }
-    uint32_t g = 0;
-    const int rc = gemm_status(&g, clear);
+    uint32_t g = 0, p = 0;
+    int rc = gemm_status(&g, clear);
     if (rc) return rc;
-    if (!*status) *status = g;
+    rc = p2p_status(&p, clear);
+    if (rc) return rc;
+    if (!*status) *status = g ? g : p;
     return Q35CU_OK;
 }
 

@@ -67,6 +67,7 @@ int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tsca
                     cudaStream_t st);
 int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
 int gemm_status(uint32_t *status, bool clear);
+int p2p_status(uint32_t *status, bool clear);
 int launch_bf16_to_f32_scales(const uint16_t *src, float *dst, size_t n, cudaStream_t st);
 int launch_f32_to_bf16_scales(const float *src, uint16_t *dst, size_t n, cudaStream_t st);
 int launch_synth_fp8(uint64_t seed, float stddev, uint32_t grows, uint32_t gcols,

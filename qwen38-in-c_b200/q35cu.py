@@ -89,6 +89,12 @@ _SIGS = [
     ("q35cu_tp_finalize", C.c_int, []),
     ("q35cu_allreduce_f32", C.c_int, [_vp, C.c_size_t, _vp]),
     ("q35cu_allgather_f32", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
+    ("q35cu_p2p_handle", C.c_int, [_vp, C.c_size_t]),
+    ("q35cu_p2p_open", C.c_int, [C.c_int, C.c_int, _vp, C.c_size_t]),
+    ("q35cu_p2p_close", C.c_int, []),
+    ("q35cu_p2p_max_elems", C.c_size_t, []),
+    ("q35cu_p2p_allreduce_f32", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
+    ("q35cu_p2p_allgather_f32", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_build_info", C.c_char_p, []),
     ("q35cu_launch_count", C.c_uint64, []),
     ("q35cu_device_status", C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
@@ -261,6 +267,8 @@ def _stream(stream) -> int:
         import torch
 
         stream = torch.cuda.current_stream().cuda_stream
+    elif hasattr(stream, "cuda_stream"):  # a torch.cuda.Stream
+        stream = stream.cuda_stream
     s = int(stream)
     return s if s != 0 else CUDA_STREAM_LEGACY
 
@@ -355,6 +363,36 @@ def allreduce(buf, stream=None) -> None:
 
 def allgather(send, recv, stream=None) -> None:
     check(load().q35cu_allgather_f32(_ptr(send), _ptr(recv), send.numel(), _stream(stream)))
+
+
+P2P_HANDLE_BYTES = 64
+
+
+def p2p_handle() -> bytes:
+    """Allocate this rank's NVLink exchange area; its CUDA IPC handle."""
+    buf = C.create_string_buffer(P2P_HANDLE_BYTES)
+    check(load().q35cu_p2p_handle(buf, P2P_HANDLE_BYTES))
+    return buf.raw
+
+
+def p2p_open(rank: int, world: int, handles: list) -> None:
+    """Map every rank's exchange area (handles in rank order)."""
+    blob = b"".join(handles)
+    buf = C.create_string_buffer(blob, len(blob))
+    check(load().q35cu_p2p_open(rank, world, buf, P2P_HANDLE_BYTES))
+
+
+def p2p_close() -> None:
+    check(load().q35cu_p2p_close())
+
+
+def p2p_allreduce(buf, out=None, stream=None) -> None:
+    out = buf if out is None else out
+    check(load().q35cu_p2p_allreduce_f32(_ptr(buf), _ptr(out), buf.numel(), _stream(stream)))
+
+
+def p2p_allgather(send, recv, stream=None) -> None:
+    check(load().q35cu_p2p_allgather_f32(_ptr(send), _ptr(recv), send.numel(), _stream(stream)))
 
 
 def declared_symbols() -> list[str]:

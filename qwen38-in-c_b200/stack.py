@@ -103,11 +103,15 @@ class Stack:
     one decode step on a stream (capturable in a CUDA graph)."""
 
     def __init__(self, rank: int = 0, world: int = 1, n_layers: int = N_LAYERS, scheme: str = "literal",
-                 seed: int = 0x5EED, device=None):
+                 seed: int = 0x5EED, device=None, coll: str = "nccl"):
         import torch
 
         assert scheme in ("literal", "paired")
+        assert coll in ("nccl", "p2p")
         self.rank, self.world, self.scheme, self.n_layers = rank, world, scheme, n_layers
+        # collectives between projections: NCCL, or the one-shot NVLink
+        # peer-memory kernels of libq35cuda (q35cu_p2p_*, opened by the caller)
+        self.coll = coll
         self.dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.layers: list[Layer] = []
         self.weights: list[q35cu.Weight] = []
@@ -156,7 +160,7 @@ class Stack:
                 off += n
             q35cu.multi([p.w for p in L.col_in], xi, outs, 1, stream)
             if literal:
-                q35cu.allgather(self.col_local[:off], self.col_full[:off * self.world], stream)
+                self._allgather(self.col_local[:off], self.col_full[:off * self.world], stream)
             # out / o consume this rank's K-slice of their input: for DeltaNet the
             # local z shard IS z[c0:c0+nc] (same 128-aligned split of 6144); for
             # GQA the first nc values of the local q shard stand in for the
@@ -166,15 +170,27 @@ class Stack:
             src = outs[-1] if L.kind == "dn" else outs[0]
             q35cu.gemv(ao.w, src[:nc], self.o_buf, 1, stream)
             if self.world > 1:
-                q35cu.allreduce(self.o_buf, stream)
+                self._allreduce(self.o_buf, stream)
             # MLP: gate/up column-parallel, down row-parallel on the gate shard
             g_n = L.gate.window[1]
             q35cu.multi([L.gate.w, L.up.w], self.o_buf, [self.gu_local[:g_n], self.gu_local[g_n:2 * g_n]], 1, stream)
             if literal:
-                q35cu.allgather(self.gu_local[:2 * g_n], self.gu_full[:2 * g_n * self.world], stream)
+                self._allgather(self.gu_local[:2 * g_n], self.gu_full[:2 * g_n * self.world], stream)
             q35cu.gemv(L.down.w, self.gu_local[:g_n], self.y[i], 1, stream)
             if self.world > 1:
-                q35cu.allreduce(self.y[i], stream)
+                self._allreduce(self.y[i], stream)
+
+    def _allreduce(self, buf, stream) -> None:
+        if self.coll == "p2p":
+            q35cu.p2p_allreduce(buf, stream=stream)
+        else:
+            q35cu.allreduce(buf, stream)
+
+    def _allgather(self, send, recv, stream) -> None:
+        if self.coll == "p2p":
+            q35cu.p2p_allgather(send, recv, stream)
+        else:
+            q35cu.allgather(send, recv, stream)
 
     def launches_per_step(self) -> int:
         """Kernels (this library's) + collectives one step issues on this rank."""

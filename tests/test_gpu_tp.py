@@ -11,8 +11,12 @@ Needs at least two GPUs (skipped otherwise).  Each rank
   bit for bit: every row is computed whole), all-reduce for row-parallel
   (the K sum is split across ranks; must meet the guarded 1e-5 GEMV bound
   against the CPU oracle);
-* runs two layers of the decode-step harness with both schemes and checks
-  that the replicated outputs agree bit for bit across ranks.
+* checks the one-shot NVLink collectives (q35cu_p2p_*): exact on integer
+  data, bit-identical to NCCL (at two ranks a sum has one order), correct
+  across CUDA-graph replays (their sequence numbers live on the device);
+* runs two layers of the decode-step harness with both schemes on both
+  collective backends and checks that the replicated outputs agree bit for
+  bit across ranks and between the backends.
 
 The shard layout and combination rules follow the reference's projections
 (qwen35-c/src/q35_model.c: q/k/v/z/gate/up produce rows, o/out/down reduce
@@ -78,6 +82,42 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     rep["allreduce_exact"] = bool(torch.equal(buf.cpu(), torch.arange(n, dtype=torch.float32) * (world * (world + 1) // 2)))
     rep["allgather_exact"] = bool(torch.equal(recv.cpu(), torch.arange(world, dtype=torch.float32).repeat_interleave(777)))
 
+    # one-shot NVLink collectives: exact on integer data, bit-identical to NCCL
+    # (at two ranks a sum has one order), stable across CUDA-graph replays
+    hs = [None] * world
+    dist.all_gather_object(hs, q35cu.p2p_handle())
+    q35cu.p2p_open(rank, world, hs)
+    buf = torch.arange(n, dtype=torch.float32, device="cuda") * (rank + 1)
+    q35cu.p2p_allreduce(buf)
+    recv.zero_()
+    q35cu.p2p_allgather(send, recv)
+    torch.cuda.synchronize()
+    rep["p2p_allreduce_exact"] = bool(torch.equal(buf.cpu(), torch.arange(n, dtype=torch.float32) * (world * (world + 1) // 2)))
+    rep["p2p_allgather_exact"] = bool(torch.equal(recv.cpu(), torch.arange(world, dtype=torch.float32).repeat_interleave(777)))
+    v = torch.randn(5120, generator=torch.Generator().manual_seed(100 + rank)).cuda()
+    a_nccl, a_p2p = v.clone(), torch.empty_like(v)
+    q35cu.allreduce(a_nccl)
+    q35cu.p2p_allreduce(v, a_p2p)
+    torch.cuda.synchronize()
+    rep["p2p_equals_nccl"] = bool(torch.equal(a_nccl.cpu(), a_p2p.cpu()))
+    src = torch.empty(5120, device="cuda")
+    dst = torch.empty(5120, device="cuda")
+    s_ = torch.cuda.Stream()
+    s_.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s_):
+        with torch.cuda.graph(g, stream=s_):
+            q35cu.p2p_allreduce(src, dst, stream=s_)
+    torch.cuda.current_stream().wait_stream(s_)
+    ok = True
+    for it in range(5):
+        src.copy_(torch.full((5120,), float(it * 10 + rank)))
+        g.replay()
+        torch.cuda.synchronize()
+        ok &= bool(torch.equal(dst.cpu(), torch.full((5120,), float(world * it * 10 + world * (world - 1) // 2))))
+    del g
+    rep["p2p_graph_replays"] = ok
+
     # sharded projections against the whole weight
     orc = oracle.Oracle()
     rep["shapes"] = []
@@ -116,19 +156,30 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             full.free()
             rep["shapes"].append(entry)
 
-    # two layers of the decode step, both schemes: replicated outputs agree across ranks
+    # two layers of the decode step, both schemes, both collective backends:
+    # replicated outputs agree across ranks, and P2P equals NCCL (two ranks)
     st = stack.Stack(rank, world, n_layers=2, scheme="literal")
     st.x.copy_(torch.randn(st.x.shape, generator=torch.Generator().manual_seed(5)).cuda())
-    for scheme in ("literal", "paired"):
-        st.scheme = scheme
-        st.step()
-        torch.cuda.synchronize()
-        y = st.y.clone()
-        ys = [torch.empty_like(y).cpu() for _ in range(world)]
-        dist.all_gather_object(ys, y.cpu())
-        rep[f"stack_{scheme}_finite"] = bool(torch.isfinite(y).all())
-        rep[f"stack_{scheme}_replicated"] = all(torch.equal(ys[0], t) for t in ys)
+    outs = {}
+    for coll in ("nccl", "p2p"):
+        st.coll = coll
+        for scheme in ("literal", "paired"):
+            st.scheme = scheme
+            st.step()
+            torch.cuda.synchronize()
+            y = st.y.clone()
+            ys = [torch.empty_like(y).cpu() for _ in range(world)]
+            dist.all_gather_object(ys, y.cpu())
+            rep[f"stack_{coll}_{scheme}_finite"] = bool(torch.isfinite(y).all())
+            rep[f"stack_{coll}_{scheme}_replicated"] = all(torch.equal(ys[0], t) for t in ys)
+            outs[(coll, scheme)] = y.cpu()
+    rep["stack_p2p_equals_nccl"] = all(torch.equal(outs[("nccl", sc)], outs[("p2p", sc)]) for sc in ("literal", "paired"))
     st.free()
+    status = q35cu.C.c_uint32(0)
+    q35cu.check(q35cu.load().q35cu_device_status(q35cu.C.byref(status), 1))
+    rep["device_status"] = int(status.value)
+    dist.barrier()
+    q35cu.p2p_close()
     q35cu.tp_finalize()
     with open(os.path.join(out_dir, f"tp_gpu_rank{rank}.json"), "w") as f:
         json.dump(rep, f)
@@ -149,8 +200,14 @@ def test_tp_two_gpus(tmp_path):
     reps = [json.loads((tmp_path / f"tp_gpu_rank{r}.json").read_text()) for r in range(world)]
     for rep in reps:
         assert rep["allreduce_exact"] and rep["allgather_exact"], rep
-        for scheme in ("literal", "paired"):
-            assert rep[f"stack_{scheme}_finite"] and rep[f"stack_{scheme}_replicated"], (scheme, rep)
+        assert rep["p2p_allreduce_exact"] and rep["p2p_allgather_exact"], rep
+        assert rep["p2p_equals_nccl"] and rep["p2p_graph_replays"], rep
+        assert rep["device_status"] == 0, rep
+        for coll in ("nccl", "p2p"):
+            for scheme in ("literal", "paired"):
+                key = f"stack_{coll}_{scheme}"
+                assert rep[key + "_finite"] and rep[key + "_replicated"], (key, rep)
+        assert rep["stack_p2p_equals_nccl"], rep
     shapes = reps[0]["shapes"]
     assert len(shapes) == len(SHAPES)
     for e in shapes:

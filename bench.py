@@ -473,8 +473,8 @@ def run_ours(args):
 
     results = {}
     graphs = []
-    variants = [("p2p", "literal"), ("p2p", "paired"), ("nccl", "literal"), ("nccl", "paired")] if world > 1 \
-        else [("nccl", "literal")]
+    variants = [("fused", "literal"), ("fused", "paired"), ("p2p", "literal"), ("p2p", "paired"),
+                ("nccl", "literal"), ("nccl", "paired")] if world > 1 else [("nccl", "literal")]
     for coll, scheme in variants:
         st.scheme, st.coll = scheme, coll
         # eager warm-up, then capture one step in a CUDA graph
@@ -584,7 +584,8 @@ def run_ours(args):
                                    f"48 DeltaNet + 16 GQA layers",
                        "weight_bytes_per_step": total_bytes, "parallelism": f"tp{world}",
                        "tp_scheme": "literal (all-gather after column-parallel, all-reduce after row-parallel)",
-                       "collectives": ("one-shot NVLink peer-memory kernels (q35cu_p2p_*)" if world > 1 else "none"),
+                       "collectives": ("fused into the GEMV epilogues over NVLink peer memory (q35cu_multi_fp8_tp)"
+                                       if world > 1 else "none"),
                        "l2": "inputs larger than L2 (weights per GPU per step >> 126 MB)", "cuda_graph": True},
             "gpu_launches": main["kernels_per_step"] * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -600,7 +601,8 @@ def run_ours(args):
             line["variants"] = {f"{c}_{sc}": {"ms_per_step": round(r["ms"], 4),
                                               "value": round(total_bytes / (r["ms"] * 1e-3) / 1e9, 1)}
                                 for (c, sc), r in results.items()}
-            line["variants_note"] = ("p2p = libq35cuda one-shot NVLink collectives, nccl = NCCL; literal = all-gather "
+            line["variants_note"] = ("fused = exchange in the GEMV epilogue (no collective kernel), p2p = libq35cuda "
+                                     "one-shot NVLink collective kernels, nccl = NCCL; literal = all-gather "
                                      "after column-parallel + all-reduce after row-parallel, paired = Megatron pairing "
                                      "(no all-gather, the row-parallel projection consumes the local shard)")
             line["collectives_per_step"] = colls

@@ -185,6 +185,22 @@ int q35cu_p2p_close(void);
 size_t q35cu_p2p_max_elems(void);
 int q35cu_p2p_allreduce_f32(const float *in, float *out, size_t n, void *stream);
 int q35cu_p2p_allgather_f32(const float *send, float *recv, size_t n_per_rank, void *stream);
+/* The decode GEMV (one token) with the tensor-parallel exchange fused into
+ * its epilogue over the same peer memory (q35cu_p2p_open first): every rank
+ * splits the rows over CTAs the same way, so each CTA publishes its output
+ * rows to every rank and waits only for its peers' copies of those rows --
+ * no separate collective kernel.
+ *   Q35CU_TP_ALLREDUCE (row-parallel: down/o/out): Y[s] = the sum over ranks
+ *     (in rank order) of every rank's product;
+ *   Q35CU_TP_ALLGATHER (column-parallel: gate/up/qkv/z/q/k/v): Y[s] as
+ *     q35cu_multi_fp8, and gathered[q * R + v] = rank q's row v, with v the
+ *     call's row index over its segments in order and R their total rows
+ *     (the layout of q35cu_allgather_f32 on the packed outputs).
+ * X is [cols] fp32.  Every rank must make the same sequence of calls. */
+typedef enum { Q35CU_TP_ALLREDUCE = 1, Q35CU_TP_ALLGATHER = 2 } q35cu_tp_mode;
+int q35cu_multi_fp8_tp(const q35cu_weight *const w[4], const float *X, float *const Y[4], int mode,
+                       float *gathered, void *stream);
+int q35cu_gemv_fp8_tp(const q35cu_weight *w, const float *X, float *Y, int mode, float *gathered, void *stream);
 
 /* ---- info --------------------------------------------------------------- */
 const char *q35cu_build_info(void);

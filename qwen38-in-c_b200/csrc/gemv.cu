@@ -51,6 +51,7 @@
 
 #include <type_traits>
 
+#include "p2p_ll.cuh"
 #include "q35cu_internal.h"
 
 namespace q35cu {
@@ -415,6 +416,9 @@ struct MArgs {
     uint32_t ipr;         // items per row block = ceil(K / 256)
     uint32_t rb_round;    // row blocks per round (partials buffer)
     int nseg;
+    int tp_mode;          // GemvTp::mode (m == 1 only)
+    float *gathered;      // all-gather destination [world][total_rows]
+    P2PView p2p;          // the ranks' exchange areas
 };
 
 // one 16-row block of the CTA, resolved once: weight row pointer, the
@@ -629,6 +633,8 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
             if (lane == 0) xmul[tt * kbn + kb] = down;
         }
     }
+    __shared__ uint32_t tp_seq_s;
+    if (MT == 1 && a.tp_mode && t == 0) tp_seq_s = p2p_next_seq(a.p2p);  // the previous kernel has completed
     __syncthreads();
 
     for (uint32_t rb0 = 0; rb0 < nrb; rb0 += a.rb_round) {
@@ -661,9 +667,37 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
             float y = 0.f;
             for (uint32_t s = 0; s < ipr; ++s) y += part[((size_t)(rbl * ipr + s) * 16 + i) * MT + tt];
             const Seg &sg = a.seg[rb.nrows_seg >> 8];
+            if (MT == 1 && a.tp_mode) {  // one token: publish the row to every rank
+                const uint32_t v = sg.vbegin + rb.r + i, tp_seq = tp_seq_s;
+                for (int d = 0; d < a.p2p.world; ++d) p2p_put(p2p_slot(a.p2p.area[d], tp_seq, a.p2p.rank) + v, y, tp_seq);
+                if (a.tp_mode == 1) continue;  // all-reduce: Y is the cross-rank sum, written below
+            }
             sg.Y[(size_t)(tok0 + tt) * sg.ldy + rb.r + i] = y;
         }
         __syncthreads();
+    }
+
+    // Tensor-parallel epilogue (one token).  Every rank splits the rows over
+    // CTAs the same way, so this CTA only needs its peers' words for its own
+    // rows [vr0, vr1): no grid-wide barrier, no separate collective kernel.
+    if (MT == 1 && a.tp_mode) {
+        uint8_t *mine = a.p2p.area[a.p2p.rank];
+        const uint32_t tp_seq = tp_seq_s;
+        for (uint32_t v = vr0 + t; v < vr1; v += kM2Threads) {
+            if (a.tp_mode == 1) {
+                float y = 0.f;
+                for (int q = 0; q < a.p2p.world; ++q) y += p2p_get(p2p_slot(mine, tp_seq, q) + v, tp_seq, &g_device_status);
+                int s = 0;
+                for (int j = 1; j < a.nseg; ++j)
+                    if (v >= a.seg[j].vbegin) s = j;
+                a.seg[s].Y[v - a.seg[s].vbegin] = y;
+            } else {
+                for (int q = 0; q < a.p2p.world; ++q)
+                    a.gathered[(size_t)q * a.total_rows + v] = p2p_get(p2p_slot(mine, tp_seq, q) + v, tp_seq, &g_device_status);
+            }
+        }
+        __syncthreads();
+        if (t == 0) p2p_finish(a.p2p, tp_seq);
     }
 }
 
@@ -793,7 +827,7 @@ int launch_mma(const MArgs &a, dim3 grid, size_t smem, cudaStream_t st)
 }
 
 // FP8 weights with cols % 128 == 0: the tensor-core decode GEMV
-int launch_gemv_mma(const Args &a0, cudaStream_t st)
+int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp)
 {
     MArgs a{};
     for (int s = 0; s < 4; ++s) a.seg[s] = a0.seg[s];
@@ -806,6 +840,14 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st)
     a.nseg = a0.nseg;
     a.xcol_bytes = 2 * a0.K + 32;
     a.ipr = (a0.K + kItemCols - 1) / kItemCols;
+    a.tp_mode = tp.mode;
+    a.gathered = tp.gathered;
+    if (tp.mode) {
+        if (a0.m != 1) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: the tensor-parallel epilogue takes one token");
+        if (!p2p_view(&a.p2p)) return set_error(Q35CU_ERR_NCCL, "gemv: p2p collectives not open");
+        if (a0.total_rows > kP2PMaxElems) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: %u rows exceed the exchange area", a0.total_rows);
+        if (tp.mode == 2 && !tp.gathered) return set_error(Q35CU_ERR_ARG, "gemv: all-gather needs a destination");
+    }
     const uint32_t budget = 216 * 1024;
     const uint32_t sms = (uint32_t)device_sms();
     const uint32_t gx = ((a.total_rows + 15) / 16) < sms ? (a.total_rows + 15) / 16 : sms;
@@ -864,7 +906,7 @@ void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes)
 }
 
 int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint32_t K, uint32_t ldx, uint32_t m,
-                cudaStream_t st)
+                cudaStream_t st, const GemvTp &tp)
 {
     if (nseg < 1 || nseg > 4 || m == 0 || K == 0) return set_error(Q35CU_ERR_ARG, "gemv: bad launch shape");
     Args a{};
@@ -886,7 +928,8 @@ int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint
     }
     a.total_rows = vb;
     if (vb == 0) return Q35CU_OK;
-    if (vec_ok && kind == 0 && K % 128 == 0 && getenv("Q35CU_GEMV_SIMT") == nullptr) return launch_gemv_mma(a, st);
+    if (vec_ok && kind == 0 && K % 128 == 0 && getenv("Q35CU_GEMV_SIMT") == nullptr) return launch_gemv_mma(a, st, tp);
+    if (tp.mode) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: the tensor-parallel epilogue needs the tensor-core GEMV");
     uint32_t T = 0, P = 0;
     gemv_geometry(kind, K, &T, &P);
     if (P > 4) vec_ok = false;

@@ -36,6 +36,7 @@
 
 #include <cstring>
 
+#include "p2p_ll.cuh"
 #include "q35cu_internal.h"
 
 namespace q35cu {
@@ -45,85 +46,25 @@ __device__ uint32_t g_p2p_status;
 
 namespace {
 
-constexpr int kMaxRanks = 8;
-constexpr int kMaxChunks = 32;        // CTAs (and flags) per collective
+constexpr int kMaxChunks = 32;  // CTAs per collective
 constexpr uint32_t kThreads = 256;
-constexpr size_t kMaxElems = 256 * 1024;  // fp32 values per rank per collective
-constexpr uint32_t kSpinLimit = 1u << 24;
 
-// exchange area of one rank (byte offsets)
-constexpr size_t kSeqOff = 0;    // u32 sequence number of the last collective (local only)
-constexpr size_t kTicketOff = 4;  // u32 CTAs of the current collective that finished (local only)
-constexpr size_t kDataOff = 4096;                                           // [2][kMaxRanks][kMaxElems] u64
-constexpr size_t kAreaBytes = kDataOff + 2 * kMaxRanks * kMaxElems * 8;
-
-struct P2PArgs {
-    uint8_t *area[kMaxRanks];  // every rank's exchange area as mapped in this process
-    int rank, world;
-};
-
-__device__ __forceinline__ uint64_t *slot_ptr(uint8_t *area, uint32_t set, int src)
-{
-    return reinterpret_cast<uint64_t *>(area + kDataOff) + ((size_t)set * kMaxRanks + src) * kMaxElems;
-}
-__device__ __forceinline__ void st_word(uint64_t *p, float v, uint32_t seq)
-{
-    const uint64_t w = (uint64_t)__float_as_uint(v) | ((uint64_t)seq << 32);
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ uint64_t ld_word(const uint64_t *p)
-{
-    uint64_t w;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    return w;
-}
-// the value of word p once it carries `seq` (bounded wait)
-__device__ __forceinline__ float wait_word(const uint64_t *p, uint32_t seq)
-{
-    uint64_t w = ld_word(p);
-    for (uint32_t i = 0; (uint32_t)(w >> 32) != seq; ++i) {
-        if (i >= kSpinLimit) {
-            atomicExch(&g_p2p_status, (uint32_t)Q35CU_ERR_TIMEOUT);
-            break;
-        }
-        if (i > 32) __nanosleep(32);
-        w = ld_word(p);
-    }
-    return __uint_as_float((uint32_t)w);
-}
-
-// This CTA's chunk [lo, hi): read the sequence number, push src[lo, hi) into
-// slot[rank] of every area.  Returns the sequence number.
-__device__ __forceinline__ uint32_t push(const P2PArgs &a, const float *src, uint32_t lo, uint32_t hi)
+// push this CTA's chunk src[lo, hi) into slot[rank] of every area; returns
+// the collective's sequence number
+__device__ __forceinline__ uint32_t push(const P2PView &a, const float *src, uint32_t lo, uint32_t hi)
 {
     __shared__ uint32_t s_seq;
-    const uint32_t t = threadIdx.x;
-    if (t == 0) s_seq = *reinterpret_cast<volatile uint32_t *>(a.area[a.rank] + kSeqOff) + 1;
+    if (threadIdx.x == 0) s_seq = p2p_next_seq(a);
     __syncthreads();
-    const uint32_t seq = s_seq, set = seq & 1;
-    for (uint32_t i = lo + t; i < hi; i += kThreads) {
+    const uint32_t seq = s_seq;
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += kThreads) {
         const float v = src[i];
-        for (int d = 0; d < a.world; ++d) st_word(slot_ptr(a.area[d], set, a.rank) + i, v, seq);
+        for (int d = 0; d < a.world; ++d) p2p_put(p2p_slot(a.area[d], seq, a.rank) + i, v, seq);
     }
     return seq;
 }
-// the last CTA to finish advances the sequence number for the next collective
-__device__ __forceinline__ void finish(const P2PArgs &a, uint32_t seq)
-{
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        uint8_t *mine = a.area[a.rank];
-        uint32_t *ticket = reinterpret_cast<uint32_t *>(mine + kTicketOff);
-        __threadfence();
-        if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
-            *ticket = 0;
-            *reinterpret_cast<volatile uint32_t *>(mine + kSeqOff) = seq;
-            __threadfence();
-        }
-    }
-}
 
-__global__ void __launch_bounds__(kThreads) p2p_allreduce_kernel(const __grid_constant__ P2PArgs a, const float *in,
+__global__ void __launch_bounds__(kThreads) p2p_allreduce_kernel(const __grid_constant__ P2PView a, const float *in,
                                                                  float *out, uint32_t n)
 {
     asm volatile("griddepcontrol.launch_dependents;");
@@ -135,13 +76,14 @@ __global__ void __launch_bounds__(kThreads) p2p_allreduce_kernel(const __grid_co
     uint8_t *mine = a.area[a.rank];
     for (uint32_t i = lo + threadIdx.x; i < hi; i += kThreads) {
         float v = 0.f;
-        for (int s = 0; s < a.world; ++s) v += wait_word(slot_ptr(mine, seq & 1, s) + i, seq);  // rank order
+        for (int s = 0; s < a.world; ++s) v += p2p_get(p2p_slot(mine, seq, s) + i, seq, &g_p2p_status);  // rank order
         out[i] = v;
     }
-    finish(a, seq);
+    __syncthreads();
+    if (threadIdx.x == 0) p2p_finish(a, seq);
 }
 
-__global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_constant__ P2PArgs a, const float *send,
+__global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_constant__ P2PView a, const float *send,
                                                                  float *recv, uint32_t n)
 {
     asm volatile("griddepcontrol.launch_dependents;");
@@ -152,14 +94,15 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
     uint8_t *mine = a.area[a.rank];
     for (int s = 0; s < a.world; ++s)
         for (uint32_t i = lo + threadIdx.x; i < hi; i += kThreads)
-            recv[(size_t)s * n + i] = wait_word(slot_ptr(mine, seq & 1, s) + i, seq);
-    finish(a, seq);
+            recv[(size_t)s * n + i] = p2p_get(p2p_slot(mine, seq, s) + i, seq, &g_p2p_status);
+    __syncthreads();
+    if (threadIdx.x == 0) p2p_finish(a, seq);
 }
 
 struct P2PState {
     int device = -1;
     uint8_t *own = nullptr;
-    P2PArgs args{};
+    P2PView args{};
     bool open = false;
 };
 P2PState g_p2p;
@@ -189,6 +132,13 @@ uint32_t chunks_for(size_t n)
 
 }  // namespace
 
+bool p2p_view(P2PView *out)
+{
+    if (!g_p2p.open) return false;
+    *out = g_p2p.args;
+    return true;
+}
+
 int p2p_status(uint32_t *status, bool clear)
 {
     Q35CU_CUDA(cudaMemcpyFromSymbol(status, g_p2p_status, 4));
@@ -205,7 +155,7 @@ using namespace q35cu;
 
 #define Q35_API extern "C" __attribute__((visibility("default")))
 
-Q35_API size_t q35cu_p2p_max_elems(void) { return kMaxElems; }
+Q35_API size_t q35cu_p2p_max_elems(void) { return kP2PMaxElems; }
 
 Q35_API int q35cu_p2p_handle(void *out, size_t cap)
 {
@@ -217,10 +167,10 @@ Q35_API int q35cu_p2p_handle(void *out, size_t cap)
         return set_error(Q35CU_ERR_ARG, "p2p exchange area belongs to device %d, not %d", g_p2p.device, dev);
     if (!g_p2p.own) {
         void *p = nullptr;
-        Q35CU_CUDA(cudaMalloc(&p, kAreaBytes));
+        Q35CU_CUDA(cudaMalloc(&p, kP2PAreaBytes));
         // sequence numbers and words start at zero (no word carries a live
         // sequence number) before any peer can see the area
-        cudaError_t e = cudaMemset(p, 0, kAreaBytes);
+        cudaError_t e = cudaMemset(p, 0, kP2PAreaBytes);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) {
             cudaFree(p);
@@ -237,12 +187,12 @@ Q35_API int q35cu_p2p_handle(void *out, size_t cap)
 
 Q35_API int q35cu_p2p_open(int rank, int world, const void *handles, size_t handle_bytes)
 {
-    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !handles ||
+    if (world < 1 || world > kP2PMaxRanks || rank < 0 || rank >= world || !handles ||
         handle_bytes < sizeof(cudaIpcMemHandle_t))
         return set_error(Q35CU_ERR_ARG, "p2p_open: rank %d world %d", rank, world);
     if (!g_p2p.own) return set_error(Q35CU_ERR_ARG, "p2p_open: call q35cu_p2p_handle first");
     if (g_p2p.open) return set_error(Q35CU_ERR_ARG, "p2p_open: already open");
-    P2PArgs a{};
+    P2PView a{};
     a.rank = rank;
     a.world = world;
     for (int r = 0; r < world; ++r) {
@@ -276,7 +226,7 @@ Q35_API int q35cu_p2p_close(void)
                 if (e != cudaSuccess && rc == Q35CU_OK) rc = cuda_error(e, "cudaIpcCloseMemHandle");
             }
         g_p2p.open = false;
-        g_p2p.args = P2PArgs{};
+        g_p2p.args = P2PView{};
     }
     if (g_p2p.own) {
         const cudaError_t e = cudaFree(g_p2p.own);
@@ -290,7 +240,7 @@ Q35_API int q35cu_p2p_close(void)
 Q35_API int q35cu_p2p_allreduce_f32(const float *in, float *out, size_t n, void *stream)
 {
     if (!g_p2p.open) return set_error(Q35CU_ERR_NCCL, "p2p collectives not open");
-    if (!in || !out || n > kMaxElems) return set_error(Q35CU_ERR_ARG, "p2p_allreduce: n %zu (max %zu)", n, kMaxElems);
+    if (!in || !out || n > kP2PMaxElems) return set_error(Q35CU_ERR_ARG, "p2p_allreduce: n %zu (max %zu)", n, kP2PMaxElems);
     if (!n) return Q35CU_OK;
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : default_stream();
     return launch_p2p(p2p_allreduce_kernel, chunks_for(n), st, in, out, (uint32_t)n);
@@ -299,8 +249,8 @@ Q35_API int q35cu_p2p_allreduce_f32(const float *in, float *out, size_t n, void 
 Q35_API int q35cu_p2p_allgather_f32(const float *send, float *recv, size_t n_per_rank, void *stream)
 {
     if (!g_p2p.open) return set_error(Q35CU_ERR_NCCL, "p2p collectives not open");
-    if (!send || !recv || n_per_rank > kMaxElems)
-        return set_error(Q35CU_ERR_ARG, "p2p_allgather: n %zu (max %zu)", n_per_rank, kMaxElems);
+    if (!send || !recv || n_per_rank > kP2PMaxElems)
+        return set_error(Q35CU_ERR_ARG, "p2p_allgather: n %zu (max %zu)", n_per_rank, kP2PMaxElems);
     if (!n_per_rank) return Q35CU_OK;
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : default_stream();
     return launch_p2p(p2p_allgather_kernel, chunks_for(n_per_rank), st, send, recv, (uint32_t)n_per_rank);

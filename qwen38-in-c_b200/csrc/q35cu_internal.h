@@ -50,8 +50,15 @@ struct GemvSeg {
     uint32_t has_nan;   // weight holds e4m3 NaN codes
 };
 
+// tensor-parallel epilogue of the decode GEMV (m = 1): 0 none, 1 all-reduce
+// the outputs across ranks (Y = sum of every rank's product), 2 all-gather
+// them (Y as usual, plus gathered[q * R + v] = rank q's virtual row v)
+struct GemvTp {
+    int mode = 0;
+    float *gathered = nullptr;
+};
 int launch_gemv(int kind, const GemvSeg *segs, int nseg, const float *X,
-                uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st);
+                uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st, const GemvTp &tp = GemvTp{});
 int launch_swiglu(const float *g, const float *u, float *o, size_t n, cudaStream_t st);
 void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes);
 int device_status(uint32_t *status, bool clear);
@@ -68,6 +75,9 @@ int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tsca
 int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
 int gemm_status(uint32_t *status, bool clear);
 int p2p_status(uint32_t *status, bool clear);
+struct P2PView;
+// the mapped exchange areas of q35cu_p2p_open (false if not open)
+bool p2p_view(P2PView *out);
 int launch_bf16_to_f32_scales(const uint16_t *src, float *dst, size_t n, cudaStream_t st);
 int launch_f32_to_bf16_scales(const float *src, uint16_t *dst, size_t n, cudaStream_t st);
 int launch_synth_fp8(uint64_t seed, float stddev, uint32_t grows, uint32_t gcols,

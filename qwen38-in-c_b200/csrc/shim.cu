@@ -643,6 +643,38 @@ Q35_API int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint
     return launch_gemv(0, segs, n, X, K, ldx, m, pick(stream));
 }
 
+Q35_API int q35cu_multi_fp8_tp(const q35cu_weight *const w[4], const float *X, float *const Y[4], int mode,
+                               float *gathered, void *stream)
+{
+    if (!w || !Y || !X) return set_error(Q35CU_ERR_ARG, "multi_fp8_tp: bad arguments");
+    if (mode != Q35CU_TP_ALLREDUCE && mode != Q35CU_TP_ALLGATHER)
+        return set_error(Q35CU_ERR_ARG, "multi_fp8_tp: mode %d", mode);
+    GemvSeg segs[4];
+    int n = 0;
+    uint32_t K = 0;
+    for (int s = 0; s < 4; ++s) {
+        if (!w[s]) continue;
+        if (w[s]->kind != 0 || !Y[s]) return set_error(Q35CU_ERR_ARG, "multi_fp8_tp: segment %d", s);
+        if (K && w[s]->cols != K) return set_error(Q35CU_ERR_ARG, "multi_fp8_tp: segments disagree on cols");
+        K = w[s]->cols;
+        segs[n++] = seg_of(w[s], Y[s], w[s]->rows);
+    }
+    if (!n) return Q35CU_OK;
+    GemvTp tp;
+    tp.mode = mode;
+    tp.gathered = gathered;
+    return launch_gemv(0, segs, n, X, K, K, 1, pick(stream), tp);
+}
+
+Q35_API int q35cu_gemv_fp8_tp(const q35cu_weight *w, const float *X, float *Y, int mode, float *gathered,
+                              void *stream)
+{
+    const q35cu_weight *ws[4] = {w, nullptr, nullptr, nullptr};
+    float *ys[4] = {Y, nullptr, nullptr, nullptr};
+    if (!w) return set_error(Q35CU_ERR_ARG, "gemv_fp8_tp: bad arguments");
+    return q35cu_multi_fp8_tp(ws, X, ys, mode, gathered, stream);
+}
+
 Q35_API size_t q35cu_gemm_fp8_workspace_bytes(uint32_t m, uint32_t cols)
 {
     return gemm_workspace_bytes(m, cols);

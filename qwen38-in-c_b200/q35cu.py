@@ -95,6 +95,8 @@ _SIGS = [
     ("q35cu_p2p_max_elems", C.c_size_t, []),
     ("q35cu_p2p_allreduce_f32", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_p2p_allgather_f32", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
+    ("q35cu_multi_fp8_tp", C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp]),
+    ("q35cu_gemv_fp8_tp", C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp]),
     ("q35cu_build_info", C.c_char_p, []),
     ("q35cu_launch_count", C.c_uint64, []),
     ("q35cu_device_status", C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
@@ -393,6 +395,23 @@ def p2p_allreduce(buf, out=None, stream=None) -> None:
 
 def p2p_allgather(send, recv, stream=None) -> None:
     check(load().q35cu_p2p_allgather_f32(_ptr(send), _ptr(recv), send.numel(), _stream(stream)))
+
+
+TP_ALLREDUCE, TP_ALLGATHER = 1, 2
+
+
+def multi_tp(ws, X, Ys, mode: int, gathered=None, stream=None) -> None:
+    """One-token decode GEMV of up to four weights with the TP exchange fused in."""
+    ws = list(ws) + [None] * (4 - len(ws))
+    Ys = list(Ys) + [None] * (4 - len(Ys))
+    wp = (_vp * 4)(*[None if w is None else w.h.value for w in ws])
+    yp = (_vp * 4)(*[None if y is None else _ptr(y) for y in Ys])
+    check(load().q35cu_multi_fp8_tp(wp, _ptr(X), yp, mode, None if gathered is None else _ptr(gathered),
+                                    _stream(stream)))
+
+
+def gemv_tp(w, X, Y, mode: int, gathered=None, stream=None) -> None:
+    multi_tp([w], X, [Y], mode, gathered, stream)
 
 
 def declared_symbols() -> list[str]:

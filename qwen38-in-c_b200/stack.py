@@ -107,10 +107,12 @@ class Stack:
         import torch
 
         assert scheme in ("literal", "paired")
-        assert coll in ("nccl", "p2p")
+        assert coll in ("nccl", "p2p", "fused")
         self.rank, self.world, self.scheme, self.n_layers = rank, world, scheme, n_layers
-        # collectives between projections: NCCL, or the one-shot NVLink
-        # peer-memory kernels of libq35cuda (q35cu_p2p_*, opened by the caller)
+        # collectives between projections: NCCL, the one-shot NVLink
+        # peer-memory kernels of libq35cuda (q35cu_p2p_*, opened by the
+        # caller), or "fused": the same exchange inside the GEMVs' epilogues
+        # (q35cu_multi_fp8_tp) with no collective kernel at all
         self.coll = coll
         self.dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.layers: list[Layer] = []
@@ -158,9 +160,13 @@ class Stack:
                 n = p.window[1]
                 outs.append(self.col_local[off:off + n])
                 off += n
-            q35cu.multi([p.w for p in L.col_in], xi, outs, 1, stream)
-            if literal:
-                self._allgather(self.col_local[:off], self.col_full[:off * self.world], stream)
+            fused = self.coll == "fused" and self.world > 1
+            if fused and literal:
+                q35cu.multi_tp([p.w for p in L.col_in], xi, outs, q35cu.TP_ALLGATHER, self.col_full, stream)
+            else:
+                q35cu.multi([p.w for p in L.col_in], xi, outs, 1, stream)
+                if literal:
+                    self._allgather(self.col_local[:off], self.col_full[:off * self.world], stream)
             # out / o consume this rank's K-slice of their input: for DeltaNet the
             # local z shard IS z[c0:c0+nc] (same 128-aligned split of 6144); for
             # GQA the first nc values of the local q shard stand in for the
@@ -168,17 +174,27 @@ class Stack:
             ao = L.attn_out
             nc = ao.window[3]
             src = outs[-1] if L.kind == "dn" else outs[0]
-            q35cu.gemv(ao.w, src[:nc], self.o_buf, 1, stream)
-            if self.world > 1:
-                self._allreduce(self.o_buf, stream)
+            if fused:
+                q35cu.gemv_tp(ao.w, src[:nc], self.o_buf, q35cu.TP_ALLREDUCE, None, stream)
+            else:
+                q35cu.gemv(ao.w, src[:nc], self.o_buf, 1, stream)
+                if self.world > 1:
+                    self._allreduce(self.o_buf, stream)
             # MLP: gate/up column-parallel, down row-parallel on the gate shard
             g_n = L.gate.window[1]
-            q35cu.multi([L.gate.w, L.up.w], self.o_buf, [self.gu_local[:g_n], self.gu_local[g_n:2 * g_n]], 1, stream)
-            if literal:
-                self._allgather(self.gu_local[:2 * g_n], self.gu_full[:2 * g_n * self.world], stream)
-            q35cu.gemv(L.down.w, self.gu_local[:g_n], self.y[i], 1, stream)
-            if self.world > 1:
-                self._allreduce(self.y[i], stream)
+            gu = [self.gu_local[:g_n], self.gu_local[g_n:2 * g_n]]
+            if fused and literal:
+                q35cu.multi_tp([L.gate.w, L.up.w], self.o_buf, gu, q35cu.TP_ALLGATHER, self.gu_full, stream)
+            else:
+                q35cu.multi([L.gate.w, L.up.w], self.o_buf, gu, 1, stream)
+                if literal:
+                    self._allgather(self.gu_local[:2 * g_n], self.gu_full[:2 * g_n * self.world], stream)
+            if fused:
+                q35cu.gemv_tp(L.down.w, self.gu_local[:g_n], self.y[i], q35cu.TP_ALLREDUCE, None, stream)
+            else:
+                q35cu.gemv(L.down.w, self.gu_local[:g_n], self.y[i], 1, stream)
+                if self.world > 1:
+                    self._allreduce(self.y[i], stream)
 
     def _allreduce(self, buf, stream) -> None:
         if self.coll == "p2p":

@@ -14,9 +14,11 @@ Needs at least two GPUs (skipped otherwise).  Each rank
 * checks the one-shot NVLink collectives (q35cu_p2p_*): exact on integer
   data, bit-identical to NCCL (at two ranks a sum has one order), correct
   across CUDA-graph replays (their sequence numbers live on the device);
-* runs two layers of the decode-step harness with both schemes on both
-  collective backends and checks that the replicated outputs agree bit for
-  bit across ranks and between the backends.
+* runs two layers of the decode-step harness with both schemes on the three
+  collective backends (NCCL, the one-shot peer-memory kernels, and the
+  exchange fused into the GEMV epilogue, q35cu_multi_fp8_tp) and checks that
+  the replicated outputs agree bit for bit across ranks and between the
+  backends, and that the fused all-gather fills the same gathered buffers.
 
 The shard layout and combination rules follow the reference's projections
 (qwen35-c/src/q35_model.c: q/k/v/z/gate/up produce rows, o/out/down reduce
@@ -161,7 +163,7 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     st = stack.Stack(rank, world, n_layers=2, scheme="literal")
     st.x.copy_(torch.randn(st.x.shape, generator=torch.Generator().manual_seed(5)).cuda())
     outs = {}
-    for coll in ("nccl", "p2p"):
+    for coll in ("nccl", "p2p", "fused"):
         st.coll = coll
         for scheme in ("literal", "paired"):
             st.scheme = scheme
@@ -174,6 +176,17 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             rep[f"stack_{coll}_{scheme}_replicated"] = all(torch.equal(ys[0], t) for t in ys)
             outs[(coll, scheme)] = y.cpu()
     rep["stack_p2p_equals_nccl"] = all(torch.equal(outs[("nccl", sc)], outs[("p2p", sc)]) for sc in ("literal", "paired"))
+    rep["stack_fused_equals_p2p"] = all(torch.equal(outs[("fused", sc)], outs[("p2p", sc)]) for sc in ("literal", "paired"))
+    # the fused all-gather fills the same gathered buffers as the collective
+    st.coll, st.scheme = "p2p", "literal"
+    st.step()
+    g_p2p = (st.col_full.clone(), st.gu_full.clone())
+    st.coll = "fused"
+    st.col_full.zero_()
+    st.gu_full.zero_()
+    st.step()
+    torch.cuda.synchronize()
+    rep["fused_gather_equals_p2p"] = bool(torch.equal(g_p2p[0], st.col_full) and torch.equal(g_p2p[1], st.gu_full))
     st.free()
     status = q35cu.C.c_uint32(0)
     q35cu.check(q35cu.load().q35cu_device_status(q35cu.C.byref(status), 1))
@@ -203,11 +216,12 @@ def test_tp_two_gpus(tmp_path):
         assert rep["p2p_allreduce_exact"] and rep["p2p_allgather_exact"], rep
         assert rep["p2p_equals_nccl"] and rep["p2p_graph_replays"], rep
         assert rep["device_status"] == 0, rep
-        for coll in ("nccl", "p2p"):
+        for coll in ("nccl", "p2p", "fused"):
             for scheme in ("literal", "paired"):
                 key = f"stack_{coll}_{scheme}"
                 assert rep[key + "_finite"] and rep[key + "_replicated"], (key, rep)
         assert rep["stack_p2p_equals_nccl"], rep
+        assert rep["stack_fused_equals_p2p"] and rep["fused_gather_equals_p2p"], rep
     shapes = reps[0]["shapes"]
     assert len(shapes) == len(SHAPES)
     for e in shapes:

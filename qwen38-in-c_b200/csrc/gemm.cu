@@ -676,6 +676,12 @@ int gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m, floa
     return launch_gemm_fp8(w, xh, ts, m, Y, st);
 }
 
+uint32_t *gemm_status_word()
+{
+    void *p = nullptr;
+    return cudaGetSymbolAddress(&p, g_gemm_status) == cudaSuccess ? static_cast<uint32_t *>(p) : nullptr;
+}
+
 int gemm_status(uint32_t *status, bool clear)
 {
     Q35CU_CUDA(cudaMemcpyFromSymbol(status, g_gemm_status, 4));

@@ -991,6 +991,12 @@ int scan_nan_codes(const uint8_t *W, size_t bytes, uint32_t *d_flag, cudaStream_
     return Q35CU_OK;
 }
 
+uint32_t *device_status_word()
+{
+    void *p = nullptr;
+    return cudaGetSymbolAddress(&p, g_device_status) == cudaSuccess ? static_cast<uint32_t *>(p) : nullptr;
+}
+
 int device_status(uint32_t *status, bool clear)
 {
     Q35CU_CUDA(cudaMemcpyFromSymbol(status, g_device_status, 4));

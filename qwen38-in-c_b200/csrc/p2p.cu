@@ -139,6 +139,12 @@ bool p2p_view(P2PView *out)
     return true;
 }
 
+uint32_t *p2p_status_word()
+{
+    void *p = nullptr;
+    return cudaGetSymbolAddress(&p, g_p2p_status) == cudaSuccess ? static_cast<uint32_t *>(p) : nullptr;
+}
+
 int p2p_status(uint32_t *status, bool clear)
 {
     Q35CU_CUDA(cudaMemcpyFromSymbol(status, g_p2p_status, 4));

@@ -74,6 +74,12 @@ int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tsca
                     cudaStream_t st);
 int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
 int gemm_status(uint32_t *status, bool clear);
+// device addresses of the three status words (GEMV and generic kernels,
+// GEMM, peer-memory collectives) on the current device, for a host call that
+// reads them together with its output in one copy
+uint32_t *device_status_word();
+uint32_t *gemm_status_word();
+uint32_t *p2p_status_word();
 int p2p_status(uint32_t *status, bool clear);
 struct P2PView;
 // the mapped exchange areas of q35cu_p2p_open (false if not open)

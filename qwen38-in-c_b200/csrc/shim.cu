@@ -91,6 +91,7 @@ struct DevState {
     void *d_xbf = nullptr;    // GEMM workspace: prepared (f16) copy of a prefill activation batch
     size_t xbf_cap = 0;
     uint32_t *d_flag = nullptr;  // 4-byte scratch word for upload scans
+    uint32_t *status_src[3] = {nullptr, nullptr, nullptr};  // the status words (host_call)
 };
 
 struct Key {
@@ -779,6 +780,17 @@ uint32_t gemm_min_tokens()
     return v;
 }
 
+// the three status words, side by side (for host_call's single copy back)
+__global__ void gather_status_kernel(const uint32_t *a, const uint32_t *b, const uint32_t *c, uint32_t *dst)
+{
+    if (threadIdx.x == 0) {
+        dst[0] = *reinterpret_cast<const volatile uint32_t *>(a);
+        dst[1] = *reinterpret_cast<const volatile uint32_t *>(b);
+        dst[2] = *reinterpret_cast<const volatile uint32_t *>(c);
+        dst[3] = 0;
+    }
+}
+
 // a bounded device-side wait that gave up leaves a code in the status word
 int check_device_status()
 {
@@ -790,14 +802,25 @@ int check_device_status()
 }
 
 // stage X in, run `fn` (which launches on d->stream into the device output
-// region), stage Y out.  in_bytes / out_bytes are exact byte counts.
+// region), stage Y out.  in_bytes / out_bytes are exact byte counts.  The
+// three device status words travel back behind the output in the same copy
+// (one tiny kernel gathers them), so a call costs one H2D, one D2H and one
+// synchronisation; they are cleared only when one is set.
 template <class F>
 int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
 {
     DevState *d = dev_state();
     if (!d) return t_err;
+    if (!d->status_src[0]) {
+        d->status_src[0] = device_status_word();
+        d->status_src[1] = gemm_status_word();
+        d->status_src[2] = p2p_status_word();
+        if (!d->status_src[0] || !d->status_src[1] || !d->status_src[2])
+            return set_error(Q35CU_ERR_CUDA, "status words not found");
+    }
     const size_t in_al = (in_bytes + 255) & ~(size_t)255;
-    int rc = ensure_stage(d, in_al + out_bytes);
+    const size_t out_al = (out_bytes + 15) & ~(size_t)15;
+    int rc = ensure_stage(d, in_al + out_al + 16);
     if (rc) return rc;
     char *h = static_cast<char *>(d->h_stage);
     char *dv = static_cast<char *>(d->d_stage);
@@ -805,10 +828,17 @@ int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
     Q35CU_CUDA(cudaMemcpyAsync(dv, h, in_bytes, cudaMemcpyHostToDevice, d->stream));
     rc = fn(reinterpret_cast<const float *>(dv), reinterpret_cast<float *>(dv + in_al), d->stream);
     if (rc) return rc;
-    Q35CU_CUDA(cudaMemcpyAsync(h + in_al, dv + in_al, out_bytes, cudaMemcpyDeviceToHost, d->stream));
+    uint32_t *st_dev = reinterpret_cast<uint32_t *>(dv + in_al + out_al);
+    gather_status_kernel<<<1, 32, 0, d->stream>>>(d->status_src[0], d->status_src[1], d->status_src[2], st_dev);
+    count_launch();
+    Q35CU_CUDA(cudaGetLastError());
+    Q35CU_CUDA(cudaMemcpyAsync(h + in_al, dv + in_al, out_al + 16, cudaMemcpyDeviceToHost, d->stream));
     Q35CU_CUDA(cudaStreamSynchronize(d->stream));
-    rc = check_device_status();
-    if (rc) return rc;
+    const uint32_t *st = reinterpret_cast<const uint32_t *>(h + in_al + out_al);
+    if (st[0] | st[1] | st[2]) {
+        rc = check_device_status();  // reads and clears all three
+        if (rc) return rc;
+    }
     memcpy(Y, h + in_al, out_bytes);
     return Q35CU_OK;
 }

@@ -202,6 +202,25 @@ int q35cu_multi_fp8_tp(const q35cu_weight *const w[4], const float *X, float *co
                        float *gathered, void *stream);
 int q35cu_gemv_fp8_tp(const q35cu_weight *w, const float *X, float *Y, int mode, float *gathered, void *stream);
 
+/* A decode chain: a fixed sequence of one-token decode GEMVs (each up to four
+ * weights sharing X, optionally with the fused tensor-parallel exchange
+ * above) run by one cooperative kernel launch.  The CTAs stay resident across
+ * the ops and wait on a grid barrier before each op after the first -- with
+ * that op's first weights already in flight -- so no launch ramp or tail
+ * separates two projections.  Ops run in the order added; op k may read what
+ * ops < k wrote.  X and Y are device pointers fixed when the op is added
+ * (their contents may change between runs).  The first run lays out and
+ * uploads the op table (synchronously): make it before any stream capture;
+ * later runs are a single asynchronous launch and may be captured.  The
+ * reference has no counterpart: it calls q35_mm_fp8 / _multi4 per projection
+ * from its layer code (qwen35-c/src/q35_model.c, q35_deltanet.c, q35_attn.c). */
+typedef struct q35cu_chain q35cu_chain;
+int q35cu_chain_create(q35cu_chain **out);
+int q35cu_chain_add(q35cu_chain *c, const q35cu_weight *const w[4], const float *X, float *const Y[4], int mode,
+                    float *gathered);
+int q35cu_chain_run(q35cu_chain *c, void *stream);
+void q35cu_chain_free(q35cu_chain *c);
+
 /* ---- info --------------------------------------------------------------- */
 const char *q35cu_build_info(void);
 /* Kernel launches this library issued since load (all entry points). */

@@ -49,6 +49,7 @@
 // the copies it has in flight before the CTA exits.
 #include <cuda_fp16.h>
 
+#include <cstring>
 #include <type_traits>
 
 #include "p2p_ll.cuh"
@@ -461,11 +462,38 @@ __device__ __forceinline__ uint16_t f16_bits(float v)
     return h;
 }
 
-template <int MT>
-__global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_constant__ MArgs a)
+// Grid barrier of the chain kernel (all CTAs resident: cooperative launch).
+// Each CTA adds one arrival per barrier; barrier j completes when the count
+// reaches j * gridDim.x.  Bounded; a wait that gives up records
+// Q35CU_ERR_TIMEOUT and lets the CTA go on.
+__device__ __forceinline__ void chain_barrier(uint32_t *bar, uint32_t target)
 {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * a.ipr);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(bar, 1u);
+        uint32_t i = 0, v;
+        for (;;) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+            if (v >= target) break;
+            if (++i >= kSpinLimit) {
+                atomicExch(&g_device_status, (uint32_t)Q35CU_ERR_TIMEOUT);
+                break;
+            }
+            if (i > 16) __nanosleep(32);
+        }
+    }
+    __syncthreads();
+}
+
+// One decode GEMV, run by every CTA of the grid.  The standalone kernel waits
+// for the previous kernel with griddepcontrol.wait; the chain kernel (CHAIN)
+// waits on its grid barrier `bar` for the previous op instead (op > 0).  In
+// both, the CTA's first weight item is already in flight when it waits.
+template <int MT, bool CHAIN>
+__device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const MmaSmem &L, uint32_t *bar,
+                                          uint32_t op)
+{
     uint8_t *xs = smem + L.xs;                                    // [2*MT][xcol_bytes] f16 columns
     float *xmul = reinterpret_cast<float *>(smem + L.xmul);       // [MT][kblocks] 2^-e
     RowBlock *rbt = reinterpret_cast<RowBlock *>(smem + L.rbt);   // the CTA's row blocks
@@ -479,7 +507,7 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     const uint32_t vr1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.total_rows) / gridDim.x);
     const uint32_t tok0 = blockIdx.y * MT;
 
-    griddep_launch();
+    if (!CHAIN) griddep_launch();
     if (t == 0) {  // the CTA's 16-row blocks, cut at segment boundaries
         uint32_t n = 0;
         for (uint32_t vr = vr0; vr < vr1 && n < kMaxRowBlocks;) {
@@ -588,7 +616,10 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     float sa[4], sb[4];
     if (it < nitems) issue(va, sa, rbi, sp);  // weights only: before waiting on the previous kernel
 
-    griddep_wait();
+    if (!CHAIN)
+        griddep_wait();
+    else if (op > 0)
+        chain_barrier(bar, op * gridDim.x);
     // activation -> f16 hi/lo columns: one warp per (token, 128-column block);
     // a warp's blocks are loaded four at a time so their L2 round trips overlap
     for (uint32_t base = warp; base < MT * kbn; base += 4 * kM2Warps) {
@@ -698,6 +729,48 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
         }
         __syncthreads();
         if (t == 0) p2p_finish(a.p2p, tp_seq);
+    }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_constant__ MArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * a.ipr);
+    gemv_body<MT, false>(a, smem, L, nullptr, 0);
+}
+
+// A chain of one-token decode GEMVs in one cooperative launch: every CTA
+// walks the ops in order with a grid barrier before each op after the first,
+// so no launch ramp or tail separates two projections and each op's first
+// weights are in flight before the barrier.  The op descriptors live in
+// device memory; the shared-memory layout is the largest op's.
+struct ChainArgs {
+    const MArgs *ops;
+    uint32_t nops;
+    uint32_t *bar;     // [0] barrier count, [1] exit ticket; zero at launch, reset at exit
+    MmaSmem L;
+};
+
+__global__ void __launch_bounds__(kM2Threads, 1) gemv_chain_kernel(const __grid_constant__ ChainArgs c)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ MArgs op_s;
+    for (uint32_t k = 0; k < c.nops; ++k) {
+        __syncthreads();  // the previous op is done with op_s and shared memory
+        for (uint32_t i = threadIdx.x; i < sizeof(MArgs) / 4; i += kM2Threads)
+            reinterpret_cast<uint32_t *>(&op_s)[i] = reinterpret_cast<const uint32_t *>(c.ops + k)[i];
+        __syncthreads();
+        gemv_body<1, true>(op_s, smem, c.L, c.bar, k);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // the last CTA out resets the counters for the next launch
+        __threadfence();
+        if (atomicAdd(c.bar + 1, 1u) == gridDim.x - 1) {
+            c.bar[0] = 0;
+            c.bar[1] = 0;
+            __threadfence();
+        }
     }
 }
 
@@ -903,6 +976,118 @@ void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes)
     T = (T + 31) / 32 * 32;
     *threads = T;
     *passes = P;
+}
+
+// ---- the decode chain (host side) -----------------------------------------
+size_t chain_op_bytes() { return sizeof(MArgs); }
+
+// one op of a chain: the launch arguments of launch_gemv_mma for one token,
+// with the grid fixed at one CTA per SM (rb_round is set by chain_layout)
+int chain_build_op(const GemvSeg *segs_in, int nseg, const float *X, uint32_t K, const GemvTp &tp, void *out)
+{
+    if (nseg < 1 || nseg > 4 || !X || K == 0) return set_error(Q35CU_ERR_ARG, "chain: bad op");
+    if (K % 128 || (uintptr_t)X % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "chain: cols %u (needs a multiple of 128)", K);
+    MArgs a{};
+    uint32_t vb = 0;
+    for (int s = 0; s < nseg; ++s) {
+        const GemvSeg &g = segs_in[s];
+        if ((uintptr_t)g.W % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "chain: misaligned weight");
+        a.seg[s] = Seg{g.W, g.S, g.Y, g.rows, g.ldy, vb, g.has_nan};
+        vb += g.rows;
+    }
+    a.X = X;
+    a.K = K;
+    a.ldx = K;
+    a.m = 1;
+    a.kblocks = K / 128;
+    a.total_rows = vb;
+    a.nseg = nseg;
+    a.xcol_bytes = 2 * K + 32;
+    a.ipr = (K + kItemCols - 1) / kItemCols;
+    a.tp_mode = tp.mode;
+    a.gathered = tp.gathered;
+    if (tp.mode) {
+        if (!p2p_view(&a.p2p)) return set_error(Q35CU_ERR_NCCL, "chain: p2p collectives not open");
+        if (vb > kP2PMaxElems) return set_error(Q35CU_ERR_UNSUPPORTED, "chain: %u rows exceed the exchange area", vb);
+        if (tp.mode == 2 && !tp.gathered) return set_error(Q35CU_ERR_ARG, "chain: all-gather needs a destination");
+    }
+    const uint32_t sms = (uint32_t)device_sms();
+    const uint32_t rows_cta = (vb + sms - 1) / sms;
+    if ((rows_cta + 15) / 16 + 2 * (uint32_t)nseg > kMaxRowBlocks) return set_error(Q35CU_ERR_UNSUPPORTED, "chain: rows");
+    memcpy(out, &a, sizeof(a));
+    return Q35CU_OK;
+}
+
+// the shared-memory layout every op of the chain fits in; sets each op's
+// rows-per-round.  layout_out: {xs, xmul, rbt, part, total} bytes.
+int chain_layout(void *ops, uint32_t nops, uint32_t layout_out[5])
+{
+    MArgs *o = static_cast<MArgs *>(ops);
+    uint32_t xcol = 0, kb = 0, ipr_max = 0;
+    for (uint32_t i = 0; i < nops; ++i) {
+        xcol = o[i].xcol_bytes > xcol ? o[i].xcol_bytes : xcol;
+        kb = o[i].kblocks > kb ? o[i].kblocks : kb;
+        ipr_max = o[i].ipr > ipr_max ? o[i].ipr : ipr_max;
+    }
+    // Shared memory is sized to what the ops need, not to the budget: every
+    // byte above that is taken from L1, which holds the weight loads in flight.
+    const uint32_t budget = 216 * 1024;
+    MmaSmem L = mma_smem_layout(1, xcol, kb, 0);
+    if (L.part + ipr_max * 16 * 4 > budget) return set_error(Q35CU_ERR_UNSUPPORTED, "chain: cols too large");
+    const uint32_t sms = (uint32_t)device_sms();
+    uint32_t need = 0;  // partial slots for every op to run in one round
+    for (uint32_t i = 0; i < nops; ++i) {
+        const uint32_t rows_cta = (o[i].total_rows + sms - 1) / sms;
+        const uint32_t nrb_max = (rows_cta + 15) / 16 + 2 * (uint32_t)o[i].nseg;
+        need = nrb_max * o[i].ipr > need ? nrb_max * o[i].ipr : need;
+    }
+    const uint32_t cap = (budget - L.part) / (16 * 4);
+    const uint32_t slots = need < cap ? need : cap;
+    for (uint32_t i = 0; i < nops; ++i) {
+        const uint32_t rows_cta = (o[i].total_rows + sms - 1) / sms;
+        const uint32_t nrb_max = (rows_cta + 15) / 16 + 2 * (uint32_t)o[i].nseg;
+        uint32_t rbr = slots / o[i].ipr;
+        rbr = rbr < 1 ? 1 : (rbr > nrb_max ? nrb_max : rbr);
+        o[i].rb_round = rbr;
+    }
+    L.total = L.part + slots * 16 * 4;
+    layout_out[0] = L.xs;
+    layout_out[1] = L.xmul;
+    layout_out[2] = L.rbt;
+    layout_out[3] = L.part;
+    layout_out[4] = L.total;
+    return Q35CU_OK;
+}
+
+int launch_chain(const void *d_ops, uint32_t nops, uint32_t *d_bar, const uint32_t layout[5], cudaStream_t st)
+{
+    if (!nops) return Q35CU_OK;
+    static bool configured[64] = {};
+    int dev = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
+    if (!configured[dev]) {
+        Q35CU_CUDA(cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
+        configured[dev] = true;
+    }
+    ChainArgs c{};
+    c.ops = static_cast<const MArgs *>(d_ops);
+    c.nops = nops;
+    c.bar = d_bar;
+    c.L = MmaSmem{layout[0], layout[1], layout[2], layout[3], layout[4]};
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)device_sms());
+    cfg.blockDim = dim3(kM2Threads);
+    cfg.dynamicSmemBytes = layout[4];
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid barrier cannot wait on an unscheduled CTA
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q35CU_CUDA(cudaLaunchKernelEx(&cfg, gemv_chain_kernel, c));
+    count_launch();
+    return Q35CU_OK;
 }
 
 int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint32_t K, uint32_t ldx, uint32_t m,

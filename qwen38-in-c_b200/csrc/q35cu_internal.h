@@ -59,6 +59,11 @@ struct GemvTp {
 };
 int launch_gemv(int kind, const GemvSeg *segs, int nseg, const float *X,
                 uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st, const GemvTp &tp = GemvTp{});
+// the decode chain: op descriptors are opaque bytes (chain_op_bytes each)
+size_t chain_op_bytes();
+int chain_build_op(const GemvSeg *segs, int nseg, const float *X, uint32_t K, const GemvTp &tp, void *out);
+int chain_layout(void *ops, uint32_t nops, uint32_t layout_out[5]);
+int launch_chain(const void *d_ops, uint32_t nops, uint32_t *d_bar, const uint32_t layout[5], cudaStream_t st);
 int launch_swiglu(const float *g, const float *u, float *o, size_t n, cudaStream_t st);
 void gemv_geometry(int kind, uint32_t K, uint32_t *threads, uint32_t *passes);
 int device_status(uint32_t *status, bool clear);

@@ -667,6 +667,105 @@ Q35_API int q35cu_multi_fp8_tp(const q35cu_weight *const w[4], const float *X, f
     return launch_gemv(0, segs, n, X, K, K, 1, pick(stream), tp);
 }
 
+struct q35cu_chain {
+    std::vector<uint8_t> ops;  // chain_op_bytes() per op
+    uint32_t n = 0;
+    void *d_ops = nullptr;
+    size_t d_cap = 0;
+    uint32_t *d_bar = nullptr;
+    uint32_t layout[5] = {};
+    bool dirty = true;
+    int device = -1;
+};
+
+Q35_API int q35cu_chain_create(q35cu_chain **out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!out) return set_error(Q35CU_ERR_ARG, "chain_create: NULL");
+    *out = nullptr;
+    if (!dev_state()) return t_err;
+    q35cu_chain *c = new (std::nothrow) q35cu_chain;
+    if (!c) return set_error(Q35CU_ERR_NOMEM, "chain_create");
+    c->device = g_device;
+    *out = c;
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_chain_add(q35cu_chain *c, const q35cu_weight *const w[4], const float *X, float *const Y[4],
+                            int mode, float *gathered)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!c || !w || !X || !Y) return set_error(Q35CU_ERR_ARG, "chain_add: bad arguments");
+    if (mode != 0 && mode != Q35CU_TP_ALLREDUCE && mode != Q35CU_TP_ALLGATHER)
+        return set_error(Q35CU_ERR_ARG, "chain_add: mode %d", mode);
+    if (!dev_state()) return t_err;
+    if (g_device != c->device) return set_error(Q35CU_ERR_ARG, "chain_add: chain belongs to device %d", c->device);
+    GemvSeg segs[4];
+    int n = 0;
+    uint32_t K = 0;
+    for (int s = 0; s < 4; ++s) {
+        if (!w[s]) continue;
+        if (w[s]->kind != 0 || !Y[s]) return set_error(Q35CU_ERR_ARG, "chain_add: segment %d", s);
+        if (K && w[s]->cols != K) return set_error(Q35CU_ERR_ARG, "chain_add: segments disagree on cols");
+        K = w[s]->cols;
+        segs[n++] = seg_of(w[s], Y[s], w[s]->rows);
+    }
+    if (!n) return set_error(Q35CU_ERR_ARG, "chain_add: no weight");
+    GemvTp tp;
+    tp.mode = mode;
+    tp.gathered = gathered;
+    const size_t ob = chain_op_bytes();
+    c->ops.resize((size_t)(c->n + 1) * ob);
+    const int rc = chain_build_op(segs, n, X, K, tp, c->ops.data() + (size_t)c->n * ob);
+    if (rc) {
+        c->ops.resize((size_t)c->n * ob);
+        return rc;
+    }
+    ++c->n;
+    c->dirty = true;
+    return Q35CU_OK;
+}
+
+Q35_API int q35cu_chain_run(q35cu_chain *c, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!c) return set_error(Q35CU_ERR_ARG, "chain_run: NULL");
+    if (!dev_state()) return t_err;
+    if (g_device != c->device) return set_error(Q35CU_ERR_ARG, "chain_run: chain belongs to device %d", c->device);
+    if (!c->n) return Q35CU_OK;
+    if (c->dirty) {  // lay out and upload the op table (synchronous: not inside a stream capture)
+        int rc = chain_layout(c->ops.data(), c->n, c->layout);
+        if (rc) return rc;
+        if (c->ops.size() > c->d_cap) {
+            if (c->d_ops) dev_free(c->d_ops, c->d_cap);
+            c->d_ops = nullptr;
+            c->d_cap = 0;
+            rc = dev_alloc(&c->d_ops, c->ops.size());
+            if (rc) return rc;
+            c->d_cap = c->ops.size();
+        }
+        if (!c->d_bar) {
+            void *p = nullptr;
+            rc = dev_alloc(&p, 256);
+            if (rc) return rc;
+            c->d_bar = static_cast<uint32_t *>(p);
+            Q35CU_CUDA(cudaMemset(c->d_bar, 0, 256));
+        }
+        Q35CU_CUDA(cudaMemcpy(c->d_ops, c->ops.data(), c->ops.size(), cudaMemcpyHostToDevice));
+        c->dirty = false;
+    }
+    return launch_chain(c->d_ops, c->n, c->d_bar, c->layout, pick(stream));
+}
+
+Q35_API void q35cu_chain_free(q35cu_chain *c)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!c) return;
+    if (c->d_ops) dev_free(c->d_ops, c->d_cap);
+    if (c->d_bar) dev_free(c->d_bar, 256);
+    delete c;
+}
+
 Q35_API int q35cu_gemv_fp8_tp(const q35cu_weight *w, const float *X, float *Y, int mode, float *gathered,
                               void *stream)
 {

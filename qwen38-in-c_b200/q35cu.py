@@ -97,6 +97,10 @@ _SIGS = [
     ("q35cu_p2p_allgather_f32", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_multi_fp8_tp", C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp]),
     ("q35cu_gemv_fp8_tp", C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp]),
+    ("q35cu_chain_create", C.c_int, [C.POINTER(_vp)]),
+    ("q35cu_chain_add", C.c_int, [_vp, _vp, _vp, _vp, C.c_int, _vp]),
+    ("q35cu_chain_run", C.c_int, [_vp, _vp]),
+    ("q35cu_chain_free", None, [_vp]),
     ("q35cu_build_info", C.c_char_p, []),
     ("q35cu_launch_count", C.c_uint64, []),
     ("q35cu_device_status", C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
@@ -412,6 +416,31 @@ def multi_tp(ws, X, Ys, mode: int, gathered=None, stream=None) -> None:
 
 def gemv_tp(w, X, Y, mode: int, gathered=None, stream=None) -> None:
     multi_tp([w], X, [Y], mode, gathered, stream)
+
+
+class Chain:
+    """A decode chain (q35cu_chain_*): one-token GEMVs run by one cooperative launch."""
+
+    def __init__(self):
+        self.h = _vp()
+        check(load().q35cu_chain_create(C.byref(self.h)))
+        self._keep = []
+
+    def add(self, ws, X, Ys, mode: int = 0, gathered=None) -> None:
+        ws = list(ws) + [None] * (4 - len(ws))
+        Ys = list(Ys) + [None] * (4 - len(Ys))
+        wp = (_vp * 4)(*[None if w is None else w.h.value for w in ws])
+        yp = (_vp * 4)(*[None if y is None else _ptr(y) for y in Ys])
+        self._keep.append((X, Ys, gathered))
+        check(load().q35cu_chain_add(self.h, wp, _ptr(X), yp, mode, None if gathered is None else _ptr(gathered)))
+
+    def run(self, stream=None) -> None:
+        check(load().q35cu_chain_run(self.h, _stream(stream)))
+
+    def free(self) -> None:
+        if self.h:
+            load().q35cu_chain_free(self.h)
+            self.h = _vp()
 
 
 def declared_symbols() -> list[str]:

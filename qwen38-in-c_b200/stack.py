@@ -196,6 +196,41 @@ class Stack:
                 if self.world > 1:
                     self._allreduce(self.y[i], stream)
 
+    # -- the same step as one decode chain (q35cu_chain_*) -------------------
+    def build_chain(self, scheme: str | None = None):
+        """A q35cu.Chain with the ops of step() (TP exchanges fused into the
+        GEMV epilogues when world > 1)."""
+        scheme = scheme or self.scheme
+        literal = scheme == "literal" and self.world > 1
+        tp = self.world > 1
+        ch = q35cu.Chain()
+        for i, L in enumerate(self.layers):
+            outs, off = [], 0
+            for p in L.col_in:
+                n = p.window[1]
+                outs.append(self.col_local[off:off + n])
+                off += n
+            ch.add([p.w for p in L.col_in], self.x[i], outs,
+                   q35cu.TP_ALLGATHER if literal else 0, self.col_full if literal else None)
+            ao = L.attn_out
+            src = outs[-1] if L.kind == "dn" else outs[0]
+            ch.add([ao.w], src[:ao.window[3]], [self.o_buf], q35cu.TP_ALLREDUCE if tp else 0)
+            g_n = L.gate.window[1]
+            gu = [self.gu_local[:g_n], self.gu_local[g_n:2 * g_n]]
+            ch.add([L.gate.w, L.up.w], self.o_buf, gu,
+                   q35cu.TP_ALLGATHER if literal else 0, self.gu_full if literal else None)
+            ch.add([L.down.w], self.gu_local[:g_n], [self.y[i]], q35cu.TP_ALLREDUCE if tp else 0)
+        return ch
+
+    def step_chain(self, stream=None) -> None:
+        """step() as one cooperative launch (the chain is built on first use)."""
+        if not hasattr(self, "_chains"):
+            self._chains = {}
+        ch = self._chains.get(self.scheme)
+        if ch is None:
+            ch = self._chains[self.scheme] = self.build_chain(self.scheme)
+        ch.run(stream)
+
     def _allreduce(self, buf, stream) -> None:
         if self.coll == "p2p":
             q35cu.p2p_allreduce(buf, stream=stream)
@@ -215,6 +250,9 @@ class Stack:
         return self.n_layers * per_layer_k, self.n_layers * per_layer_c
 
     def free(self) -> None:
+        for ch in getattr(self, "_chains", {}).values():
+            ch.free()
+        self._chains = {}
         for w in self.weights:
             w.free()
         self.weights = []

@@ -354,6 +354,94 @@ def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
             "by_projection": per}
 
 
+def time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, m=8192, reps=3):
+    """Configuration 4: long prefill (M=8192 tokens) through the 64-layer
+    projection set under tensor parallelism, on this stack's shards.  Literal
+    scheme: column-parallel GEMMs + NCCL all-gather of their [M, N/p] outputs,
+    row-parallel GEMMs + NCCL all-reduce of the [M, 5120] partials (100+ MB
+    messages: NCCL's regime).  One DeltaNet and one GQA layer are timed (CUDA
+    events, median of `reps`, max over ranks) and extrapolated x48 / x16; the
+    activations are bf16-rounded N(0,1), converted by the library."""
+    import stack
+
+    dn = next(L for L in st.layers if L.kind == "dn")
+    gqa = next(L for L in st.layers if L.kind == "gqa")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    f32 = dict(dtype=torch.float32, device=dev)
+    x = torch.randn((m, stack.HIDDEN), device=dev).to(torch.bfloat16)
+    kmax = max(stack.HIDDEN, dn.down.window[3], dn.attn_out.window[3])
+    work = torch.empty(q35cu.gemm_workspace_bytes(m, kmax), dtype=torch.uint8, device=dev)
+    xb = torch.empty((m * kmax,), dtype=torch.bfloat16, device=dev)
+    o = torch.empty((m, stack.HIDDEN), **f32)
+    y = torch.empty((m, stack.HIDDEN), **f32)
+    col = {p.name: torch.empty((m, p.window[1]), **f32) for L in (dn, gqa) for p in L.col_in}
+    gath = {k: torch.empty((world * v.numel(),), **f32) for k, v in col.items()} if world > 1 else {}
+    g_n = dn.gate.window[1]
+    gu = {n: torch.empty((m, g_n), **f32) for n in ("gate", "up")}
+    gu_g = {n: torch.empty((world * m * g_n,), **f32) for n in gu} if world > 1 else {}
+    attn = torch.randn((m, gqa.attn_out.window[3]), **f32)  # stands in for the local heads' attention output
+
+    def bf16(src):
+        n = src.numel()
+        q35cu.f32_to_bf16(src, xb[:n])
+        return xb[:n].view(src.shape[0], -1)
+
+    def gemm(w, xin, yout):
+        q35cu.gemm(w, xin.view(torch.int16), yout, work)
+
+    def layer(L):
+        for p in L.col_in:
+            gemm(p.w, x, col[p.name])
+            if world > 1:
+                q35cu.allgather(col[p.name], gath[p.name])
+        src = col["z"] if L.kind == "dn" else attn
+        gemm(L.attn_out.w, bf16(src), o)
+        if world > 1:
+            q35cu.allreduce(o)
+        xo = bf16(o)
+        gemm(L.gate.w, xo, gu["gate"])
+        gemm(L.up.w, xo, gu["up"])
+        if world > 1:
+            for n in ("gate", "up"):
+                q35cu.allgather(gu[n], gu_g[n])
+        gemm(L.down.w, bf16(gu["gate"]), y)
+        if world > 1:
+            q35cu.allreduce(y)
+
+    def flops(L):
+        return 2.0 * m * sum(p.window[1] * p.window[3] for p in L.col_in + [L.attn_out, L.gate, L.up, L.down])
+
+    out = {}
+    for name, L in (("dn", dn), ("gqa", gqa)):
+        layer(L)  # warm-up
+        torch.cuda.synchronize()
+        barrier()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            layer(L)
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        barrier()
+        out[name] = max_over_ranks(statistics.median(ts))
+        out[name + "_flops_rank"] = flops(L)
+    n_dn = sum(1 for L in st.layers if L.kind == "dn")
+    n_gqa = len(st.layers) - n_dn
+    ms = n_dn * out["dn"] + n_gqa * out["gqa"]
+    total_flops = 2.0 * m * stack.weight_bytes(len(st.layers))  # every rank's shards: the whole model
+    rank_flops = n_dn * out["dn_flops_rank"] + n_gqa * out["gqa_flops_rank"]
+    return {"m": m, "ms_per_pass_extrapolated": round(ms, 2), "tflop_per_pass": round(total_flops / 1e12, 1),
+            "TFLOPs": round(total_flops / (ms * 1e-3) / 1e12, 1),
+            "per_gpu_TFLOPs": round(rank_flops / (ms * 1e-3) / 1e12, 1),
+            "frac_per_gpu": round(rank_flops / (ms * 1e-3) / 1e12 / bf16_peak, 4),
+            "ms_per_layer": {"deltanet": round(out["dn"], 3), "gqa": round(out["gqa"], 3)},
+            "sample": "one DeltaNet + one GQA layer timed (median of 3, max over ranks), x%d / x%d" % (n_dn, n_gqa),
+            "collectives": "NCCL all-gather after column-parallel, all-reduce after row-parallel" if world > 1
+            else "none"}
+
+
 def stack_max_cols(st):
     return max(max(p.w.cols for p in L.col_in + [L.attn_out, L.gate, L.up, L.down]) for L in st.layers)
 
@@ -594,6 +682,10 @@ def run_ours(args):
                     traffic = round(float(line.split("|")[2].split()[0]) * bytes_per_launch)
 
     extras = {}
+    if not args.no_extras:  # every rank takes part (collectives)
+        c4 = time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak)
+        if rank == 0:
+            extras["config4_prefill"] = c4
     if rank == 0 and world == 1 and not args.no_extras:
         extras["config0_gemv"] = time_gemv_rotating(q35cu, torch, 17408, 5120, 1)
         sweep = []

@@ -354,7 +354,7 @@ def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
             "by_projection": per}
 
 
-def time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, m=8192, reps=3):
+def time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, m=8192, reps=3, scheme="literal"):
     """Configuration 4: long prefill (M=8192 tokens) through the 64-layer
     projection set under tensor parallelism, on this stack's shards.  Literal
     scheme: column-parallel GEMMs + NCCL all-gather of their [M, N/p] outputs,
@@ -389,10 +389,12 @@ def time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, m=
     def gemm(w, xin, yout):
         q35cu.gemm(w, xin.view(torch.int16), yout, work)
 
+    literal = scheme == "literal"
+
     def layer(L):
         for p in L.col_in:
             gemm(p.w, x, col[p.name])
-            if world > 1:
+            if world > 1 and literal:
                 q35cu.allgather(col[p.name], gath[p.name])
         src = col["z"] if L.kind == "dn" else attn
         gemm(L.attn_out.w, bf16(src), o)
@@ -401,7 +403,7 @@ def time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, m=
         xo = bf16(o)
         gemm(L.gate.w, xo, gu["gate"])
         gemm(L.up.w, xo, gu["up"])
-        if world > 1:
+        if world > 1 and literal:
             for n in ("gate", "up"):
                 q35cu.allgather(gu[n], gu_g[n])
         gemm(L.down.w, bf16(gu["gate"]), y)
@@ -438,8 +440,9 @@ def time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, m=
             "frac_per_gpu": round(rank_flops / (ms * 1e-3) / 1e12 / bf16_peak, 4),
             "ms_per_layer": {"deltanet": round(out["dn"], 3), "gqa": round(out["gqa"], 3)},
             "sample": "one DeltaNet + one GQA layer timed (median of 3, max over ranks), x%d / x%d" % (n_dn, n_gqa),
-            "collectives": "NCCL all-gather after column-parallel, all-reduce after row-parallel" if world > 1
-            else "none"}
+            "collectives": ("none" if world == 1 else
+                            "NCCL all-gather after column-parallel, all-reduce after row-parallel" if literal else
+                            "NCCL all-reduce after row-parallel (Megatron pairing: no all-gather)")}
 
 
 def stack_max_cols(st):
@@ -684,6 +687,8 @@ def run_ours(args):
     extras = {}
     if not args.no_extras:  # every rank takes part (collectives)
         c4 = time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak)
+        if world > 1:
+            c4["paired"] = time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, scheme="paired")
         if rank == 0:
             extras["config4_prefill"] = c4
     if rank == 0 and world == 1 and not args.no_extras:

@@ -226,20 +226,31 @@ def gemv_bytes(rows, cols, m=1):
     return rows * cols + 4 * ((rows + 127) // 128) * ((cols + 127) // 128) + 4 * m * (rows + cols)
 
 
-def time_gemv_rotating(q35cu, torch, rows, cols, m, copies=5, rounds=20):
-    """Isolated GEMV: `copies` distinct weights cycled so none is L2-resident."""
+def time_gemv_rotating(q35cu, torch, rows, cols, m, copies=5, rounds=20, path="gemv"):
+    """Isolated GEMV: `copies` distinct weights cycled so none is L2-resident.
+    path "gemv": the CUDA-core decode GEMV (q35cu_gemv_fp8); "tc": the tensor
+    cores with exact fp32 activations (q35cu_gemv_fp8_tc, the path
+    q35_mm_fp8_batch takes for 16..127 tokens)."""
     ws = [q35cu.Weight.synth_fp8(1000 + i, rows, cols) for i in range(copies)]
     try:
         X = torch.randn((m, cols), device="cuda")
         Y = torch.empty((m, rows), device="cuda")
+        work = torch.empty(q35cu.load().q35cu_gemv_fp8_tc_workspace_bytes(m, cols), dtype=torch.uint8, device="cuda")
+
+        def call(w):
+            if path == "tc":
+                q35cu.gemv_tc(w, X, Y, work)
+            else:
+                q35cu.gemv(w, X, Y, m)
+
         for w in ws:
-            q35cu.gemv(w, X, Y, m)
+            call(w)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(rounds):
             for w in ws:
-                q35cu.gemv(w, X, Y, m)
+                call(w)
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (rounds * copies)
@@ -247,7 +258,7 @@ def time_gemv_rotating(q35cu, torch, rows, cols, m, copies=5, rounds=20):
         for w in ws:
             w.free()
     b = gemv_bytes(rows, cols, m)
-    return {"rows": rows, "cols": cols, "m": m, "us": round(us, 2), "GBps": round(b / us / 1e3, 1),
+    return {"rows": rows, "cols": cols, "m": m, "path": path, "us": round(us, 2), "GBps": round(b / us / 1e3, 1),
             "TFLOPs": round(2 * m * rows * cols / us / 1e6, 3)}
 
 
@@ -697,6 +708,8 @@ def run_ours(args):
         for rows, cols in ((17408, 5120), (5120, 17408)):
             for m in (1, 4, 16, 64):
                 sweep.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10))
+                if m >= 16:  # what q35_mm_fp8_batch runs at this size
+                    sweep.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10, path="tc"))
         extras["config1_sweep"] = sweep
         extras["config2_prefill"] = time_prefill_c2(q35cu, torch, bf16_peak)
 

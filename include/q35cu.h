@@ -143,6 +143,18 @@ int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m,
 #define Q35CU_NOALLOC_MAX_ACTS (8u << 20)
 int q35cu_gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m,
                                float *Y, void *stream);
+/* Multi-token decode on the tensor cores with exact fp32 activations: Y [m,
+ * rows] = X [m, cols] fp32 times the dequantised weight.  Each token row is
+ * scaled by a power of two and split into two f16 rows (hi = f16(x), lo =
+ * f16(x - hi): about 22 bits of x), both multiplied on the tcgen05 GEMM, and
+ * summed in the epilogue; the weight streams once per 96 tokens instead of
+ * once per 4.  Meets the decode GEMV's per-element bound (guarded 1e-5) but
+ * is not bit-identical to q35cu_gemv_fp8.  q35_mm_fp8_batch uses it for
+ * batches of 16 (Q35CU_GEMV_TC_MIN_TOKENS) to 127 tokens.  cols % 16 == 0;
+ * workspace >= q35cu_gemv_fp8_tc_workspace_bytes(m, cols), 16-byte aligned. */
+size_t q35cu_gemv_fp8_tc_workspace_bytes(uint32_t m, uint32_t cols);
+int q35cu_gemv_fp8_tc(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
+                      size_t workspace_bytes, void *stream);
 /* fp32 -> bf16 (nearest even) conversion of n values. */
 int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream);
 /* y[rows] = W x for a bf16 weight (q35_mm_bf16). */

@@ -97,9 +97,10 @@ constexpr uint32_t kStageArrivals = 1 + kConvWarps + kEpiWarps;
 
 struct GemmArgs {
     const float *S;       // weight scales [ceil(N/128), kblocks]
-    const float *tscale;  // per token 2^e_t [m]
-    float *Y;             // [m, N] token-major
+    const float *tscale;  // per activation row 2^e_t [m]
+    float *Y;             // [m, N] token-major ([m / 2, N] when pair)
     uint32_t N, K, m, kblocks, mtiles, ntiles;
+    uint32_t pair;        // rows 2t, 2t+1 are the hi and lo halves of token t: Y[t] = their sum
 };
 
 struct Smem {  // offsets from the 1024-aligned base
@@ -431,10 +432,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sc = sc_next;
             }
             if (ok && n < a.N) {
+                if (a.pair) {  // t0 is even: columns (2i, 2i+1) are token (t0 + 2i) / 2's hi and lo
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const uint32_t tok = t0 + i;
-                    if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                    for (int i = 0; i < 32; ++i) {
+                        const uint32_t tok2 = t0 + 2 * i;
+                        if (tok2 < a.m)
+                            a.Y[(size_t)(tok2 >> 1) * a.N + n] = (acc[2 * i] + acc[2 * i + 1]) * __ldg(a.tscale + tok2);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        const uint32_t tok = t0 + i;
+                        if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                    }
                 }
             }
         }
@@ -506,6 +516,56 @@ __global__ void __launch_bounds__(kPrepThreads) gemm_prep_kernel(const void *X, 
     if (threadIdx.x == 0) tscale[row] = __uint_as_float((uint32_t)(127 + e) << 23);
 }
 
+// Exact fp32 activations on the tensor cores (the multi-token decode path):
+// each token row x (not rounded) is scaled by the power of two 2^-e that
+// puts its largest magnitude in [2^14, 2^15) and split into two f16 rows,
+// hi = f16(x 2^-e) and lo = f16(x 2^-e - hi) (the difference is exact in
+// fp32), so hi + lo carries x to about 22 bits (relative to each element
+// down to 2^-28 of the row's largest).  Rows 2t and 2t+1 of Xh; both carry
+// tscale = 2^e.
+__global__ void __launch_bounds__(kPrepThreads) gemm_prep_split_kernel(const float *X, uint32_t K, uint16_t *Xh,
+                                                                       float *tscale)
+{
+    __shared__ float red[kPrepThreads / 32];
+    const size_t row = blockIdx.x;
+    const uint32_t k4 = K / 4;
+    const float4 *x4 = reinterpret_cast<const float4 *>(X) + row * k4;
+    float mx = 0.f;
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = __ldg(x4 + i);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < kPrepThreads / 32; ++i) mx = fmaxf(mx, red[i]);
+    const int eb = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+    int e = 0;
+    if (eb == 0 && mx > 0.f) e = -112;
+    else if (eb > 0 && eb < 255) e = max(eb - 127 - 14, -112);
+    const float down = __uint_as_float((uint32_t)(127 - e) << 23);
+    uint2 *hi = reinterpret_cast<uint2 *>(Xh) + (2 * row) * k4;
+    uint2 *lo = hi + k4;
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = __ldg(x4 + i);
+        const float s[4] = {v.x * down, v.y * down, v.z * down, v.w * down};
+        __half h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            h[j] = __float2half_rn(s[j]);
+            l[j] = __float2half_rn(s[j] - __half2float(h[j]));
+        }
+        hi[i] = make_uint2(__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16),
+                           __half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16));
+        lo[i] = make_uint2(__half_as_ushort(l[0]) | ((uint32_t)__half_as_ushort(l[1]) << 16),
+                           __half_as_ushort(l[2]) | ((uint32_t)__half_as_ushort(l[3]) << 16));
+    }
+    if (threadIdx.x == 0) tscale[2 * row] = tscale[2 * row + 1] = __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -556,6 +616,28 @@ size_t gemm_workspace_bytes(uint32_t m, uint32_t K)
     return (((size_t)m * K * 2 + 255) & ~(size_t)255) + (size_t)m * 4;
 }
 
+size_t gemm_exact_workspace_bytes(uint32_t m, uint32_t K) { return gemm_workspace_bytes(2 * m, K); }
+
+// multi-token decode on the tensor cores with exact fp32 activations:
+// split prep (2m f16 rows) + the GEMM in pair mode
+int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
+                      cudaStream_t st)
+{
+    if (!m) return Q35CU_OK;
+    const uint32_t K = w->cols;
+    if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
+    if ((uintptr_t)X % 16 || (uintptr_t)workspace % 16)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned activations or workspace");
+    if ((uint64_t)m * 2 > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: too many tokens");
+    const size_t need = gemm_exact_workspace_bytes(m, K);
+    uint16_t *xh = static_cast<uint16_t *>(workspace);
+    float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + need - (size_t)2 * m * 4);
+    gemm_prep_split_kernel<<<m, kPrepThreads, 0, st>>>(X, K, xh, ts);
+    count_launch();
+    Q35CU_CUDA(cudaGetLastError());
+    return launch_gemm_fp8(w, xh, ts, 2 * m, Y, st, true);
+}
+
 int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *Xh, float *tscale,
                      cudaStream_t st)
 {
@@ -573,7 +655,7 @@ int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *
 }
 
 int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
-                    cudaStream_t st)
+                    cudaStream_t st, bool pair)
 {
     const uint32_t N = w->rows, K = w->cols;
     if (!m) return Q35CU_OK;
@@ -586,7 +668,7 @@ int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tsca
     if (rc) return rc;
     rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
     if (rc) return rc;
-    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles};
+    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, pair ? 1u : 0u};
     static bool configured[64] = {};
     int dev = 0, sms = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));

@@ -76,7 +76,11 @@ size_t gemm_workspace_bytes(uint32_t m, uint32_t K);
 int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *Xh, float *tscale,
                      cudaStream_t st);
 int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
-                    cudaStream_t st);
+                    cudaStream_t st, bool pair = false);
+// multi-token decode on the tensor cores, fp32 activations split hi/lo
+size_t gemm_exact_workspace_bytes(uint32_t m, uint32_t K);
+int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
+                      cudaStream_t st);
 int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
 int gemm_status(uint32_t *status, bool clear);
 // device addresses of the three status words (GEMV and generic kernels,

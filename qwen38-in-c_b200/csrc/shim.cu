@@ -775,6 +775,22 @@ Q35_API int q35cu_gemv_fp8_tp(const q35cu_weight *w, const float *X, float *Y, i
     return q35cu_multi_fp8_tp(ws, X, ys, mode, gathered, stream);
 }
 
+Q35_API size_t q35cu_gemv_fp8_tc_workspace_bytes(uint32_t m, uint32_t cols)
+{
+    return gemm_exact_workspace_bytes(m, cols);
+}
+
+Q35_API int q35cu_gemv_fp8_tc(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
+                              size_t workspace_bytes, void *stream)
+{
+    if (!w || w->kind != 0 || !X || !Y) return set_error(Q35CU_ERR_ARG, "gemv_fp8_tc: bad arguments");
+    if (!m) return Q35CU_OK;
+    const size_t need = gemm_exact_workspace_bytes(m, w->cols);
+    if (!workspace || workspace_bytes < need)
+        return set_error(Q35CU_ERR_ARG, "gemv_fp8_tc: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    return launch_gemm_exact(w, X, m, Y, workspace, pick(stream));
+}
+
 Q35_API size_t q35cu_gemm_fp8_workspace_bytes(uint32_t m, uint32_t cols)
 {
     return gemm_workspace_bytes(m, cols);
@@ -879,6 +895,21 @@ uint32_t gemm_min_tokens()
     return v;
 }
 
+// batches of at least this many (and fewer than gemm_min_tokens) tokens take
+// the tensor cores with exact fp32 activations (hi/lo split); smaller ones
+// stay on the decode GEMV, bit-identical to single calls
+// (Q35CU_GEMV_TC_MIN_TOKENS overrides; 0 disables)
+uint32_t gemv_tc_min_tokens()
+{
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("Q35CU_GEMV_TC_MIN_TOKENS");
+        v = e ? atoi(e) : 16;
+        if (v <= 0) v = 0x7FFFFFFF;
+    }
+    return (uint32_t)v;
+}
+
 // the three status words, side by side (for host_call's single copy back)
 __global__ void gather_status_kernel(const uint32_t *a, const uint32_t *b, const uint32_t *c, uint32_t *dst)
 {
@@ -976,11 +1007,14 @@ Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint
     if (!W || !scale_bf16 || !X) rc = set_error(Q35CU_ERR_ARG, "q35_mm_fp8_batch: NULL input");
     q35cu_weight *w = rc ? nullptr : cached_weight(0, W, scale_bf16, rows, cols);
     if (!rc && !w) rc = t_err;
-    // prefill-sized batches run the tensor-core GEMM on bf16-rounded activations
+    // prefill-sized batches run the tensor-core GEMM on bf16-rounded
+    // activations; multi-token decode batches run it on exact fp32
+    // activations split hi/lo
     const bool tc = n >= gemm_min_tokens() && cols % 16 == 0;
-    if (!rc && tc) {
+    const bool tc_exact = !tc && n >= gemv_tc_min_tokens() && cols % 16 == 0;
+    if (!rc && (tc || tc_exact)) {
         DevState *d = dev_state();
-        const size_t xb = gemm_workspace_bytes(n, cols);
+        const size_t xb = tc ? gemm_workspace_bytes(n, cols) : gemm_exact_workspace_bytes(n, cols);
         if (xb > d->xbf_cap) {
             if (d->d_xbf) dev_free(d->d_xbf, d->xbf_cap);
             d->d_xbf = nullptr;
@@ -998,6 +1032,10 @@ Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint
             int r = launch_gemm_prep(dx, true, n, cols, xh, ts, st);
             if (r) return r;
             return launch_gemm_fp8(w, xh, ts, n, dy, st);
+        });
+    else if (!rc && tc_exact)
+        rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
+            return launch_gemm_exact(w, dx, n, dy, dev_state()->d_xbf, st);
         });
     else if (!rc)
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {

@@ -75,6 +75,8 @@ _SIGS = [
     ("q35cu_gemv_fp8", C.c_int, [_vp, _vp, _u32, _u32, _vp, _u32, _vp]),
     ("q35cu_multi_fp8", C.c_int, [C.POINTER(_vp), _vp, _u32, _u32, C.POINTER(_vp), _vp]),
     ("q35cu_gemm_fp8_workspace_bytes", C.c_size_t, [_u32, _u32]),
+    ("q35cu_gemv_fp8_tc_workspace_bytes", C.c_size_t, [_u32, _u32]),
+    ("q35cu_gemv_fp8_tc", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8_f32_noalloc", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
     ("q35cu_f32_to_bf16", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
@@ -315,6 +317,18 @@ def gemm(w: Weight, Xb, Y, workspace=None, stream=None) -> None:
     assert workspace.numel() * workspace.element_size() >= need
     check(load().q35cu_gemm_fp8(w.h, _ptr(Xb), m, _ptr(Y), _ptr(workspace),
                                 workspace.numel() * workspace.element_size(), _stream(stream)))
+
+
+def gemv_tc(w: Weight, X, Y, workspace=None, stream=None) -> None:
+    """Multi-token decode on the tensor cores, exact fp32 activations (hi/lo split)."""
+    assert X.dtype.itemsize == 4 and X.is_contiguous() and Y.is_contiguous()
+    m = X.shape[0]
+    need = int(load().q35cu_gemv_fp8_tc_workspace_bytes(m, w.cols))
+    if workspace is None:
+        import torch
+        workspace = torch.empty(need, dtype=torch.uint8, device=X.device)
+    check(load().q35cu_gemv_fp8_tc(w.h, _ptr(X), m, _ptr(Y), _ptr(workspace),
+                                   workspace.numel() * workspace.element_size(), _stream(stream)))
 
 
 def f32_to_bf16(x, y, stream=None) -> None:

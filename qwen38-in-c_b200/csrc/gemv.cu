@@ -409,7 +409,7 @@ constexpr int kM2Threads = kM2Warps * 32;
 constexpr uint32_t kItemCols = 256;   // columns per work item
 constexpr uint32_t kMaxRowBlocks = 256;
 
-struct MArgs {
+struct alignas(16) MArgs {
     Seg seg[4];
     const float *X;
     uint32_t K, ldx, m, kblocks, total_rows;
@@ -462,16 +462,24 @@ __device__ __forceinline__ uint16_t f16_bits(float v)
     return h;
 }
 
-// Grid barrier of the chain kernel (all CTAs resident: cooperative launch).
-// Each CTA adds one arrival per barrier; barrier j completes when the count
-// reaches j * gridDim.x.  Bounded; a wait that gives up records
-// Q35CU_ERR_TIMEOUT and lets the CTA go on.
-__device__ __forceinline__ void chain_barrier(uint32_t *bar, uint32_t target)
+// Grid barrier of the chain kernel (all CTAs resident: cooperative launch),
+// split in two: a CTA arrives as soon as its outputs of an op are written and
+// waits only when it needs the next op's activation, after it has set up the
+// next op and put its first weights in flight.  Each CTA adds one arrival per
+// op boundary; boundary j is passed when the count reaches j * gridDim.x.
+// Bounded; a wait that gives up records Q35CU_ERR_TIMEOUT and lets the CTA
+// go on.
+__device__ __forceinline__ void chain_arrive(uint32_t *bar)
 {
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
         atomicAdd(bar, 1u);
+    }
+}
+__device__ __forceinline__ void chain_wait(uint32_t *bar, uint32_t target)
+{
+    if (threadIdx.x == 0) {
         uint32_t i = 0, v;
         for (;;) {
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
@@ -480,7 +488,7 @@ __device__ __forceinline__ void chain_barrier(uint32_t *bar, uint32_t target)
                 atomicExch(&g_device_status, (uint32_t)Q35CU_ERR_TIMEOUT);
                 break;
             }
-            if (i > 16) __nanosleep(32);
+            if (i > 2048) __nanosleep(32);
         }
     }
     __syncthreads();
@@ -488,17 +496,17 @@ __device__ __forceinline__ void chain_barrier(uint32_t *bar, uint32_t target)
 
 // One decode GEMV, run by every CTA of the grid.  The standalone kernel waits
 // for the previous kernel with griddepcontrol.wait; the chain kernel (CHAIN)
-// waits on its grid barrier `bar` for the previous op instead (op > 0).  In
-// both, the CTA's first weight item is already in flight when it waits.
+// waits on its grid barrier `bar` for the previous op instead (op > 0) and
+// arrives for the next one when its outputs are written (last == false).  In
+// both, the warps' first two weight items are in flight when they wait.
 template <int MT, bool CHAIN>
 __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const MmaSmem &L, uint32_t *bar,
-                                          uint32_t op)
+                                          uint32_t op, bool last = true)
 {
     uint8_t *xs = smem + L.xs;                                    // [2*MT][xcol_bytes] f16 columns
     float *xmul = reinterpret_cast<float *>(smem + L.xmul);       // [MT][kblocks] 2^-e
     RowBlock *rbt = reinterpret_cast<RowBlock *>(smem + L.rbt);   // the CTA's row blocks
     float *part = reinterpret_cast<float *>(smem + L.part);       // [items in round][16 rows][MT]
-    __shared__ uint32_t nrb_s;
 
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t g = lane >> 2, tq = lane & 3;
@@ -508,29 +516,27 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     const uint32_t tok0 = blockIdx.y * MT;
 
     if (!CHAIN) griddep_launch();
-    if (t == 0) {  // the CTA's 16-row blocks, cut at segment boundaries
-        uint32_t n = 0;
-        for (uint32_t vr = vr0; vr < vr1 && n < kMaxRowBlocks;) {
-            int s = 0;
-            for (int i = 1; i < a.nseg; ++i)
-                if (vr >= a.seg[i].vbegin) s = i;
-            const Seg &sg = a.seg[s];
-            uint32_t e = vr + 16;
-            const uint32_t send = sg.vbegin + sg.rows;
-            e = e < vr1 ? e : vr1;
-            e = e < send ? e : send;
+    // the CTA's 16-row blocks, cut at segment boundaries: thread i resolves
+    // block i (segment s holds ceil(len_s / 16) blocks of the CTA's rows)
+    uint32_t nrb = 0;
+    for (int s = 0; s < a.nseg; ++s) {
+        const Seg &sg = a.seg[s];
+        const uint32_t lo = vr0 > sg.vbegin ? vr0 : sg.vbegin, e = sg.vbegin + sg.rows;
+        const uint32_t hi = vr1 < e ? vr1 : e;
+        const uint32_t nb = hi > lo ? (hi - lo + 15) / 16 : 0;
+        if (t >= nrb && t < nrb + nb && t < kMaxRowBlocks) {
+            const uint32_t vr = lo + (t - nrb) * 16, ve = vr + 16 < hi ? vr + 16 : hi;
             RowBlock rb;
             rb.r = vr - sg.vbegin;
             rb.w = sg.W + (size_t)rb.r * K;
             rb.s = sg.S;
-            rb.nrows_seg = (e - vr) | ((uint32_t)s << 8);
-            rbt[n++] = rb;
-            vr = e;
+            rb.nrows_seg = (ve - vr) | ((uint32_t)s << 8);
+            rbt[t] = rb;
         }
-        nrb_s = n;
+        nrb += nb;
     }
+    nrb = nrb < kMaxRowBlocks ? nrb : kMaxRowBlocks;
     __syncthreads();
-    const uint32_t nrb = nrb_s;
 
     // this lane's loads of an item: rows g, g+8 x 4 groups of 64 columns, and
     // the block scales of both rows.  Out-of-range rows and columns read a
@@ -612,28 +618,39 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
         while (sp >= ipr) { sp -= ipr; ++rbi; }
     };
 
+    // issue cursor (items are issued in compute order, two ahead of the one
+    // being multiplied)
+    uint32_t jt = it, rbj = rbi, sj = sp;
+    auto advance_issue = [&]() {
+        jt += kM2Warps;
+        sj += kM2Warps;
+        while (sj >= ipr) { sj -= ipr; ++rbj; }
+    };
     uint4 va[8], vb[8];
     float sa[4], sb[4];
-    if (it < nitems) issue(va, sa, rbi, sp);  // weights only: before waiting on the previous kernel
-
+    // weights only: the warp's first two items are in flight before it waits
+    // for the previous kernel (or op)
+    if (jt < nitems) { issue(va, sa, rbj, sj); advance_issue(); }
+    if (jt < nitems) { issue(vb, sb, rbj, sj); advance_issue(); }
     if (!CHAIN)
         griddep_wait();
     else if (op > 0)
-        chain_barrier(bar, op * gridDim.x);
+        chain_wait(bar, op * gridDim.x);
     // activation -> f16 hi/lo columns: one warp per (token, 128-column block);
-    // a warp's blocks are loaded four at a time so their L2 round trips overlap
-    for (uint32_t base = warp; base < MT * kbn; base += 4 * kM2Warps) {
-        float4 xv4[4];
+    // a warp's blocks are loaded XU at a time so their L2 round trips overlap
+    constexpr int XU = MT == 1 ? 8 : 4;
+    for (uint32_t base = warp; base < MT * kbn; base += XU * kM2Warps) {
+        float4 xv4[XU];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < XU; ++u) {
             const uint32_t idx = base + u * kM2Warps;
             const uint32_t tt = idx / kbn, kb = idx % kbn;
             xv4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (idx < MT * kbn && tok0 + tt < a.m)
-                xv4[u] = __ldg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + kb * 128 + lane * 4));
+                xv4[u] = __ldcg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + kb * 128 + lane * 4));
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < XU; ++u) {
             const uint32_t idx = base + u * kM2Warps;
             if (idx >= MT * kbn) break;
             const uint32_t tt = idx / kbn, kb = idx % kbn;
@@ -668,27 +685,26 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     if (MT == 1 && a.tp_mode && t == 0) tp_seq_s = p2p_next_seq(a.p2p);  // the previous kernel has completed
     __syncthreads();
 
+    bool flip = false;  // the warp's next item sits in vb
     for (uint32_t rb0 = 0; rb0 < nrb; rb0 += a.rb_round) {
         const uint32_t nrb_r = (nrb - rb0) < a.rb_round ? (nrb - rb0) : a.rb_round;
         const uint32_t iend = (rb0 + nrb_r) * ipr;  // items of this round: [rb0 * ipr, iend)
-        // ping-pong: the other buffer's item is in flight while this one multiplies
-        while (it < iend) {
-            uint32_t c_it = it, c_sp = sp;
-            advance();
-            if (it < nitems) issue(vb, sb, rbi, sp);
-            compute(va, sa, c_sp, c_it - rb0 * ipr);
-            if (it >= iend) {
-                // the next item (if any) sits in vb and belongs to the next round
-                for (int q = 0; q < 8; ++q) va[q] = vb[q];
-                for (int q = 0; q < 4; ++q) sa[q] = sb[q];
-                break;
+        // ping-pong: buffer P holds item it, Q the next one; a buffer is
+        // refilled with the item two ahead as soon as it has been multiplied.
+        // Returns true when the round ends with the next item in Q.
+        auto run = [&](uint4 (&P)[8], float (&Ps)[4], uint4 (&Q)[8], float (&Qs)[4]) -> bool {
+            while (it < iend) {
+                compute(P, Ps, sp, it - rb0 * ipr);
+                advance();
+                if (jt < nitems) { issue(P, Ps, rbj, sj); advance_issue(); }
+                if (it >= iend) return true;
+                compute(Q, Qs, sp, it - rb0 * ipr);
+                advance();
+                if (jt < nitems) { issue(Q, Qs, rbj, sj); advance_issue(); }
             }
-            c_it = it;
-            c_sp = sp;
-            advance();
-            if (it < nitems) issue(va, sa, rbi, sp);
-            compute(vb, sb, c_sp, c_it - rb0 * ipr);
-        }
+            return false;
+        };
+        flip ^= flip ? run(vb, sb, va, sa) : run(va, sa, vb, sb);
         __syncthreads();
         // combine: output (row i of block, token tt) = sum over the block's items, in column order
         for (uint32_t o = t; o < nrb_r * 16 * MT; o += kM2Threads) {
@@ -730,6 +746,7 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
         __syncthreads();
         if (t == 0) p2p_finish(a.p2p, tp_seq);
     }
+    if (CHAIN && !last) chain_arrive(bar);
 }
 
 template <int MT>
@@ -755,13 +772,23 @@ struct ChainArgs {
 __global__ void __launch_bounds__(kM2Threads, 1) gemv_chain_kernel(const __grid_constant__ ChainArgs c)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ MArgs op_s;
+    __shared__ MArgs op_s[2];
+    constexpr uint32_t kOpVecs = sizeof(MArgs) / 16;
+    static_assert(sizeof(MArgs) % 16 == 0, "op descriptors move in 16-byte pieces");
+    // the descriptors travel through L2 into shared memory one op ahead
+    auto fetch_op = [&](uint32_t k) {
+        if (threadIdx.x < kOpVecs)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(reinterpret_cast<uint4 *>(&op_s[k & 1]) + threadIdx.x)),
+                         "l"(reinterpret_cast<const uint4 *>(c.ops + k) + threadIdx.x)
+                         : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    fetch_op(0);
     for (uint32_t k = 0; k < c.nops; ++k) {
-        __syncthreads();  // the previous op is done with op_s and shared memory
-        for (uint32_t i = threadIdx.x; i < sizeof(MArgs) / 4; i += kM2Threads)
-            reinterpret_cast<uint32_t *>(&op_s)[i] = reinterpret_cast<const uint32_t *>(c.ops + k)[i];
-        __syncthreads();
-        gemv_body<1, true>(op_s, smem, c.L, c.bar, k);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();  // op k's descriptor has landed; the previous op is done with the other one and shared memory
+        if (k + 1 < c.nops) fetch_op(k + 1);
+        gemv_body<1, true>(op_s[k & 1], smem, c.L, c.bar, k, k + 1 == c.nops);
     }
     __syncthreads();
     if (threadIdx.x == 0) {  // the last CTA out resets the counters for the next launch

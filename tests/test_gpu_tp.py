@@ -18,7 +18,9 @@ Needs at least two GPUs (skipped otherwise).  Each rank
   collective backends (NCCL, the one-shot peer-memory kernels, and the
   exchange fused into the GEMV epilogue, q35cu_multi_fp8_tp) and checks that
   the replicated outputs agree bit for bit across ranks and between the
-  backends, and that the fused all-gather fills the same gathered buffers.
+  backends, and that the fused all-gather fills the same gathered buffers;
+* runs the same step as one decode chain (q35cu_chain_*, a cooperative launch
+  with the exchanges fused) and checks it equals the fused step bit for bit.
 
 The shard layout and combination rules follow the reference's projections
 (qwen35-c/src/q35_model.c: q/k/v/z/gate/up produce rows, o/out/down reduce
@@ -187,6 +189,20 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     st.step()
     torch.cuda.synchronize()
     rep["fused_gather_equals_p2p"] = bool(torch.equal(g_p2p[0], st.col_full) and torch.equal(g_p2p[1], st.gu_full))
+    # the decode chain (one cooperative launch per step, exchanges fused)
+    # equals the fused per-projection step, both schemes, twice in a row
+    for scheme in ("literal", "paired"):
+        st.coll, st.scheme = "fused", scheme
+        st.step()
+        torch.cuda.synchronize()
+        ref = st.y.clone()
+        ok = True
+        for _ in range(2):
+            st.y.fill_(float("nan"))
+            st.step_chain()
+            torch.cuda.synchronize()
+            ok &= bool(torch.equal(ref, st.y))
+        rep[f"chain_{scheme}_equals_fused"] = ok
     st.free()
     status = q35cu.C.c_uint32(0)
     q35cu.check(q35cu.load().q35cu_device_status(q35cu.C.byref(status), 1))
@@ -222,6 +238,7 @@ def test_tp_two_gpus(tmp_path):
                 assert rep[key + "_finite"] and rep[key + "_replicated"], (key, rep)
         assert rep["stack_p2p_equals_nccl"], rep
         assert rep["stack_fused_equals_p2p"] and rep["fused_gather_equals_p2p"], rep
+        assert rep["chain_literal_equals_fused"] and rep["chain_paired_equals_fused"], rep
     shapes = reps[0]["shapes"]
     assert len(shapes) == len(SHAPES)
     for e in shapes:

@@ -457,14 +457,16 @@ class Chain:
             self.h = _vp()
 
 
-def declared_symbols() -> list[str]:
-    """Every function/variable name declared in include/*.h (for the export test)."""
+def declared_symbols(header: str | None = None) -> list[str]:
+    """Every function/variable name declared in include/*.h (for the export
+    test): the matmul library's headers by default (q35_plat.h is
+    libq35plat.so's), or one named header."""
     import re
 
     names = []
     inc = os.path.join(REPO, "include")
     for fn in sorted(os.listdir(inc)):
-        if not fn.endswith(".h"):
+        if not fn.endswith(".h") or (header is None and fn == "q35_plat.h") or (header and fn != header):
             continue
         with open(os.path.join(inc, fn)) as f:
             src = f.read()

@@ -23,6 +23,18 @@ def test_library_exports_every_declared_symbol(lib):
         assert hasattr(lib, s)
 
 
+def test_platform_library_exports_every_declared_symbol():
+    """include/q35_plat.h (the engine's platform layer) -> libq35plat.so."""
+    import os
+
+    declared = q35cu.declared_symbols("q35_plat.h")
+    assert "q35_plat_mmap_ro" in declared and len(declared) == 27
+    path = os.path.join(os.path.dirname(q35cu.LIB_PATH), "libq35plat.so")
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    assert not [s for s in declared if s not in exported]
+
+
 def test_reference_signatures_are_unchanged():
     """q35_mm.h keeps the reference's prototypes (qwen35-c/include/q35/q35_mm.h:16-48)."""
     import os

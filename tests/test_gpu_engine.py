@@ -1,0 +1,91 @@
+"""The drop-in claim end to end: the reference's engine and its own test
+programs (qwen35-c/src, qwen35-c/tests), compiled unmodified without
+q35_mm.c and the Windows platform layer, resolve every q35_mm_* entry point
+to libq35cuda.so and every q35_plat_* entry point to libq35plat.so (built by
+oracle/Makefile's `engine` target into oracle/_ref/engine, with the fixtures
+they read copied beside them).
+
+* test_st (safetensors loader through mmap_ro / dir walk) and test_kern
+  (the engine's CPU kernels) need no GPU;
+* test_mm, test_batch_mm (the matmul contract), test_deltanet, test_attn
+  (layers whose projections run on the GPU), test_model (the tiny 3-layer
+  hybrid model of the fixtures: DeltaNet + GQA + MLP, every matmul on the
+  B200, logits against the reference's stored logits) and test_oracle
+  (logits of a transformer reference) run on the GPU.
+
+The programs' own pass criteria decide; exit code 77 is their "skip".
+The reference's mm fixtures lack the qkvlike_fp8.w8 blob (listed in its
+.MISSING_LARGE_BLOBS): test_mm checks every case up to it and then stops on
+the missing file, so that run must show every present case "ok", no
+"FAIL", and the missing blob as the only error."""
+from __future__ import annotations
+
+import os
+import subprocess
+
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ENG = os.path.join(os.path.dirname(HERE), "oracle", "_ref", "engine")
+
+
+def _run(prog: str, *args: str, timeout: int = 600) -> subprocess.CompletedProcess:
+    exe = os.path.join(ENG, prog)
+    if not os.path.exists(exe):
+        pytest.skip(f"{exe} not built (make -C oracle engine, needs the reference tree)")
+    return subprocess.run([exe, *args], cwd=ENG, capture_output=True, text=True, timeout=timeout)
+
+
+def _fix(name: str) -> str:
+    return os.path.join(ENG, "fixtures", name)
+
+
+def _check(r: subprocess.CompletedProcess) -> None:
+    if r.returncode == 77:
+        pytest.skip(r.stdout.strip()[-200:])
+    assert r.returncode == 0, (r.returncode, r.stdout[-3000:], r.stderr[-2000:])
+
+
+def test_engine_st_cpu():
+    _check(_run("test_st", _fix("st")))
+
+
+def test_engine_kern_cpu():
+    _check(_run("test_kern", _fix("kern")))
+
+
+@pytest.mark.gpu
+def test_engine_mm(gpu):
+    r = _run("test_mm", _fix("mm"))
+    oks = [ln for ln in r.stdout.splitlines() if ln.startswith("ok ")]
+    assert not [ln for ln in r.stdout.splitlines() if ln.startswith("FAIL")], r.stdout
+    if r.returncode != 0:  # stopped at the blob the reference does not ship
+        assert "qkvlike_fp8.w8" in r.stderr, (r.stdout, r.stderr)
+        assert len(oks) >= 5, r.stdout  # tiny, edge, exact1, wide, deep (fp8)
+    assert all("impl=sm_100a" in ln for ln in oks), r.stdout
+
+
+@pytest.mark.gpu
+def test_engine_batch_mm(gpu):
+    _check(_run("test_batch_mm"))
+
+
+@pytest.mark.gpu
+def test_engine_deltanet(gpu):
+    _check(_run("test_deltanet", _fix("deltanet")))
+
+
+@pytest.mark.gpu
+def test_engine_attn(gpu):
+    _check(_run("test_attn", _fix("attn")))
+
+
+@pytest.mark.gpu
+def test_engine_model(gpu):
+    r = _run("test_model", _fix("model"))
+    _check(r)
+
+
+@pytest.mark.gpu
+def test_engine_oracle(gpu):
+    _check(_run("test_oracle", _fix("oracle")))

@@ -96,6 +96,21 @@ int q35cu_weight_download_fp8(const q35cu_weight *w, uint8_t *W, uint16_t *scale
  * rows, cols) from the device weight w without an upload (a loader that
  * streamed the tensor to HBM itself).  w must outlive the binding. */
 int q35cu_weight_bind(const uint8_t *host_W, const uint16_t *host_sc, const q35cu_weight *w);
+
+/* Upload the matmul operands of one mapped safetensors shard now (base, len:
+ * the whole file as mapped) and key them by their addresses in the mapping,
+ * exactly as the first q35_mm_fp8 / q35_mm_bf16 call on them would: every
+ * FP8 "X.weight" [rows, cols] with its BF16 "X.weight_scale_inv" grid (the
+ * pair may span shards: the half seen first waits, by name, for the other),
+ * and a BF16 "lm_head.weight".  The engine binds these pointers straight into
+ * its mappings (qwen35-c/src/q35_model.c:252-273), so its first forward pass
+ * then uploads nothing.  libq35plat's q35_plat_mmap_prefetch calls this when
+ * libq35cuda is loaded (set Q35_PRELOAD=0 to keep first-touch uploads).
+ * q35cu_preload_forget drops the unmatched halves that point into a mapping
+ * about to be unmapped; q35cu_preload_bytes counts the bytes preloaded. */
+int q35cu_preload_safetensors(const void *base, size_t len);
+void q35cu_preload_forget(const void *base, size_t len);
+size_t q35cu_preload_bytes(void);
 void q35cu_weight_free(q35cu_weight *w);
 uint32_t q35cu_weight_rows(const q35cu_weight *w);
 uint32_t q35cu_weight_cols(const q35cu_weight *w);

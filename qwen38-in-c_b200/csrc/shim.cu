@@ -21,6 +21,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <string>
 #include <unordered_map>
 #include <vector>
 
@@ -569,6 +570,219 @@ Q35_API int q35cu_weight_download_fp8(const q35cu_weight *w, uint8_t *W, uint16_
     Q35CU_CUDA(cudaMemcpyAsync(sc, d->d_stage, n * 2, cudaMemcpyDeviceToHost, d->stream));
     Q35CU_CUDA(cudaStreamSynchronize(d->stream));
     return Q35CU_OK;
+}
+
+// ---- safetensors preload ---------------------------------------------------
+//
+// The engine maps every shard read-only and binds its matmul operands as
+// pointers into the mappings (qwen35-c/src/q35_model.c:204-208, 252-273:
+// tensor "X.weight" F8_E4M3 [rows, cols] with "X.weight_scale_inv" BF16
+// [ceil(rows/128), ceil(cols/128)]; lm_head.weight BF16 for q35_mm_bf16).
+// q35cu_preload_safetensors walks one mapped shard in file order and uploads
+// those operands now, keyed by exactly those pointers, so the first forward
+// pass finds them resident instead of uploading on first touch.  A weight and
+// its scale may sit in different shards: the first one seen waits, by name,
+// until the other's shard is preloaded.
+namespace {
+
+// A minimal JSON reader for the safetensors header: a flat object of
+// name -> {"dtype": s, "shape": [n...], "data_offsets": [a, b]} (plus
+// "__metadata__").  Unknown members are skipped.
+struct JsonCursor {
+    const char *p, *e;
+    bool ok = true;
+    void ws() { while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p; }
+    bool eat(char c)
+    {
+        ws();
+        if (p < e && *p == c) { ++p; return true; }
+        return false;
+    }
+    bool str(std::string *out)
+    {
+        ws();
+        if (p >= e || *p != '"') return ok = false;
+        ++p;
+        std::string v;
+        while (p < e && *p != '"') {
+            if (*p == '\\') {
+                if (++p >= e) return ok = false;
+                const char c = *p;
+                if (c == 'u') {  // names are ASCII in practice; keep the escape literally
+                    v += "\\u";
+                } else {
+                    v += c == 'n' ? '\n' : c == 't' ? '\t' : c == 'r' ? '\r' : c == 'b' ? '\b' : c == 'f' ? '\f' : c;
+                }
+                ++p;
+                continue;
+            }
+            v += *p++;
+        }
+        if (p >= e) return ok = false;
+        ++p;
+        if (out) *out = v;
+        return true;
+    }
+    bool num(uint64_t *out)
+    {
+        ws();
+        if (p >= e || *p < '0' || *p > '9') return ok = false;
+        uint64_t v = 0;
+        while (p < e && *p >= '0' && *p <= '9') {
+            v = v * 10 + (uint64_t)(*p - '0');
+            ++p;
+        }
+        if (out) *out = v;
+        return true;
+    }
+    bool skip()  // any value
+    {
+        ws();
+        if (p >= e) return ok = false;
+        if (*p == '"') return str(nullptr);
+        if (*p == '{' || *p == '[') {
+            const char close = *p == '{' ? '}' : ']';
+            ++p;
+            if (eat(close)) return true;
+            for (;;) {
+                if (close == '}') {
+                    if (!str(nullptr) || !eat(':')) return ok = false;
+                }
+                if (!skip()) return false;
+                if (eat(close)) return true;
+                if (!eat(',')) return ok = false;
+            }
+        }
+        while (p < e && *p != ',' && *p != '}' && *p != ']') ++p;  // number, true, false, null
+        return true;
+    }
+};
+
+struct StTensor {
+    std::string dtype;
+    std::vector<uint64_t> shape;
+    uint64_t off0 = 0, off1 = 0;
+};
+
+// calls fn(name, tensor) for every tensor of the header; false if malformed
+template <class F>
+bool st_header(const uint8_t *base, size_t len, F &&fn)
+{
+    if (len < 8) return false;
+    uint64_t hlen = 0;
+    for (int i = 7; i >= 0; --i) hlen = (hlen << 8) | base[i];
+    if (hlen > len - 8) return false;
+    JsonCursor j{reinterpret_cast<const char *>(base + 8), reinterpret_cast<const char *>(base + 8 + hlen)};
+    if (!j.eat('{')) return false;
+    if (j.eat('}')) return true;
+    for (;;) {
+        std::string name;
+        if (!j.str(&name) || !j.eat(':')) return false;
+        if (name == "__metadata__") {
+            if (!j.skip()) return false;
+        } else {
+            StTensor t;
+            if (!j.eat('{')) return false;
+            if (!j.eat('}')) {
+                for (;;) {
+                    std::string key;
+                    if (!j.str(&key) || !j.eat(':')) return false;
+                    if (key == "dtype") {
+                        if (!j.str(&t.dtype)) return false;
+                    } else if (key == "shape" || key == "data_offsets") {
+                        if (!j.eat('[')) return false;
+                        std::vector<uint64_t> v;
+                        if (!j.eat(']')) {
+                            for (;;) {
+                                uint64_t x;
+                                if (!j.num(&x)) return false;
+                                v.push_back(x);
+                                if (j.eat(']')) break;
+                                if (!j.eat(',')) return false;
+                            }
+                        }
+                        if (key == "shape") t.shape = v;
+                        else if (v.size() == 2) { t.off0 = v[0]; t.off1 = v[1]; }
+                        else return false;
+                    } else if (!j.skip()) {
+                        return false;
+                    }
+                    if (j.eat('}')) break;
+                    if (!j.eat(',')) return false;
+                }
+            }
+            if (t.off1 < t.off0 || t.off1 > len - 8 - hlen) return false;
+            fn(name, t, base + 8 + hlen + t.off0);
+        }
+        if (j.eat('}')) return true;
+        if (!j.eat(',')) return false;
+    }
+}
+
+struct StHalf {
+    const uint8_t *p;
+    uint64_t d0, d1;  // shape
+};
+std::unordered_map<std::string, StHalf> g_st_w, g_st_s;  // unmatched FP8 weights / scale grids, by weight name
+size_t g_preload_bytes = 0;
+
+}  // namespace
+
+Q35_API int q35cu_preload_safetensors(const void *base, size_t len)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!base) return set_error(Q35CU_ERR_ARG, "preload: NULL mapping");
+    if (!dev_state()) return t_err;
+    const uint8_t *b = static_cast<const uint8_t *>(base);
+    static const std::string kSuffix = "_scale_inv";
+    std::vector<std::pair<StHalf, StHalf>> pairs;  // (weight, scale) in file order
+    std::vector<StHalf> bf16;                      // lm_head
+    const bool parsed = st_header(b, len, [&](const std::string &name, const StTensor &t, const uint8_t *p) {
+        if (t.shape.size() != 2) return;
+        const StHalf h{p, t.shape[0], t.shape[1]};
+        if (t.dtype == "F8_E4M3") {
+            auto it = g_st_s.find(name);
+            if (it != g_st_s.end()) { pairs.push_back({h, it->second}); g_st_s.erase(it); }
+            else g_st_w[name] = h;
+        } else if (t.dtype == "BF16" && name.size() > kSuffix.size() &&
+                   name.compare(name.size() - kSuffix.size(), kSuffix.size(), kSuffix) == 0) {
+            const std::string wname = name.substr(0, name.size() - kSuffix.size());
+            auto it = g_st_w.find(wname);
+            if (it != g_st_w.end()) { pairs.push_back({it->second, h}); g_st_w.erase(it); }
+            else g_st_s[wname] = h;
+        } else if (t.dtype == "BF16" && name == "lm_head.weight") {
+            bf16.push_back(h);
+        }
+    });
+    if (!parsed) return set_error(Q35CU_ERR_ARG, "preload: not a safetensors header");
+    for (const auto &pr : pairs) {
+        const StHalf &w = pr.first, &sc = pr.second;
+        if (w.d0 > 0xFFFFFFFFull || w.d1 > 0xFFFFFFFFull || sc.d0 != (w.d0 + 127) / 128 || sc.d1 != (w.d1 + 127) / 128)
+            continue;  // not a block-scaled pair the engine would bind
+        if (!cached_weight(0, w.p, sc.p, (uint32_t)w.d0, (uint32_t)w.d1)) return t_err;
+        g_preload_bytes += w.d0 * w.d1;
+    }
+    for (const auto &h : bf16) {
+        if (h.d0 > 0xFFFFFFFFull || h.d1 > 0xFFFFFFFFull) continue;
+        if (!cached_weight(1, h.p, nullptr, (uint32_t)h.d0, (uint32_t)h.d1)) return t_err;
+        g_preload_bytes += h.d0 * h.d1 * 2;
+    }
+    return Q35CU_OK;
+}
+
+Q35_API void q35cu_preload_forget(const void *base, size_t len)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    const uint8_t *lo = static_cast<const uint8_t *>(base), *hi = lo + len;
+    for (auto *m : {&g_st_w, &g_st_s})
+        for (auto it = m->begin(); it != m->end();)
+            it = (it->second.p >= lo && it->second.p < hi) ? m->erase(it) : std::next(it);
+}
+
+Q35_API size_t q35cu_preload_bytes(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    return g_preload_bytes;
 }
 
 Q35_API int q35cu_weight_bind(const uint8_t *host_W, const uint16_t *host_sc, const q35cu_weight *w)

@@ -12,7 +12,12 @@
  *                    reference returns NULL when large pages are unavailable
  *   dir_*            opendir/readdir, regular files only
  *   mmap_ro          open + mmap(PROT_READ, MAP_PRIVATE), MADV_SEQUENTIAL
- *   mmap_prefetch    MADV_WILLNEED over the mapping, then one touch per page
+ *   mmap_prefetch    MADV_WILLNEED over the mapping, then one touch per page;
+ *                    when libq35cuda is loaded in the process and the mapping
+ *                    is a safetensors shard, its matmul weights are then
+ *                    uploaded to the GPU (q35cu_preload_safetensors), so the
+ *                    first forward pass does not upload on first touch
+ *                    (Q35_PRELOAD=0 turns this off)
  *   avail_phys       MemAvailable of /proc/meminfo (sysconf fallback)
  *   peak_rss         getrusage ru_maxrss
  *   num_phys_cores   distinct (package, core) pairs of the CPUs this process
@@ -26,6 +31,7 @@
 
 #include <arpa/inet.h>
 #include <dirent.h>
+#include <dlfcn.h>
 #include <errno.h>
 #include <fcntl.h>
 #include <netinet/in.h>
@@ -223,9 +229,34 @@ Q35_API Q35PlatMmap *q35_plat_mmap_ro(const char *path, const uint8_t **out_base
     return m;
 }
 
+/* libq35cuda's preload entry points, when that library is in the process:
+ * linked into the program, or opened with local symbol scope (a host
+ * language's FFI) -- found by its soname without loading it */
+typedef int (*preload_fn)(const void *, size_t);
+typedef void (*forget_fn)(const void *, size_t);
+
+static void *q35cuda_sym(const char *name)
+{
+    void *s = dlsym(RTLD_DEFAULT, name);
+    if (s) return s;
+    void *h = dlopen("libq35cuda.so", RTLD_NOLOAD | RTLD_LAZY);
+    if (!h) return NULL;
+    s = dlsym(h, name);
+    dlclose(h);  /* drops only the reference RTLD_NOLOAD took */
+    return s;
+}
+
+static int preload_enabled(void)
+{
+    const char *e = getenv("Q35_PRELOAD");
+    return !(e && strcmp(e, "0") == 0);
+}
+
 Q35_API void q35_plat_munmap(Q35PlatMmap *m)
 {
     if (!m) return;
+    forget_fn forget = (forget_fn)q35cuda_sym("q35cu_preload_forget");
+    if (forget && m->base) forget(m->base, m->len);
     if (m->base) munmap(m->base, m->len);
     if (m->fd >= 0) close(m->fd);
     free(m);
@@ -246,6 +277,14 @@ Q35_API void q35_plat_mmap_prefetch(Q35PlatMmap *m)
 {
     if (!m || !m->base) return;
     q35_plat_prefetch(m->base, m->len);
+    if (!preload_enabled()) return;
+    const uint8_t *b = (const uint8_t *)m->base;
+    uint64_t hlen = 0;  /* a safetensors shard: 8-byte header length, then a JSON object */
+    if (m->len < 10) return;
+    for (int i = 7; i >= 0; --i) hlen = (hlen << 8) | b[i];
+    if (hlen > m->len - 8 || b[8] != '{') return;
+    preload_fn preload = (preload_fn)q35cuda_sym("q35cu_preload_safetensors");
+    if (preload) preload(m->base, m->len);  /* a failure leaves first-touch uploads in place */
 }
 
 Q35_API uint64_t q35_plat_avail_phys(void)

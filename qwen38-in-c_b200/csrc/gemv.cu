@@ -408,6 +408,7 @@ constexpr int kM2Warps = 16;
 constexpr int kM2Threads = kM2Warps * 32;
 constexpr uint32_t kItemCols = 256;   // columns per work item
 constexpr uint32_t kMaxRowBlocks = 256;
+constexpr uint32_t kMaxChunks = 512;  // 256-column activation chunks (K <= 131072)
 
 struct alignas(16) MArgs {
     Seg seg[4];
@@ -500,8 +501,8 @@ __device__ __forceinline__ void chain_wait(uint32_t *bar, uint32_t target)
 // arrives for the next one when its outputs are written (last == false).  In
 // both, the warps' first two weight items are in flight when they wait.
 template <int MT, bool CHAIN>
-__device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const MmaSmem &L, uint32_t *bar,
-                                          uint32_t op, bool last = true)
+__device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const MmaSmem &L, uint32_t *xflag,
+                                          uint32_t epoch, uint32_t *bar, uint32_t op, bool last = true)
 {
     uint8_t *xs = smem + L.xs;                                    // [2*MT][xcol_bytes] f16 columns
     float *xmul = reinterpret_cast<float *>(smem + L.xmul);       // [MT][kblocks] 2^-e
@@ -572,6 +573,17 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     const uint8_t *xcol = xs + (size_t)(g % (2 * MT)) * a.xcol_bytes + tq * 32;
     auto compute = [&](const uint4 (&v)[8], const float (&sc)[4], uint32_t sp, uint32_t slot) {
         const uint32_t c0 = sp * kItemCols;
+        if (MT == 1 && !CHAIN) {  // this item's activation chunk is converted (bounded wait)
+            if (lane == 0) {
+                for (uint32_t i = 0; *reinterpret_cast<volatile uint32_t *>(&xflag[sp]) != epoch; ++i)
+                    if (i >= kSpinLimit) {
+                        atomicExch(&g_device_status, (uint32_t)Q35CU_ERR_TIMEOUT);
+                        break;
+                    }
+                __threadfence_block();
+            }
+            __syncwarp();
+        }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
@@ -636,54 +648,90 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
         griddep_wait();
     else if (op > 0)
         chain_wait(bar, op * gridDim.x);
-    // activation -> f16 hi/lo columns: one warp per (token, 128-column block);
-    // a warp's blocks are loaded XU at a time so their L2 round trips overlap
-    constexpr int XU = MT == 1 ? 8 : 4;
-    for (uint32_t base = warp; base < MT * kbn; base += XU * kM2Warps) {
-        float4 xv4[XU];
+    // activation -> f16 hi/lo columns, one 128-column block at a time
+    auto convert_block = [&](uint32_t tt, uint32_t kb, const float4 &v) {
+        const uint32_t k = kb * 128 + lane * 4;
+        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-        for (int u = 0; u < XU; ++u) {
-            const uint32_t idx = base + u * kM2Warps;
-            const uint32_t tt = idx / kbn, kb = idx % kbn;
-            xv4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (idx < MT * kbn && tok0 + tt < a.m)
-                xv4[u] = __ldcg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + kb * 128 + lane * 4));
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        int e = 0;  // 2^e with max |x*2^e| < 2^15; |e| <= 126 keeps 2^e and 2^-e normal
+        if (mx > 0.f && mx <= 3.402823466e38f) {
+            const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;
+            e = 14 - E;
+            e = e > 126 ? 126 : (e < -126 ? -126 : e);
         }
+        const float up = __uint_as_float((uint32_t)(e + 127) << 23);
+        const float down = __uint_as_float((uint32_t)(127 - e) << 23);
+        const float xv[4] = {v.x * up, v.y * up, v.z * up, v.w * up};
+        uint16_t hi[4], lo[4];
 #pragma unroll
-        for (int u = 0; u < XU; ++u) {
-            const uint32_t idx = base + u * kM2Warps;
-            if (idx >= MT * kbn) break;
-            const uint32_t tt = idx / kbn, kb = idx % kbn;
-            const uint32_t k = kb * 128 + lane * 4;
-            const float4 v = xv4[u];
-            float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        for (int j = 0; j < 4; ++j) {
+            hi[j] = f16_bits(xv[j]);
+            lo[j] = f16_bits(xv[j] - __half2float(__ushort_as_half(hi[j])));
+        }
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) =
+            make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) =
+            make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
+        if (lane == 0) xmul[tt * kbn + kb] = down;
+    };
+    // chunk flags in standalone launches (the chain converts with a barrier:
+    // its kernel has no registers to spare for the flag bookkeeping)
+    constexpr bool FLAGS = MT == 1 && !CHAIN;
+    if (FLAGS) {
+        // Warp w converts the column chunks w, w + 16, ... (a chunk = the two
+        // blocks of one item; its own first item's chunk comes first) and
+        // marks each chunk ready with this op's epoch: a warp then waits only
+        // for the chunks of the item it multiplies, not for the whole vector.
+        const uint32_t nchunk = (kbn + 1) / 2;
+        for (uint32_t c0 = warp; c0 < nchunk; c0 += 4 * kM2Warps) {
+            float4 xv4[8];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-            int e = 0;  // 2^e with max |x*2^e| < 2^15; |e| <= 126 keeps 2^e and 2^-e normal
-            if (mx > 0.f && mx <= 3.402823466e38f) {
-                const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;
-                e = 14 - E;
-                e = e > 126 ? 126 : (e < -126 ? -126 : e);
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t c = c0 + (u >> 1) * kM2Warps, kb = 2 * c + (u & 1);
+                xv4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c < nchunk && kb < kbn && tok0 < a.m)
+                    xv4[u] = __ldcg(reinterpret_cast<const float4 *>(a.X + (size_t)tok0 * a.ldx + kb * 128 + lane * 4));
             }
-            const float up = __uint_as_float((uint32_t)(e + 127) << 23);
-            const float down = __uint_as_float((uint32_t)(127 - e) << 23);
-            const float xv[4] = {v.x * up, v.y * up, v.z * up, v.w * up};
-            uint16_t hi[4], lo[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                hi[j] = f16_bits(xv[j]);
-                lo[j] = f16_bits(xv[j] - __half2float(__ushort_as_half(hi[j])));
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t c = c0 + (u >> 1) * kM2Warps, kb = 2 * c + (u & 1);
+                if (c >= nchunk) break;
+                if (kb < kbn) convert_block(0, kb, xv4[u]);
+                if (u & 1) {
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        *reinterpret_cast<volatile uint32_t *>(&xflag[c]) = epoch;
+                    }
+                }
             }
-            *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) =
-                make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
-            *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) =
-                make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
-            if (lane == 0) xmul[tt * kbn + kb] = down;
+        }
+    } else {
+        // one warp per (token, 128-column block), XU blocks of a warp loaded
+        // at once so their L2 round trips overlap
+        constexpr int XU = MT == 1 ? 8 : 4;
+        for (uint32_t base = warp; base < MT * kbn; base += XU * kM2Warps) {
+            float4 xv4[XU];
+#pragma unroll
+            for (int u = 0; u < XU; ++u) {
+                const uint32_t idx = base + u * kM2Warps;
+                const uint32_t tt = idx / kbn, kb = idx % kbn;
+                xv4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (idx < MT * kbn && tok0 + tt < a.m)
+                    xv4[u] = __ldcg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + kb * 128 + lane * 4));
+            }
+#pragma unroll
+            for (int u = 0; u < XU; ++u) {
+                const uint32_t idx = base + u * kM2Warps;
+                if (idx >= MT * kbn) break;
+                convert_block(idx / kbn, idx % kbn, xv4[u]);
+            }
         }
     }
     __shared__ uint32_t tp_seq_s;
     if (MT == 1 && a.tp_mode && t == 0) tp_seq_s = p2p_next_seq(a.p2p);  // the previous kernel has completed
-    __syncthreads();
+    if (!FLAGS) __syncthreads();  // the whole activation is converted
 
     bool flip = false;  // the warp's next item sits in vb
     for (uint32_t rb0 = 0; rb0 < nrb; rb0 += a.rb_round) {
@@ -753,8 +801,10 @@ template <int MT>
 __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_constant__ MArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t xflag[kMaxChunks];
+    for (uint32_t i = threadIdx.x; i < kMaxChunks; i += kM2Threads) xflag[i] = 0;  // ordered by the body's first barrier
     const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * a.ipr);
-    gemv_body<MT, false>(a, smem, L, nullptr, 0);
+    gemv_body<MT, false>(a, smem, L, xflag, 1, nullptr, 0);
 }
 
 // A chain of one-token decode GEMVs in one cooperative launch: every CTA
@@ -788,7 +838,7 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_chain_kernel(const __grid_
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads();  // op k's descriptor has landed; the previous op is done with the other one and shared memory
         if (k + 1 < c.nops) fetch_op(k + 1);
-        gemv_body<1, true>(op_s[k & 1], smem, c.L, c.bar, k, k + 1 == c.nops);
+        gemv_body<1, true>(op_s[k & 1], smem, c.L, nullptr, 0, c.bar, k, k + 1 == c.nops);
     }
     __syncthreads();
     if (threadIdx.x == 0) {  // the last CTA out resets the counters for the next launch
@@ -954,6 +1004,7 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp)
     const uint32_t rows_cta = (a.total_rows + gx - 1) / gx;
     const uint32_t nrb_max = (rows_cta + 15) / 16 + 2 * (uint32_t)a.nseg;
     if (nrb_max > kMaxRowBlocks) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: %u rows per CTA", rows_cta);
+    if ((a.kblocks + 1) / 2 > kMaxChunks) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: cols %u too large", a0.K);
     int mt = a0.m >= 3 ? 4 : (int)a0.m;
     auto fits = [&](int mtt, uint32_t rbr) {
         return mma_smem_layout(mtt, a.xcol_bytes, a.kblocks, rbr * a.ipr).total <= budget;

@@ -67,7 +67,7 @@ constexpr int kMaxWarps = kMaxCons / 32;
 constexpr int kMaxStages = 8;
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kFull = 0xffffffffu;
-constexpr uint32_t kRingBudget = 100 * 1024;
+constexpr uint32_t kRingBudget = 200 * 1024;  // ring bytes per CTA (one CTA per SM)
 
 struct Seg {
     const uint8_t *W;
@@ -943,7 +943,7 @@ int launch_tma(const Args &a, dim3 grid, size_t smem, cudaStream_t st)
     Q35CU_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
     if (!configured[dev]) {
-        Q35CU_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        Q35CU_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024));
         configured[dev] = true;
     }
     return launch_pdl(k, grid, dim3(a.cons + 32), smem, st, a);
@@ -1025,7 +1025,10 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp)
 }
 
 // (MT, P) with MT * P <= 4 registers of activation per thread-slice; R rows
-// per stage from P (about 20 KB per stage)
+// per stage from P.  A bulk copy costs about the same per instruction at any
+// size, so stages are as large as the ring allows: the lm_head's 5120-column
+// bf16 rows (P = 2) go 8 rows = 80 KB per copy, two stages (6.6 TB/s against
+// 5.1 at 2 rows and five stages, 6.0 at 4 rows; same bits).
 template <int KIND>
 int dispatch_tma(const Args &a, dim3 grid, size_t smem, int mt, int P, cudaStream_t st)
 {
@@ -1035,8 +1038,8 @@ int dispatch_tma(const Args &a, dim3 grid, size_t smem, int mt, int P, cudaStrea
         return launch_tma<KIND, 4, 1, 4>(a, grid, smem, st);
     }
     if (P == 2) {
-        if (mt == 1) return launch_tma<KIND, 1, 2, 2>(a, grid, smem, st);
-        return launch_tma<KIND, 2, 2, 2>(a, grid, smem, st);
+        if (mt == 1) return launch_tma<KIND, 1, 2, 8>(a, grid, smem, st);
+        return launch_tma<KIND, 2, 2, 8>(a, grid, smem, st);
     }
     if (P == 3) return launch_tma<KIND, 1, 3, 1>(a, grid, smem, st);
     return launch_tma<KIND, 1, 4, 1>(a, grid, smem, st);
@@ -1198,7 +1201,7 @@ int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint
     if (P > 4) vec_ok = false;
     if (vec_ok) {
         a.cons = T;
-        const int R = P == 1 ? 4 : (P == 2 ? 2 : 1);
+        const int R = P == 1 ? 4 : (P == 2 ? 8 : 1);
         a.slot_bytes = (uint32_t)R * K * esz;
         uint32_t stages = kRingBudget / a.slot_bytes;
         stages = stages < 2 ? 2 : (stages > kMaxStages ? kMaxStages : stages);

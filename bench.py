@@ -55,6 +55,8 @@ def parse():
                     help="only the isolated configuration-0 GEMV (a small command for ncu captures)")
     ap.add_argument("--profile-c2", action="store_true",
                     help="only the configuration-2 gate projection at M=2048 through the GEMM (for ncu captures)")
+    ap.add_argument("--profile-lm-head", type=int, default=0, metavar="ROWS",
+                    help="only the bf16 lm_head matvec on ROWS x 5120, --steps calls (for ncu captures)")
     return ap.parse_args()
 
 
@@ -260,6 +262,43 @@ def time_gemv_rotating(q35cu, torch, rows, cols, m, copies=5, rounds=20, path="g
     b = gemv_bytes(rows, cols, m)
     return {"rows": rows, "cols": cols, "m": m, "path": path, "us": round(us, 2), "GBps": round(b / us / 1e3, 1),
             "TFLOPs": round(2 * m * rows * cols / us / 1e6, 3)}
+
+
+def bf16_weight(q35cu, torch, rows, cols, seed=4242):
+    """A bf16 [rows, cols] weight of N(0, 0.02) values, uploaded through
+    q35cu_weight_upload_bf16 (the lm_head operand of q35_mm_bf16)."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    dev = (torch.randn((rows, cols), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    host = dev.view(torch.int16).cpu().numpy().view("uint16")
+    del dev
+    return q35cu.Weight.upload_bf16(host)
+
+
+def time_lm_head(q35cu, torch, hbm_peak, rows=248320, cols=5120, reps=20):
+    """The bf16 lm_head matvec (q35_mm_bf16 on a device-resident weight,
+    q35cu_gemv_bf16): 2.5 GB per call, larger than L2; CUDA events per call."""
+    w = bf16_weight(q35cu, torch, rows, cols)
+    try:
+        x = torch.randn(cols, device="cuda")
+        y = torch.empty(rows, device="cuda")
+        for _ in range(3):
+            q35cu.gemv_bf16(w, x, y)
+        torch.cuda.synchronize()
+        us = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            q35cu.gemv_bf16(w, x, y)
+            b.record()
+            torch.cuda.synchronize()
+            us.append(a.elapsed_time(b) * 1e3)
+    finally:
+        w.free()
+    us.sort()
+    med = us[len(us) // 2]
+    by = 2 * rows * cols + 4 * cols + 4 * rows  # weight + x + y
+    return {"rows": rows, "cols": cols, "kernel": "gemv_tma_kernel<bf16>", "us_median": round(med, 2),
+            "us_min": round(us[0], 2), "GBps": round(by / med / 1e3, 1), "frac_of_measured_hbm": round(by / med / 1e3 / hbm_peak, 4)}
 
 
 def kernel_roofline(q35cu, torch, st, hbm_peak, reps=3):
@@ -708,6 +747,7 @@ def run_ours(args):
                 if m >= 16:  # what q35_mm_fp8_batch runs at this size
                     sweep.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10, path="tc"))
         extras["config1_sweep"] = sweep
+        extras["lm_head_bf16"] = time_lm_head(q35cu, torch, hbm_peak)
         extras["config2_prefill"] = time_prefill_c2(q35cu, torch, bf16_peak)
     if not args.no_extras:  # every rank takes part (collectives)
         c4 = time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak)
@@ -816,12 +856,36 @@ def run_profile_c2(args):
     return 0
 
 
+def run_profile_lm_head(args):
+    import torch
+
+    import q35cu
+
+    torch.cuda.set_device(0)
+    q35cu.check(q35cu.load().q35cu_set_device(0))
+    w = bf16_weight(q35cu, torch, args.profile_lm_head, 5120)
+    try:
+        x = torch.randn(5120, device="cuda")
+        y = torch.empty(args.profile_lm_head, device="cuda")
+        for _ in range(max(1, args.steps)):
+            q35cu.gemv_bf16(w, x, y)
+        torch.cuda.synchronize()
+        ok = bool(torch.isfinite(y).all())
+    finally:
+        w.free()
+    print(json.dumps({"lm_head_bf16": "ok" if ok else "non-finite", "rows": args.profile_lm_head,
+                      "launches": max(1, args.steps)}), flush=True)
+    return 0 if ok else 1
+
+
 def main():
     args = parse()
     if args.profile_c0:
         return run_profile_c0(args)
     if args.profile_c2:
         return run_profile_c2(args)
+    if args.profile_lm_head:
+        return run_profile_lm_head(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

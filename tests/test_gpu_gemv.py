@@ -136,6 +136,53 @@ def test_odd_shapes(gpu, orc, ref, rows, cols):
     _check(orc, W, sc, X, q35cu.mm_fp8_batch(W, sc, X), ref.mm_fp8_batch(W, sc, X), "batch")
 
 
+@pytest.mark.parametrize("rows,cols", [(700, 1040), (4800, 6160), (700, 12304), (400, 18448)])
+def test_cuda_core_geometries(gpu, orc, ref, rows, cols):
+    """The CUDA-core streaming kernel (cols % 128 != 0) at every register-pass
+    count P = 1..4 (1040, 6160, 12304, 18448 fp8 columns), one to four tokens
+    (1, 2 or 4 tokens per CTA column block); 4800 rows fill whole 8-row
+    stages at P = 2."""
+    g = np.random.default_rng(rows + 7 * cols)
+    import oracle
+
+    W = g.integers(0, 256, size=(rows, cols), dtype=np.uint8)
+    W[(W & 0x7F) == 0x7F] = 0x41
+    sc = oracle.bf16_bits((g.random(((rows + 127) // 128, (cols + 127) // 128)) + 0.5).astype(np.float32))
+    X = g.standard_normal((4, cols)).astype(np.float32)
+    _check(orc, W, sc, X[0], q35cu.mm_fp8(W, sc, X[0]), ref.mm_fp8(W, sc, X[0]), "single")
+    for n in (2, 3, 4):
+        _check(orc, W, sc, X[:n], q35cu.mm_fp8_batch(W, sc, X[:n]), ref.mm_fp8_batch(W, sc, X[:n]), f"batch {n}")
+
+
+def test_cuda_core_forced_on_aligned_cols(gpu, orc, ref, monkeypatch):
+    """Q35CU_GEMV_SIMT routes a cols % 128 == 0 weight to the CUDA-core kernel
+    (6272 columns: two register passes); it agrees with the tensor-core GEMV
+    within the GEMV bound."""
+    W, sc = _synth(orc, 61, 4800, 6272)
+    x = orc.synth_act(62, (6272,))
+    y_tc = q35cu.mm_fp8(W, sc, x)
+    gpu.q35cu_release_all()
+    monkeypatch.setenv("Q35CU_GEMV_SIMT", "1")
+    y_cc = q35cu.mm_fp8(W, sc, x)
+    yr = ref.mm_fp8(W, sc, x)
+    _check(orc, W, sc, x, y_cc, yr, "cuda-core")
+    _check(orc, W, sc, x, y_tc, yr, "tensor-core")
+
+
+@pytest.mark.parametrize("cols", [1024, 8192, 12288])
+def test_bf16_geometries(gpu, orc, ref, cols):
+    """q35_mm_bf16 at register-pass counts P = 1, 3, 4 (the lm_head's 5120
+    columns, P = 2, is test_bf16_lm_head_shape)."""
+    g = np.random.default_rng(cols)
+    import oracle
+
+    W16 = oracle.bf16_bits(g.standard_normal((5000, cols)).astype(np.float32) * 0.02)
+    x = g.standard_normal(cols).astype(np.float32)
+    y = q35cu.mm_bf16(W16, x)
+    wf = (W16.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    assert gemv_report(y, ref.mm_bf16(W16, x), wf @ x.astype(np.float64), np.abs(wf * x).sum(1))["ok"]
+
+
 def test_zero_sizes(gpu):
     W = np.zeros((4, 8), np.uint8)
     sc = np.zeros((1, 1), np.uint16)

@@ -22,6 +22,10 @@
 // Persistent CTAs (one per SM) walk 128 (weight rows) x 192 (tokens) tiles,
 // token tile fastest: the CTAs running together share a few weight row
 // blocks (each read from HBM about once) and the activations (L2-resident).
+// A call with at most 128 activation rows (multi-token decode on exact
+// activations: 2 rows per token) takes a 32-, 64- or 128-row token tile
+// instead, so the MMAs, the activation copies and the epilogue cover only
+// the rows it has (the weights stream the same way).
 //
 // Three measured costs shape the kernel:
 //   * shared-memory bandwidth: an MMA that reads both operands from shared
@@ -70,29 +74,39 @@ __device__ uint32_t g_gemm_status;
 namespace {
 
 constexpr int kBM = 128;   // weight rows per tile (MMA M)
-constexpr int kBN = 192;   // tokens per tile (MMA N)
+constexpr int kBN = 192;   // tokens per tile (MMA N), the widest tile; narrower tiles (BN = 32, 64, 128)
+                           // serve calls with fewer activation rows
 constexpr int kBK = 128;   // columns per block (one scale block)
-constexpr int kStages = 3;                  // activation stages (+ TMEM operand + partial slots)
-constexpr int kWStages = 4;                 // fp8 weight stages
-constexpr uint32_t kXTile = kBN * kBK * 2;  // 48 KB f16
+// fp8 weight stages (8 stages beside the narrow tiles measured no faster:
+// 28-35 us either way for 17408x5120 at 16-64 tokens)
+template <int BN> constexpr int wstages() { return 4; }
+template <int BN> constexpr uint32_t x_tile() { return BN * kBK * 2; }  // f16 activation tile (48 KB at 192)
 constexpr uint32_t kWTile = kBM * kBK;      // 16 KB fp8
-constexpr uint32_t kXAtom = kBN * 128;      // one 64-column swizzle atom of the activation tile
+template <int BN> constexpr uint32_t x_atom() { return BN * 128; }  // one 64-column swizzle atom of it
 constexpr uint32_t kSpin = 1u << 22;
 constexpr int kWarpX = 0, kWarpMma = 1, kWarpW = 2, kWarpConv = 3;
 constexpr int kConvWarps = 4;                       // one thread per weight row
 constexpr int kWarpEpi = kWarpConv + kConvWarps;    // 7
-constexpr int kEpiGroups = kBN / 64;                // 64 token columns per epilogue warp
+constexpr int kEpiGroups = kBN / 64;                // 64 token columns per epilogue warp (widest tile)
 constexpr int kEpiWarps = 4 * kEpiGroups;           // 4 lane quadrants x 3 column groups
 constexpr int kWarpMma2 = kWarpEpi + kEpiWarps;     // 19: MMA issuer of the odd blocks
 constexpr int kThreads = (kWarpMma2 + 1) * 32;
-// TMEM columns: P0 | P1 (fp32 partials, kBN each) | A0 | A1 (64 each: 128 f16 per lane)
-constexpr uint32_t kTmemA = 2 * kBN;
+// Pipeline depth D: TMEM holds D fp32 partials P[0..D) (BN columns each)
+// and D converted weight operands A[0..D) (64 columns each: 128 f16 per
+// lane); block g uses P[g % D] and A[g % D].  The slot rings (activation
+// stages, ready[], done[]) have D + 1 slots.  D = 2 at every tile width:
+// D = 4 beside the narrow tiles (room in TMEM) measured no faster.
 constexpr uint32_t kACols = kBK / 2;
 constexpr uint32_t kTmemCols = 512;
-static_assert(kTmemA + 2 * kACols <= kTmemCols, "TMEM budget");
+template <int BN> constexpr int depth() { return 2; }
+template <int BN> constexpr int stages() { return depth<BN>() + 1; }
+template <int BN> constexpr uint32_t tmem_a() { return depth<BN>() * BN; }
+static_assert(depth<kBN>() * (kBN + kACols) <= kTmemCols && depth<64>() * (64 + kACols) <= kTmemCols &&
+                  depth<128>() * (128 + kACols) <= kTmemCols && depth<32>() * (32 + kACols) <= kTmemCols,
+              "TMEM budget");
 // arrivals that complete stage g: the activation producer (with the copy's
-// bytes), the converter warps (A[g % 2] written) and the epilogue warps
-// (P[g % 2] drained of block g - 2)
+// bytes), the converter warps (A[g % D] written) and the epilogue warps
+// (P[g % D] drained of block g - D)
 constexpr uint32_t kStageArrivals = 1 + kConvWarps + kEpiWarps;
 
 struct GemmArgs {
@@ -103,11 +117,14 @@ struct GemmArgs {
     uint32_t pair;        // rows 2t, 2t+1 are the hi and lo halves of token t: Y[t] = their sum
 };
 
-struct Smem {  // offsets from the 1024-aligned base
-    static constexpr uint32_t x(int s) { return s * kXTile; }
-    static constexpr uint32_t w(int s) { return kStages * kXTile + s * kWTile; }
-    static constexpr uint32_t bars = kStages * kXTile + kWStages * kWTile;
+template <int BN>
+struct Smem {  // offsets from the 1024-aligned base (every tile size is a multiple of 1024 B)
+    static constexpr uint32_t x(int s) { return s * x_tile<BN>(); }
+    static constexpr uint32_t w(int s) { return stages<BN>() * x_tile<BN>() + s * kWTile; }
+    static constexpr uint32_t bars = stages<BN>() * x_tile<BN>() + wstages<BN>() * kWTile;
+    static_assert(2 * stages<BN>() * 8 + 2 * wstages<BN>() * 8 + 4 <= 256, "barriers fit their 256 bytes");
     static constexpr uint32_t total = bars + 256;
+    static_assert(x_tile<BN>() % 1024 == 0 && x_atom<BN>() % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 };
 
 __device__ __forceinline__ uint32_t sa(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -178,17 +195,22 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
 }
 
 // kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B f16 (bits
-// 7-9 and 10-12 = 0), both K-major, N = 128 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16)
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+// 7-9 and 10-12 = 0), both K-major, N = BN (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16)
+template <int BN>
+constexpr uint32_t idesc()
+{
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M = 128 MMAs take N = 16..256 in steps of 16");
+    return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
 
 // D[tmem] (+)= A[tmem] * B[smem descriptor], issued by the leader lane
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t acc,
-                                           uint32_t leader)
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc_,
+                                           uint32_t acc, uint32_t leader)
 {
     asm volatile(
         "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 e, %5, 0;\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b), "r"(kIdesc), "r"(acc), "r"(leader)
+        "r"(a_tmem), "l"(b), "r"(idesc_), "r"(acc), "r"(leader)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t *bar, uint32_t leader)
@@ -242,20 +264,27 @@ __device__ __forceinline__ void promote16(float *acc, const uint32_t (&p)[16], f
     }
 }
 
+// BN = tokens per tile (the MMA's N): 192 for prefill; 32, 64 or 128 when the
+// call has at most that many activation rows, so a multi-token decode call
+// moves and multiplies only the columns it has.  Epilogue warps whose 64
+// columns lie past BN only take part in the barriers.
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fp8_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                        const __grid_constant__ GemmArgs a)
 {
+    using Sm = Smem<BN>;
+    constexpr int S = stages<BN>(), D = depth<BN>(), WS = wstages<BN>();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    // stage g uses slot g % kStages of both arrays:
+    // stage g uses slot g % S of both arrays:
     //   ready[s]: activation tile landed + A[g % 2] converted + P[g % 2] free -> MMA
     //   done[s]:  the MMA of block g completed (tcgen05.commit)          -> all
-    uint64_t *ready = reinterpret_cast<uint64_t *>(sm + Smem::bars);
-    uint64_t *done = ready + kStages;
-    uint64_t *w_full = done + kStages;      // [4] TMA -> converters
-    uint64_t *w_empty = w_full + kWStages;  // [4] converters -> TMA
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_empty + kWStages);
+    uint64_t *ready = reinterpret_cast<uint64_t *>(sm + Sm::bars);
+    uint64_t *done = ready + S;
+    uint64_t *w_full = done + S;            // [4] TMA -> converters
+    uint64_t *w_empty = w_full + WS;        // [WS] converters -> TMA
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_empty + WS);
 
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const uint32_t nkb = a.kblocks;
@@ -267,11 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (t == 32) {
-        for (int i = 0; i < kStages; ++i) {
+        for (int i = 0; i < S; ++i) {
             bar_init(&ready[i], kStageArrivals);
             bar_init(&done[i], 1);
         }
-        for (int i = 0; i < kWStages; ++i) {
+        for (int i = 0; i < WS; ++i) {
             bar_init(&w_full[i], 1);
             bar_init(&w_empty[i], kConvWarps);
         }
@@ -282,29 +311,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    // Ordering argument for the shared slot rings (kStages >= 3): every
-    // arrival for block g on ready[g % 3] comes after done(g - 2) or
-    // done(g - 3), so the slot has finished its phase for block g - 3; and no
-    // waiter on done(h) can be overtaken by done(h + 3), which needs that
-    // waiter's own later arrival first.
+    // Ordering argument for the shared slot rings (S = D + 1 slots): every
+    // arrival for block g on ready[g % S] comes, in its party's program
+    // order, after that party waited on done(g - S) (the producer directly;
+    // a converter or epilogue thread while handling an earlier block), so the
+    // slot has finished its phase for block g - S; and no waiter on done(h)
+    // can be overtaken by done(h + S), which needs that waiter's own later
+    // arrival first.
     if (warp == kWarpX) {
         // ---------------- activation producer (whole warp) -----------------
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
-            const int m0 = (int)((tile % a.mtiles) * kBN);
+            const int m0 = (int)((tile % a.mtiles) * BN);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int s = g % kStages;
-                if (g >= (uint32_t)kStages) ok = __all_sync(0xffffffffu, bar_wait(&done[s], ((g / kStages) - 1) & 1));
+                const int s = g % S;
+                if (g >= (uint32_t)S) ok = __all_sync(0xffffffffu, bar_wait(&done[s], ((g / S) - 1) & 1));
                 if (!ok) break;
-                bar_expect(&ready[s], kXTile, leader);
-                tma_2d(sm + Smem::x(s), &map_x, (int)(kb * kBK), m0, &ready[s], leader);
-                tma_2d(sm + Smem::x(s) + kXAtom, &map_x, (int)(kb * kBK + 64), m0, &ready[s], leader);
+                bar_expect(&ready[s], x_tile<BN>(), leader);
+                tma_2d(sm + Sm::x(s), &map_x, (int)(kb * kBK), m0, &ready[s], leader);
+                tma_2d(sm + Sm::x(s) + x_atom<BN>(), &map_x, (int)(kb * kBK + 64), m0, &ready[s], leader);
             }
         }
         // wait (bounded) for the copies still in flight
-        for (uint32_t i = g > (uint32_t)kStages ? g - kStages : 0; i < g; ++i)
-            bar_wait(&ready[i % kStages], (i / kStages) & 1);
+        for (uint32_t i = g > (uint32_t)S ? g - S : 0; i < g; ++i)
+            bar_wait(&ready[i % S], (i / S) & 1);
     } else if (warp == kWarpW) {
         // ---------------- weight producer (whole warp) ---------------------
         uint32_t g = 0;
@@ -312,14 +343,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             const int n0 = (int)((tile / a.mtiles) * kBM);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int s = g % kWStages;
-                if (g >= (uint32_t)kWStages) ok = __all_sync(0xffffffffu, bar_wait(&w_empty[s], ((g / kWStages) - 1) & 1));
+                const int s = g % WS;
+                if (g >= (uint32_t)WS) ok = __all_sync(0xffffffffu, bar_wait(&w_empty[s], ((g / WS) - 1) & 1));
                 if (!ok) break;
                 bar_expect(&w_full[s], kWTile, leader);
-                tma_2d(sm + Smem::w(s), &map_w, (int)(kb * kBK), n0, &w_full[s], leader);
+                tma_2d(sm + Sm::w(s), &map_w, (int)(kb * kBK), n0, &w_full[s], leader);
             }
         }
-        drain(w_full, kWStages, g);
+        drain(w_full, WS, g);
     } else if (warp == kWarpMma || warp == kWarpMma2) {
         // ---------------- MMA issuers (whole warp, lane 0 issues) -----------
         // A thread issuing tcgen05.mma blocks until the tensor pipe takes the
@@ -332,23 +363,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 if ((g & 1) != parity) continue;
-                const int s = g % kStages, j = g & 1;
-                ok = __all_sync(0xffffffffu, bar_wait(&ready[s], (g / kStages) & 1));
+                const int s = g % S, j = g % D;
+                ok = __all_sync(0xffffffffu, bar_wait(&ready[s], (g / S) & 1));
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t xbase = sa(sm + Smem::x(s));
-                const uint32_t d = tmem + j * kBN, acol = tmem + kTmemA + j * kACols;
+                const uint32_t xbase = sa(sm + Sm::x(s));
+                const uint32_t d = tmem + j * BN, acol = tmem + tmem_a<BN>() + j * kACols;
 #pragma unroll
                 for (int ks = 0; ks < kBK / 16; ++ks) {
-                    const uint32_t off = (ks >> 2) * kXAtom + (ks & 3) * 32;
-                    mma_f16_ts(d, acol + ks * 8, sw128_desc(xbase + off), ks > 0, leader);
+                    const uint32_t off = (ks >> 2) * x_atom<BN>() + (ks & 3) * 32;
+                    mma_f16_ts(d, acol + ks * 8, sw128_desc(xbase + off), idesc<BN>(), ks > 0, leader);
                 }
                 mma_commit(&done[s], leader);
                 last = g;
             }
         }
         // this warp's last block must have completed before the CTA can free TMEM
-        if (ok && last != 0xFFFFFFFFu) bar_wait(&done[last % kStages], (last / kStages) & 1);
+        if (ok && last != 0xFFFFFFFFu) bar_wait(&done[last % S], (last / S) & 1);
     } else if (warp < kWarpEpi) {
         // ---------------- converters: fp8 -> f16 into TMEM -------------------
         // Thread = weight row = TMEM lane (warp w may access lanes 32*(w%4)..).
@@ -358,18 +389,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t quad = warp & 3;
         const uint32_t r = quad * 32 + lane;
         const uint32_t sw = r & 7;
-        const uint32_t lane_base = tmem + ((quad * 32) << 16) + kTmemA;
+        const uint32_t lane_base = tmem + ((quad * 32) << 16) + tmem_a<BN>();
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int s = g % kWStages, j = g & 1;
-                ok = bar_wait(&w_full[s], (g / kWStages) & 1);
-                // A[g % 2] was last read by block g - 2
-                if (ok && g >= 2) ok = bar_wait(&done[(g - 2) % kStages], ((g - 2) / kStages) & 1);
+                const int s = g % WS, j = g % D;
+                ok = bar_wait(&w_full[s], (g / WS) & 1);
+                // A[g % D] was last read by block g - D
+                if (ok && g >= (uint32_t)D) ok = bar_wait(&done[(g - D) % S], ((g - D) / S) & 1);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint8_t *wrow = sm + Smem::w(s) + r * 128;
+                const uint8_t *wrow = sm + Sm::w(s) + r * 128;
                 uint4 v[8];
 #pragma unroll
                 for (uint32_t c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4 *>(wrow + ((c ^ sw) << 4));
@@ -391,44 +422,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) bar_arrive(&ready[g % kStages]);
+                if (lane == 0) bar_arrive(&ready[g % S]);
             }
         }
     } else {
         // ---------------- epilogue: promotion and store -----------------------
         const uint32_t quad = warp & 3;                         // TMEM lanes this warp may touch
         const uint32_t grp = (warp - kWarpEpi) >> 2;            // token columns 64*grp ..
+        // columns of this warp inside the tile (all 64 in the widest tile)
+        const int ncol = BN == kBN ? 64 : (BN - 64 * (int)grp < 0 ? 0 : (BN - 64 * (int)grp > 64 ? 64 : BN - 64 * (int)grp));
         const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * 64;
-        // P[0] and P[1] start out free for blocks 0 and 1
-        if (lane == 0) {
-            bar_arrive(&ready[0]);
-            bar_arrive(&ready[1]);
-        }
+        // P[0..D) start out free for blocks 0..D-1
+        if (lane == 0)
+            for (int i = 0; i < D; ++i) bar_arrive(&ready[i]);
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             const uint32_t rb = tile / a.mtiles;
             const uint32_t n = rb * kBM + quad * 32 + lane;               // weight row
-            const uint32_t t0 = (tile % a.mtiles) * kBN + grp * 64;       // first token
+            const uint32_t t0 = (tile % a.mtiles) * BN + grp * 64;        // first token
             const float *srow = a.S + (size_t)rb * nkb;
             float acc[64];
             float sc = __ldg(srow);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int j = g & 1;
+                const int j = g % D;
                 const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
-                ok = bar_wait(&done[g % kStages], (g / kStages) & 1);
+                ok = bar_wait(&done[g % S], (g / S) & 1);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    uint32_t p[16];
-                    tmem_ld16(tbase + j * kBN + c * 16, p);
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    promote16(acc + 16 * c, p, sc, kb == 0);
+                    if (16 * c < ncol) {  // warp-uniform
+                        uint32_t p[16];
+                        tmem_ld16(tbase + j * BN + c * 16, p);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        promote16(acc + 16 * c, p, sc, kb == 0);
+                    }
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) bar_arrive(&ready[(g + 2) % kStages]);  // P[g % 2] is free for block g + 2
+                if (lane == 0) bar_arrive(&ready[(g + D) % S]);  // P[g % D] is free for block g + D
                 sc = sc_next;
             }
             if (ok && n < a.N) {
@@ -436,14 +469,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const uint32_t tok2 = t0 + 2 * i;
-                        if (tok2 < a.m)
+                        if (2 * i < ncol && tok2 < a.m)
                             a.Y[(size_t)(tok2 >> 1) * a.N + n] = (acc[2 * i] + acc[2 * i + 1]) * __ldg(a.tscale + tok2);
                     }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 64; ++i) {
                         const uint32_t tok = t0 + i;
-                        if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                        if (i < ncol && tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
                     }
                 }
             }
@@ -654,36 +687,53 @@ int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *
     return Q35CU_OK;
 }
 
-int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
-                    cudaStream_t st, bool pair)
+namespace {
+
+template <int BN>
+int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
+                   cudaStream_t st, bool pair)
 {
     const uint32_t N = w->rows, K = w->cols;
-    if (!m) return Q35CU_OK;
-    if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
-    if (((uintptr_t)Xh % 16) || ((uintptr_t)w->d_w % 16)) return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned operand");
-    const uint64_t mtiles = (m + kBN - 1) / kBN, ntiles = mtiles * ((N + kBM - 1) / kBM);
+    const uint64_t mtiles = (m + BN - 1) / BN, ntiles = mtiles * ((N + kBM - 1) / kBM);
     if (ntiles > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: shape too large");
     CUtensorMap mx, mw;
-    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xh, K, m, (uint64_t)K * 2, 64, kBN);
+    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xh, K, m, (uint64_t)K * 2, 64, BN);
     if (rc) return rc;
     rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
     if (rc) return rc;
     GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, pair ? 1u : 0u};
-    static bool configured[64] = {};
+    static bool configured[64] = {};  // per instantiation and device
     int dev = 0, sms = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));
     rc = sm_count_of(dev, &sms);
     if (rc) return rc;
-    const size_t smem = Smem::total + 1024;
+    const size_t smem = Smem<BN>::total + 1024;
     if (!configured[dev]) {
-        Q35CU_CUDA(cudaFuncSetAttribute(gemm_fp8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        Q35CU_CUDA(cudaFuncSetAttribute(gemm_fp8_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured[dev] = true;
     }
     const uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
-    gemm_fp8_tc_kernel<<<grid, kThreads, smem, st>>>(mx, mw, a);
+    gemm_fp8_tc_kernel<BN><<<grid, kThreads, smem, st>>>(mx, mw, a);
     count_launch();
     Q35CU_CUDA(cudaGetLastError());
     return Q35CU_OK;
+}
+
+}  // namespace
+
+int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
+                    cudaStream_t st, bool pair)
+{
+    const uint32_t K = w->cols;
+    if (!m) return Q35CU_OK;
+    if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
+    if (((uintptr_t)Xh % 16) || ((uintptr_t)w->d_w % 16)) return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned operand");
+    // the narrowest token tile that holds all m activation rows, up to 128;
+    // wider calls take 192-row tiles (the prefill shape)
+    if (m <= 32) return launch_gemm_bn<32>(w, Xh, tscale, m, Y, st, pair);
+    if (m <= 64) return launch_gemm_bn<64>(w, Xh, tscale, m, Y, st, pair);
+    if (m <= 128) return launch_gemm_bn<128>(w, Xh, tscale, m, Y, st, pair);
+    return launch_gemm_bn<kBN>(w, Xh, tscale, m, Y, st, pair);
 }
 
 // ---------------------------------------------------------------------------

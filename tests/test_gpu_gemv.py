@@ -74,6 +74,16 @@ def test_config1_batch_sweep(gpu, orc, ref, shape, m):
     _check(orc, W, sc, X, Y, ref.mm_fp8_batch(W, sc, X), f"C1 {shape} m={m}")
 
 
+@pytest.mark.parametrize("n", [16, 17, 32, 33, 64, 65, 127])
+def test_exact_tensor_core_tile_widths(gpu, orc, ref, n):
+    """q35_mm_fp8_batch with 16..127 tokens runs the tensor cores on exact
+    (hi/lo split) activations, 2n rows: a 32-, 64-, 128- or 192-row token
+    tile (n = 16 | 17..32 | 33..64 | 65..127), each within the GEMV bound."""
+    W, sc = _synth(orc, 70 + n, 1000, 5120)
+    X = orc.synth_act(90 + n, (n, 5120))
+    _check(orc, W, sc, X, q35cu.mm_fp8_batch(W, sc, X), ref.mm_fp8_batch(W, sc, X), f"n={n}")
+
+
 def test_batch_equals_single_bitwise(gpu, orc):
     """qwen35-c/tests/test_batch_mm.c on the GPU: batch == n x single == multi4."""
     rows, cols, n = 10240, 5120, 5

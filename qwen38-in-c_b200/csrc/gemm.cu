@@ -40,12 +40,12 @@
 //     so the MMA warp waits on one barrier per 128-column block (the TMA,
 //     the converters and the epilogue all arrive on it) and commits once.
 //
-// Roles (640 threads):
-//   warp 0      TMA producer of the activation tile [192 tokens x 128 cols]
+// Roles (640 threads; BN = tokens per tile, 192 unless the call is narrower):
+//   warp 0      TMA producer of the activation tile [BN tokens x 128 cols]
 //               f16 (two 64-column boxes, 128B swizzle), 3 stages;
 //   warps 1, 19 lane 0 issues tcgen05.mma kind::f16 (A = the weight tile from
 //               TMEM, M = 128; B = the activation tile from shared memory,
-//               N = 192; 8 steps of K = 16) into TMEM partial P[g % 2];
+//               N = BN; 8 steps of K = 16) into TMEM partial P[g % 2];
 //               warp 1 takes the even blocks, warp 19 the odd ones;
 //   warp 2      TMA producer of the fp8 weight tile [128 rows x 128 B],
 //               4 stages released by the converters;
@@ -53,7 +53,7 @@
 //               row to f16 and stores it with tcgen05.st into A[g % 2]
 //               (64 TMEM columns, two f16 per column along K);
 //   warps 7-18  epilogue: warp w owns TMEM lanes 32*(w%4).. (one weight row
-//               per thread) and 64 of the 192 token columns; it keeps the
+//               per thread) and 64 of the BN token columns; it keeps the
 //               tile's accumulator in registers, ACC += s[n/128, kb] * P per
 //               128-column block (the block scale stays out of the MMA
 //               operands, which stay exact), and stores Y after the last block.

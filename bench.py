@@ -7,18 +7,25 @@ Headline workload (``value``): benchmark configuration 3 -- one full
 64-layer FP8 decode weight stream (48 Gated-DeltaNet + 16 GQA layers, the
 configuration-2 projection shapes plus the MLP in every layer, 24.33 GB of
 FP8 weights), one token, tensor-parallel over the N GPUs (column-parallel +
-NCCL all-gather, row-parallel + NCCL all-reduce), captured in one CUDA graph
-per rank.  ``value`` = weight bytes streamed by all ranks / step time (GB/s),
-``ms_per_step`` = ms per decode token.  Inputs are resident in HBM; the
-weights (24.33 GB / N per GPU) are far larger than L2, so every step reads
-them from DRAM.
+all-gather, row-parallel + all-reduce), captured in one CUDA graph (or run as
+one cooperative launch) per rank.  ``value`` = weight bytes streamed by all
+ranks / step time (GB/s), ``ms_per_step`` = ms per decode token.  Inputs are
+resident in HBM; the weights (24.33 GB / N per GPU) are far larger than L2,
+so every step reads them from DRAM.
 
-Also reported on the same line: the isolated decode GEMV of configuration 0
-(17408x5120, five rotating weight copies so L2 never holds the next one) and
-the configuration-1 sweep (gate/up and down at M in {1,4,16,64}) -- rank 0,
-N=1 only; the live roofline of the dominant kernel; the end-to-end figure
-through the reference-facing C-ABI with host buffers; the CPU baseline
-(the reference's own q35_mm.c, compiled from its sources) on the host cores.
+Also on the same line: the live roofline of the dominant kernel; the
+end-to-end figure through the reference-facing C-ABI with host buffers; and,
+each measured in a child process of its own so that a failure there cannot
+take the headline with it (its key then holds {"error": ...}):
+configuration 0 (the isolated decode GEMV), the configuration-1 sweep, the
+bf16 lm_head matvec, configuration 2 (one layer's prefill GEMMs at M=2048),
+configuration 4 (M=8192 prefill through the projection set, under TP at
+N>1) and the CPU baseline (the reference's own q35_mm.c on the host cores,
+the full 64-layer stream).
+
+``--impl reference`` runs the reference's CPU implementation
+(oracle/_ref/libq35ref.so, qwen35-c/src/q35_mm.c compiled unmodified) over
+the same 64-layer stream, K timed steps after W warm-up steps.
 
 For N > 1 launch with torchrun (one process per GPU, rendezvous on
 127.0.0.1); rank 0 prints the single JSON line.
@@ -41,16 +48,20 @@ sys.path.insert(0, os.path.join(REPO, "qwen38-in-c_b200"))
 METRIC = "FP8 decode GEMV HBM GB/s (% peak); prefill GEMM TFLOP/s; 64-layer ms/token"
 HBM_FALLBACK_GBS = 6650.0
 BF16_FALLBACK_TFLOPS = 1590.0
+EXTRAS = ("c0", "c1", "lm_head", "c2", "c4", "cpu")
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=64, help="decode-stack depth (64 = configuration 3)")
-    ap.add_argument("--no-extras", action="store_true", help="skip the C0/C1 sweep, e2e and CPU baseline")
+    ap.add_argument("--no-extras", action="store_true", help="skip the extras, e2e and the CPU baseline")
+    ap.add_argument("--extra", choices=EXTRAS, default=None,
+                    help="run one extra measurement and print its JSON (the child-process mode)")
+    ap.add_argument("--cpu-steps", type=int, default=3, help="timed steps of the CPU baseline (our arm)")
     ap.add_argument("--profile-c0", action="store_true",
                     help="only the isolated configuration-0 GEMV (a small command for ncu captures)")
     ap.add_argument("--profile-c2", action="store_true",
@@ -60,7 +71,7 @@ def parse():
                          "activations (q35cu_gemv_fp8_tc), --steps calls (for ncu captures)")
     ap.add_argument("--profile-lm-head", type=int, default=0, metavar="ROWS",
                     help="only the bf16 lm_head matvec on ROWS x 5120, --steps calls (for ncu captures)")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def peaks():
@@ -126,49 +137,102 @@ class Clocks:
 # ---------------------------------------------------------------------------
 # the reference arm / CPU baseline: qwen35-c's q35_mm.c on the host cores
 # ---------------------------------------------------------------------------
-def cpu_layer_sample():
-    """Host weights for one DeltaNet and one GQA layer (the per-layer-kind
-    projections of the decode chain), seeded like the GPU run."""
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import oracle  # noqa: F401  (test infrastructure: CPU baseline only)
+def cpu_info() -> dict:
+    """The host CPU as this process sees it: model, the logical CPUs it may
+    run on, and how many physical cores those are (SMT siblings counted once;
+    the reference's own thread heuristic is 5/3 x physical cores,
+    qwen35-c/src/cli/cli_common.c:98-104)."""
+    allowed = os.sched_getaffinity(0)
+    model, phys, per_core = None, set(), {}
+    try:
+        with open("/proc/cpuinfo") as f:
+            for rec in f.read().split("\n\n"):
+                d = {}
+                for line in rec.splitlines():
+                    if ":" in line:
+                        k, v = line.split(":", 1)
+                        d[k.strip()] = v.strip()
+                if "processor" not in d or int(d["processor"]) not in allowed:
+                    continue
+                model = model or d.get("model name")
+                key = (d.get("physical id"), d.get("core id"))
+                phys.add(key)
+                per_core[key] = per_core.get(key, 0) + 1
+    except OSError:
+        pass
+    n_phys = len(phys) or None
+    return {"model": model, "logical_cpus": len(allowed), "physical_cores": n_phys,
+            "smt": bool(per_core) and max(per_core.values()) > 1,
+            "heuristic_threads_5_3": (min(len(allowed), n_phys * 5 // 3) if n_phys else None)}
+
+
+class CpuStream:
+    """The 64-layer decode weight stream (configuration 3) in host memory, for
+    the reference's CPU matmul.  Layers 0 (DeltaNet) and 3 (GQA) are
+    generated with the seeded generator the GPU stack uses (same seeds, same
+    N(0, 0.02) 128x128 block quantisation); every other layer holds a
+    byte-rotated copy of the weights of its kind (a different rotation per
+    layer), so each layer is distinct memory with the same value distribution
+    -- the reference's converter speed depends on the bytes, not on which
+    values sit where.  24.33 GB of FP8 weights in all."""
+
+    def __init__(self, n_layers: int = 64):
+        import numpy as np
+
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle  # noqa: F401  (test infrastructure: the CPU baseline / reference arm only)
+        import stack
+
+        self.orc = oracle.Oracle()
+        base = {}
+        for layer, kind in ((0, "dn"), (3, "gqa")):
+            ws = {}
+            for name, rows in (stack.DN_COL if kind == "dn" else stack.GQA_COL):
+                ws[name] = self.orc.synth_fp8(stack.seed_of(layer, name), rows, stack.HIDDEN)
+            ao = "out" if kind == "dn" else "o"
+            ws[ao] = self.orc.synth_fp8(stack.seed_of(layer, ao), stack.HIDDEN, stack.OUT_K)
+            ws["gate"] = self.orc.synth_fp8(stack.seed_of(layer, "gate"), stack.MLP, stack.HIDDEN)
+            ws["up"] = self.orc.synth_fp8(stack.seed_of(layer, "up"), stack.MLP, stack.HIDDEN)
+            ws["down"] = self.orc.synth_fp8(stack.seed_of(layer, "down"), stack.HIDDEN, stack.MLP)
+            base[kind] = ws
+        self.layers = []
+        for i, kind in enumerate(stack.layer_kinds(n_layers)):
+            if i in (0, 3):
+                self.layers.append((kind, base[kind]))
+                continue
+            rot = {}
+            for j, (name, (W, sc)) in enumerate(base[kind].items()):
+                shift = (i * 7919 + j * 104729) % W.size
+                rot[name] = (np.roll(W.reshape(-1), shift).reshape(W.shape), sc)
+            self.layers.append((kind, rot))
+        self.x = self.orc.synth_act(77, (n_layers, stack.HIDDEN))
+        self.weight_bytes = sum(W.nbytes for _, ws in self.layers for W, _ in ws.values())
+
+    def step(self, mm_fp8, mm_multi4) -> None:
+        """One decode step: every layer's projections in the engine's order
+        (q35_deltanet.c:329,360 / q35_attn.c:273-275,262 / q35_model.c:934,937)."""
+        import stack
+
+        for i, (kind, ws) in enumerate(self.layers):
+            names = [n for n, _ in (stack.DN_COL if kind == "dn" else stack.GQA_COL)]
+            outs = mm_multi4([ws[n][0] for n in names], [ws[n][1] for n in names], self.x[i])[: len(names)]
+            src = outs[-1] if kind == "dn" else outs[0]
+            ao = ws["out" if kind == "dn" else "o"]
+            o = mm_fp8(ao[0], ao[1], src[: stack.OUT_K].copy())
+            g, _ = mm_multi4([ws["gate"][0], ws["up"][0]], [ws["gate"][1], ws["up"][1]], o)[:2]
+            mm_fp8(ws["down"][0], ws["down"][1], g)
+
+
+def time_cpu_stream(steps: int, warmup: int) -> dict:
+    """The reference q35_mm.c (oracle/_ref, AVX2 + FMA + OpenMP, every host
+    CPU this process may use; the oracle port if _ref was not built) over
+    the full 64-layer stream: `warmup` untimed steps, then `steps` timed ones
+    (wall clock, their mean)."""
     import stack
 
-    orc = oracle.Oracle()
-    ws = {}
-    for layer, kind in ((0, "dn"), (3, "gqa")):
-        cols = stack.DN_COL if kind == "dn" else stack.GQA_COL
-        for name, rows in cols:
-            ws[(layer, name)] = orc.synth_fp8(stack.seed_of(layer, name), rows, stack.HIDDEN)
-        ao = "out" if kind == "dn" else "o"
-        ws[(layer, ao)] = orc.synth_fp8(stack.seed_of(layer, ao), stack.HIDDEN, stack.OUT_K)
-        ws[(layer, "gate")] = orc.synth_fp8(stack.seed_of(layer, "gate"), stack.MLP, stack.HIDDEN)
-        ws[(layer, "up")] = orc.synth_fp8(stack.seed_of(layer, "up"), stack.MLP, stack.HIDDEN)
-        ws[(layer, "down")] = orc.synth_fp8(stack.seed_of(layer, "down"), stack.HIDDEN, stack.MLP)
-    x = orc.synth_act(77, (2, stack.HIDDEN))
-    return orc, ws, x
-
-
-def layer_chain(mm_fp8, mm_multi4, ws, layer, kind, x):
-    """One layer of the decode chain through host-pointer matmul entry points."""
-    import stack
-
-    cols = stack.DN_COL if kind == "dn" else stack.GQA_COL
-    outs = mm_multi4([ws[(layer, n)][0] for n, _ in cols], [ws[(layer, n)][1] for n, _ in cols], x)[: len(cols)]
-    src = outs[-1] if kind == "dn" else outs[0]
-    ao = ws[(layer, "out" if kind == "dn" else "o")]
-    o = mm_fp8(ao[0], ao[1], src[: stack.OUT_K].copy())
-    g, u = mm_multi4([ws[(layer, "gate")][0], ws[(layer, "up")][0]], [ws[(layer, "gate")][1], ws[(layer, "up")][1]], o)[:2]
-    d = ws[(layer, "down")]
-    return mm_fp8(d[0], d[1], g)
-
-
-def time_cpu_reference(steps: int, warmup: int):
-    """Reference q35_mm.c (oracle/_ref, or the oracle port if it was not built)
-    over one DeltaNet + one GQA layer per step, all host threads."""
-    import stack
-
-    orc, ws, x = cpu_layer_sample()
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    t_setup = time.perf_counter()
+    cs = CpuStream()
+    setup_s = time.perf_counter() - t_setup
     import oracle
 
     if oracle.Reference.available():
@@ -177,30 +241,27 @@ def time_cpu_reference(steps: int, warmup: int):
         mm_fp8, mm_multi4 = R.mm_fp8, R.mm_fp8_multi4
     else:
         kind = "port"
-        mm_fp8 = orc.mm_fp8
+        mm_fp8 = cs.orc.mm_fp8
 
         def mm_multi4(Ws, Ss, xx):
-            return [orc.mm_fp8(w, s, xx) for w, s in zip(Ws, Ss)]
-    sample_bytes = sum(w.nbytes for w, _ in ws.values())
-    times = {"dn": [], "gqa": []}
-    for i in range(warmup + steps):
-        for layer, k in ((0, "dn"), (3, "gqa")):
-            t0 = time.perf_counter()
-            layer_chain(mm_fp8, mm_multi4, ws, layer, k, x[0 if k == "dn" else 1])
-            dt = time.perf_counter() - t0
-            if i >= warmup:
-                times[k].append(dt)
-    t_dn, t_gqa = statistics.median(times["dn"]), statistics.median(times["gqa"])
-    n_dn = sum(1 for k in stack.layer_kinds() if k == "dn")
-    n_gqa = stack.N_LAYERS - n_dn
-    step_s = n_dn * t_dn + n_gqa * t_gqa  # extrapolated to 64 layers
-    gbs = stack.weight_bytes() / step_s / 1e9
+            return [cs.orc.mm_fp8(w, s, xx) for w, s in zip(Ws, Ss)]
+    for _ in range(warmup):
+        cs.step(mm_fp8, mm_multi4)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        cs.step(mm_fp8, mm_multi4)
+        times.append(time.perf_counter() - t0)
+    step_s = sum(times) / len(times)
+    info = cpu_info()
     return {
-        "value": gbs, "unit": "GB/s", "cores": orc.threads(), "kind": kind,
-        "ms_per_step_extrapolated": step_s * 1e3,
-        "sample": f"one DeltaNet + one GQA layer chain per step ({sample_bytes / 1e6:.0f} MB FP8), median of "
-                  f"{steps} steps after {warmup} warm-up, extrapolated x48/x16 to the 64-layer stream",
+        "value": stack.weight_bytes() / step_s / 1e9, "unit": "GB/s", "cores": cs.orc.threads(), "kind": kind,
+        "ms_per_step": step_s * 1e3, "ms_per_step_min": min(times) * 1e3, "steps": steps, "warmup": warmup,
+        "sample": f"the full {len(cs.layers)}-layer decode weight stream per step ({cs.weight_bytes / 1e9:.2f} GB "
+                  f"FP8, 256 q35_mm_fp8 / q35_mm_fp8_multi4 calls), mean of {steps} timed steps after {warmup} "
+                  f"warm-up; {cs.orc.threads()} OpenMP threads",
         "impl": "q35_mm.c compiled -O2 -mavx2 -mfma -fopenmp" if kind == "reference" else "oracle C port",
+        "cpu": info, "setup_s": round(setup_s, 1),
     }
 
 
@@ -208,16 +269,17 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cb = time_cpu_reference(max(1, args.steps // 4), max(1, args.warmup // 2))
+    cb = time_cpu_stream(args.steps, args.warmup)
     line = {
         "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": cb["ms_per_step_extrapolated"], "higher_is_better": True,
+        "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (FP8 e4m3 weights, bf16 scales)",
         "data": "synthetic (seeded N(0,0.02) weights, 128x128 block-quantised; N(0,1) activations)",
         "config": {"workload": "configuration 3: 64-layer FP8 decode weight stream, M=1",
                    "weight_bytes_per_step": __import__("stack").weight_bytes()},
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu": cb["cpu"],
         "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -407,95 +469,189 @@ def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
             "by_projection": per}
 
 
-def time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, m=8192, reps=3, scheme="literal"):
+# ---------------------------------------------------------------------------
+# process setup shared by the main run and the child processes
+# ---------------------------------------------------------------------------
+class Dist:
+    """One process per GPU: torch.distributed (NCCL; gloo for host objects),
+    the library's NCCL communicator and its NVLink exchange areas."""
+
+    def __init__(self, want_p2p: bool = True):
+        import torch
+        import torch.distributed as dist
+
+        import q35cu
+
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.p2p = False
+        torch.cuda.set_device(self.local)
+        q35cu.load()
+        q35cu.check(q35cu.load().q35cu_set_device(self.local))
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.cpu_group = dist.new_group(backend="gloo")
+            uid = [q35cu.nccl_unique_id() if self.rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0, group=self.cpu_group)
+            q35cu.tp_init(self.rank, self.world, uid[0])
+            if want_p2p:
+                # the one-shot NVLink collectives: every rank's exchange-area handle
+                hs = [None] * self.world
+                dist.all_gather_object(hs, q35cu.p2p_handle(), group=self.cpu_group)
+                q35cu.p2p_open(self.rank, self.world, hs)
+                self.p2p = True
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        import q35cu
+
+        if self.world > 1:
+            self.torch.cuda.synchronize()
+            self.dist.barrier()
+            if self.p2p:
+                q35cu.p2p_close()
+            q35cu.tp_finalize()
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def time_config4(d: Dist, bf16_peak, m=8192, reps=3, scheme="literal"):
     """Configuration 4: long prefill (M=8192 tokens) through the 64-layer
-    projection set under tensor parallelism, on this stack's shards.  Literal
-    scheme: column-parallel GEMMs + NCCL all-gather of their [M, N/p] outputs,
-    row-parallel GEMMs + NCCL all-reduce of the [M, 5120] partials (100+ MB
-    messages: NCCL's regime).  One DeltaNet and one GQA layer are timed (CUDA
-    events, median of `reps`, max over ranks) and extrapolated x48 / x16; the
-    activations are bf16-rounded N(0,1), converted by the library."""
+    projection set under tensor parallelism, on this rank's shards of a
+    4-layer stack (layers 0-2 DeltaNet, layer 3 GQA; every layer of a kind has
+    the same shapes).  One DeltaNet and one GQA layer (prefill.PrefillLayers:
+    the engine's batch-prefill projection order, every GEMM through
+    q35cu_gemm_fp8) are timed with CUDA events (median of `reps`, max over
+    ranks) and extrapolated x48 / x16.  The device status word is read after
+    the warm-up and after the timed runs, so a wait that gave up is reported
+    as such rather than as a wrong number."""
+    import q35cu
+    import prefill
     import stack
 
-    dn = next(L for L in st.layers if L.kind == "dn")
-    gqa = next(L for L in st.layers if L.kind == "gqa")
-    dev = torch.device("cuda", torch.cuda.current_device())
-    f32 = dict(dtype=torch.float32, device=dev)
-    x = torch.randn((m, stack.HIDDEN), device=dev).to(torch.bfloat16)
-    kmax = max(stack.HIDDEN, dn.down.window[3], dn.attn_out.window[3])
-    work = torch.empty(q35cu.gemm_workspace_bytes(m, kmax), dtype=torch.uint8, device=dev)
-    xb = torch.empty((m * kmax,), dtype=torch.bfloat16, device=dev)
-    o = torch.empty((m, stack.HIDDEN), **f32)
-    y = torch.empty((m, stack.HIDDEN), **f32)
-    col = {p.name: torch.empty((m, p.window[1]), **f32) for L in (dn, gqa) for p in L.col_in}
-    gath = {k: torch.empty((world * v.numel(),), **f32) for k, v in col.items()} if world > 1 else {}
-    g_n = dn.gate.window[1]
-    gu = {n: torch.empty((m, g_n), **f32) for n in ("gate", "up")}
-    gu_g = {n: torch.empty((world * m * g_n,), **f32) for n in gu} if world > 1 else {}
-    attn = torch.randn((m, gqa.attn_out.window[3]), **f32)  # stands in for the local heads' attention output
-
-    def bf16(src):
-        n = src.numel()
-        q35cu.f32_to_bf16(src, xb[:n])
-        return xb[:n].view(src.shape[0], -1)
-
-    def gemm(w, xin, yout):
-        q35cu.gemm(w, xin.view(torch.int16), yout, work)
-
-    literal = scheme == "literal"
-
-    def layer(L):
-        for p in L.col_in:
-            gemm(p.w, x, col[p.name])
-            if world > 1 and literal:
-                q35cu.allgather(col[p.name], gath[p.name])
-        src = col["z"] if L.kind == "dn" else attn
-        gemm(L.attn_out.w, bf16(src), o)
-        if world > 1:
-            q35cu.allreduce(o)
-        xo = bf16(o)
-        gemm(L.gate.w, xo, gu["gate"])
-        gemm(L.up.w, xo, gu["up"])
-        if world > 1 and literal:
-            for n in ("gate", "up"):
-                q35cu.allgather(gu[n], gu_g[n])
-        gemm(L.down.w, bf16(gu["gate"]), y)
-        if world > 1:
-            q35cu.allreduce(y)
-
-    def flops(L):
-        return 2.0 * m * sum(p.window[1] * p.window[3] for p in L.col_in + [L.attn_out, L.gate, L.up, L.down])
-
-    out = {}
-    for name, L in (("dn", dn), ("gqa", gqa)):
-        layer(L)  # warm-up
-        torch.cuda.synchronize()
-        barrier()
-        ts = []
-        for _ in range(reps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            layer(L)
-            e1.record()
+    torch = d.torch
+    st = stack.Stack(d.rank, d.world, n_layers=4)
+    try:
+        pf = prefill.PrefillLayers(st, m=m, scheme=scheme)
+        out = {}
+        for name, L in (("dn", pf.dn), ("gqa", pf.gqa)):
+            pf.layer(L)  # warm-up
             torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        barrier()
-        out[name] = max_over_ranks(statistics.median(ts))
-        out[name + "_flops_rank"] = flops(L)
-    n_dn = sum(1 for L in st.layers if L.kind == "dn")
-    n_gqa = len(st.layers) - n_dn
+            q35cu.check_device_status()
+            d.barrier()
+            ts = []
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                pf.layer(L)
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            q35cu.check_device_status()
+            d.barrier()
+            out[name] = d.max_over_ranks(statistics.median(ts))
+            out[name + "_flops_rank"] = pf.flops(L)
+    finally:
+        st.free()
+    kinds = stack.layer_kinds()
+    n_dn = sum(1 for k in kinds if k == "dn")
+    n_gqa = len(kinds) - n_dn
     ms = n_dn * out["dn"] + n_gqa * out["gqa"]
-    total_flops = 2.0 * m * stack.weight_bytes(len(st.layers))  # every rank's shards: the whole model
+    total_flops = 2.0 * m * stack.weight_bytes()  # every rank's shards: the whole model
     rank_flops = n_dn * out["dn_flops_rank"] + n_gqa * out["gqa_flops_rank"]
+    literal = scheme == "literal"
     return {"m": m, "ms_per_pass_extrapolated": round(ms, 2), "tflop_per_pass": round(total_flops / 1e12, 1),
             "TFLOPs": round(total_flops / (ms * 1e-3) / 1e12, 1),
             "per_gpu_TFLOPs": round(rank_flops / (ms * 1e-3) / 1e12, 1),
             "frac_per_gpu": round(rank_flops / (ms * 1e-3) / 1e12 / bf16_peak, 4),
             "ms_per_layer": {"deltanet": round(out["dn"], 3), "gqa": round(out["gqa"], 3)},
-            "sample": "one DeltaNet + one GQA layer timed (median of 3, max over ranks), x%d / x%d" % (n_dn, n_gqa),
-            "collectives": ("none" if world == 1 else
+            "sample": "one DeltaNet + one GQA layer timed (median of %d, max over ranks), x%d / x%d"
+                      % (reps, n_dn, n_gqa),
+            "device_status": "clean after warm-up and timed runs",
+            "collectives": ("none" if d.world == 1 else
                             "NCCL all-gather after column-parallel, all-reduce after row-parallel" if literal else
                             "NCCL all-reduce after row-parallel (Megatron pairing: no all-gather)")}
+
+
+def run_extra(args) -> int:
+    """Child-process mode: one extra measurement, printed as one JSON line."""
+    if args.extra == "cpu":
+        r = time_cpu_stream(args.cpu_steps, 1)
+        print(json.dumps(r), flush=True)
+        return 0
+    import q35cu
+
+    hbm_peak, bf16_peak, _, _ = peaks()
+    d = Dist(want_p2p=False)
+    torch = d.torch
+    r = None
+    try:
+        if args.extra == "c0":
+            r = time_gemv_rotating(q35cu, torch, 17408, 5120, 1)
+        elif args.extra == "c1":
+            r = []
+            for rows, cols in ((17408, 5120), (5120, 17408)):
+                for m in (1, 4, 16, 64):
+                    r.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10))
+                    if m >= 16:  # what q35_mm_fp8_batch runs at this size
+                        r.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10, path="tc"))
+        elif args.extra == "lm_head":
+            r = time_lm_head(q35cu, torch, hbm_peak)
+        elif args.extra == "c2":
+            r = time_prefill_c2(q35cu, torch, bf16_peak)
+        elif args.extra == "c4":
+            r = time_config4(d, bf16_peak)
+            if d.world > 1:
+                r["paired"] = time_config4(d, bf16_peak, scheme="paired")
+        torch.cuda.synchronize()
+        q35cu.check_device_status()
+    finally:
+        d.close()
+    if d.rank == 0:
+        print(json.dumps(r), flush=True)
+    return 0
+
+
+def run_child(name: str, args, timeout: float = 900.0):
+    """Run `bench.py --extra name` in a child process (under the same
+    rank/world environment; a child process group of its own on another
+    port when N > 1) and return its JSON, or {"error": ...} if it failed."""
+    env = dict(os.environ)
+    if "MASTER_PORT" in env:
+        env["MASTER_PORT"] = str(int(env["MASTER_PORT"]) + 1 + EXTRAS.index(name))
+        # the child group's rank 0 hosts its own store (torchrun's agent store
+        # serves the parent group only)
+        env.pop("TORCHELASTIC_USE_AGENT_STORE", None)
+    cmd = [sys.executable, os.path.abspath(__file__), "--extra", name, "--gpus", str(args.gpus),
+           "--cpu-steps", str(args.cpu_steps)]
+    t0 = time.time()
+    try:
+        p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=timeout)
+    except subprocess.TimeoutExpired:
+        return {"error": f"timed out after {timeout:.0f} s"}
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{") or ln.startswith("[")]
+    if p.returncode != 0 or (int(os.environ.get("RANK", "0")) == 0 and not lines):
+        tail = (p.stderr or p.stdout).strip().splitlines()[-6:]
+        return {"error": f"rc={p.returncode}: " + " | ".join(tail)}
+    if not lines:
+        return None
+    r = json.loads(lines[-1])
+    if isinstance(r, dict):
+        r["child_wall_s"] = round(time.time() - t0, 1)
+    return r
 
 
 def stack_max_cols(st):
@@ -587,50 +743,31 @@ def e2e_c_abi(q35cu, st, steps, warmup):
             "path": "q35_mm_fp8_multi4 / q35_mm_fp8 (host pointers, synchronous) per projection"}
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
+def traffic_ratio():
+    """DRAM bytes (read + write) per algorithmic byte of the decode GEMV, from
+    the committed ncu capture (profiles/gemv_fp8_c0.json; the command that
+    made it is in the file)."""
+    p = os.path.join(REPO, "profiles", "gemv_fp8_c0.json")
+    if not os.path.exists(p):
+        return None, None
+    with open(p) as f:
+        d = json.load(f)
+    return d.get("traffic_per_algorithmic_byte"), d.get("kernel")
 
+
+def run_ours(args):
     import q35cu
     import stack
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    d = Dist(want_p2p=True)
+    torch, world, rank = d.torch, d.world, d.rank
     if world != args.gpus:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}; using WORLD_SIZE", file=sys.stderr)
-    torch.cuda.set_device(local)
-    q35cu.load()
-    q35cu.check(q35cu.load().q35cu_set_device(local))
-    cpu_group = None
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-        cpu_group = dist.new_group(backend="gloo")
-        uid = [q35cu.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0, group=cpu_group)
-        q35cu.tp_init(rank, world, uid[0])
-        # the one-shot NVLink collectives: every rank's exchange-area handle
-        hs = [None] * world
-        dist.all_gather_object(hs, q35cu.p2p_handle(), group=cpu_group)
-        q35cu.p2p_open(rank, world, hs)
 
     hbm_peak, bf16_peak, bf16_sus, peak_src = peaks()
     st = stack.Stack(rank, world, n_layers=args.layers, scheme="literal")
-    torch.manual_seed(1234 + rank * 0)
     st.x.copy_(torch.randn(st.x.shape, generator=torch.Generator().manual_seed(1234)).cuda())
     torch.cuda.synchronize()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     results = {}
     graphs = []
@@ -648,7 +785,8 @@ def run_ours(args):
         for _ in range(2):
             run_step()
         torch.cuda.synchronize()
-        barrier()
+        q35cu.check_device_status()
+        d.barrier()
         n0 = q35cu.load().q35cu_launch_count()
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
@@ -662,8 +800,8 @@ def run_ours(args):
         for _ in range(args.warmup):
             g.replay()
         torch.cuda.synchronize()
-        barrier()
-        clk = Clocks(local)
+        d.barrier()
+        clk = Clocks(d.local)
         clk.start()
         time.sleep(0.3)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -673,8 +811,9 @@ def run_ours(args):
         e1.record()
         torch.cuda.synchronize()
         clocks = clk.stop()
-        barrier()
-        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        q35cu.check_device_status()
+        d.barrier()
+        ms = d.max_over_ranks(e0.elapsed_time(e1) / args.steps)
         results[(coll, scheme)] = {"ms": ms, "clocks": clocks, "kernels_per_step": kernels_per_step}
 
     # the headline is the fastest variant of the literal scheme (every variant is listed)
@@ -697,7 +836,7 @@ def run_ours(args):
             g.replay()
             hy.copy_(st.y, non_blocking=True)
         torch.cuda.synchronize()
-        barrier()
+        d.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
@@ -706,7 +845,7 @@ def run_ours(args):
             hy.copy_(st.y, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
-        ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        ms_e2e = d.max_over_ranks(e0.elapsed_time(e1) / args.steps)
         e2e = {"value": round(total_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 3),
                "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4,
                "path": "pinned H2D of the 64 layer inputs + graphed TP step + D2H of the 64 layer outputs"}
@@ -726,45 +865,34 @@ def run_ours(args):
     else:
         ach, bytes_per_launch, s_per_launch, nl = ach_p, bytes_per_launch_p, s_per_launch_p, nl_p
         kernel_name = "gemv_mma_kernel (decode GEMV), all launches of one step"
-    ach = max_over_ranks(-ach) * -1 if world > 1 else ach  # slowest rank
-    # DRAM bytes (read + write) per algorithmic byte of the decode GEMV from the
-    # committed ncu capture (profiles/gemv_fp8_c0.md), scaled to one launch
-    traffic = None
-    tp = os.path.join(REPO, "profiles", "gemv_fp8_c0.md")
-    if os.path.exists(tp):
-        with open(tp) as f:
-            for line in f:
-                if line.startswith("| traffic / algorithmic bytes |"):
-                    traffic = round(float(line.split("|")[2].split()[0]) * bytes_per_launch)
+    ach = d.max_over_ranks(-ach) * -1 if world > 1 else ach  # slowest rank
+    ratio, ratio_kernel = traffic_ratio()
+    traffic = round(ratio * bytes_per_launch) if ratio else None
+    st_free_bytes = st.local_weight_bytes
 
+    for g in graphs:
+        del g
+    graphs.clear()
+    st.free()
+    torch.cuda.synchronize()
+
+    # extras, each in a child process of its own (rank 0 at N=1; configuration
+    # 4 on every rank).  The decode configurations first: the tensor-core GEMMs
+    # of configurations 2 and 4 run at the power cap, and the clocks take a
+    # while to come back.
     extras = {}
-    # the HBM-bound decode configurations first: the tensor-core GEMMs of
-    # configurations 2 and 4 run at the power cap, and the clocks take a
-    # while to come back
-    if rank == 0 and world == 1 and not args.no_extras:
-        extras["config0_gemv"] = time_gemv_rotating(q35cu, torch, 17408, 5120, 1)
-        sweep = []
-        for rows, cols in ((17408, 5120), (5120, 17408)):
-            for m in (1, 4, 16, 64):
-                sweep.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10))
-                if m >= 16:  # what q35_mm_fp8_batch runs at this size
-                    sweep.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10, path="tc"))
-        extras["config1_sweep"] = sweep
-        extras["lm_head_bf16"] = time_lm_head(q35cu, torch, hbm_peak)
-        extras["config2_prefill"] = time_prefill_c2(q35cu, torch, bf16_peak)
-    if not args.no_extras:  # every rank takes part (collectives)
-        c4 = time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak)
-        if world > 1:
-            c4["paired"] = time_config4(q35cu, torch, st, world, barrier, max_over_ranks, bf16_peak, scheme="paired")
+    if not args.no_extras:
+        if world == 1:
+            extras["config0_gemv"] = run_child("c0", args)
+            extras["config1_sweep"] = run_child("c1", args)
+            extras["lm_head_bf16"] = run_child("lm_head", args)
+            extras["config2_prefill"] = run_child("c2", args)
+        c4 = run_child("c4", args)
         if rank == 0:
             extras["config4_prefill"] = c4
-
     cpu = None
     if rank == 0 and world == 1 and not args.no_extras:
-        try:
-            cpu = time_cpu_reference(steps=3, warmup=1)
-        except Exception as e:  # the CPU baseline must not sink the GPU line
-            cpu = {"value": None, "error": repr(e)}
+        cpu = run_child("cpu", args)
 
     kernels, colls = st.launches_per_step()
     if rank == 0:
@@ -775,7 +903,8 @@ def run_ours(args):
             "data": "synthetic (seeded N(0,0.02) weights, 128x128 block-quantised in HBM; N(0,1) activations)",
             "config": {"workload": f"configuration 3: {args.layers}-layer FP8 decode weight stream, M=1, "
                                    f"48 DeltaNet + 16 GQA layers",
-                       "weight_bytes_per_step": total_bytes, "parallelism": f"tp{world}",
+                       "weight_bytes_per_step": total_bytes, "weight_bytes_per_gpu": st_free_bytes,
+                       "parallelism": f"tp{world}",
                        "tp_scheme": "literal (all-gather after column-parallel, all-reduce after row-parallel)",
                        "launch": ("one cooperative launch per step (q35cu_chain_run)" if main_key[0] == "chain"
                                   else "one launch per projection, CUDA graph"),
@@ -786,6 +915,9 @@ def run_ours(args):
             "gpu_launches": main["kernels_per_step"] * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "traffic": traffic,
+                         "traffic_basis": (f"ncu dram read+write per algorithmic byte of {ratio_kernel} "
+                                           f"(profiles/gemv_fp8_c0.json) x this launch's algorithmic bytes"
+                                           if ratio else None),
                          "kernel": kernel_name,
                          "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
                          "launches_timed": nl, "algorithmic_bytes_per_launch": round(bytes_per_launch),
@@ -807,22 +939,16 @@ def run_ours(args):
                                      "(no all-gather, the row-parallel projection consumes the local shard)")
             line["collectives_per_step"] = colls
         if cpu is not None:
-            line["cpu_baseline"] = {k: cpu.get(k) for k in ("value", "unit", "cores", "kind", "sample")}
-            line["cpu_baseline"]["ms_per_step_extrapolated"] = cpu.get("ms_per_step_extrapolated")
+            if "error" in cpu:
+                line["cpu_baseline"] = cpu
+            else:
+                line["cpu_baseline"] = {k: cpu.get(k) for k in ("value", "unit", "cores", "kind", "sample")}
+                line["cpu_baseline"]["ms_per_step"] = cpu.get("ms_per_step")
+                line["cpu_baseline"]["cpu"] = cpu.get("cpu")
         line.update(extras)
         print(json.dumps(line), flush=True)
 
-    for g in graphs:
-        del g
-    graphs.clear()
-    st.free()
-    if world > 1:
-        torch.cuda.synchronize()
-        dist.barrier()
-        q35cu.p2p_close()
-        q35cu.tp_finalize()
-        dist.barrier()
-        dist.destroy_process_group()
+    d.close()
     return 0
 
 
@@ -907,6 +1033,8 @@ def run_profile_lm_head(args):
 
 def main():
     args = parse()
+    if args.extra:
+        return run_extra(args)
     if args.profile_c0:
         return run_profile_c0(args)
     if args.profile_c2:

@@ -257,6 +257,13 @@ uint64_t q35cu_launch_count(void);
  * last clear.  Asynchronous device-pointer callers check it after a
  * synchronisation; the q35_mm_* entry points check it on every call. */
 int q35cu_device_status(uint32_t *status, int clear);
+/* Where the tensor-core GEMM wait that last gave up was: out[0] = role
+ * (1 activation producer, 2 weight producer, 3 MMA issuer, 4 converter,
+ * 5 epilogue, 6 wind-down), out[1] = CTA, out[2] = 128-column block index
+ * within the CTA's walk, out[3] = thread.  Meaningful after
+ * q35cu_device_status reported Q35CU_ERR_TIMEOUT from a GEMM (the q35_mm_*
+ * entry points put it in their error message). */
+int q35cu_gemm_timeout_info(uint32_t out[4]);
 
 #ifdef __cplusplus
 }

@@ -26,7 +26,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_ORACLE = os.path.join(HERE, "liboracle.so")
 LIB_REF = os.path.join(HERE, "_ref", "libq35ref.so")
 LIB_REF_SCALAR = os.path.join(HERE, "_ref", "libq35ref_scalar.so")
-REFERENCE_TREE = "/root/reference/qwen35-c"
+# the reference engine's source tree (its qwen35-c directory), if given
+REFERENCE_TREE = os.environ.get("Q35_REF", "")
 
 _u8p = C.POINTER(C.c_uint8)
 _u16p = C.POINTER(C.c_uint16)
@@ -42,8 +43,8 @@ def _p(a: np.ndarray, t):
 def build(ref: bool | None = None) -> None:
     """Compile liboracle.so (and _ref/*.so when the reference tree exists)."""
     targets = ["oracle"]
-    if ref or (ref is None and os.path.isdir(REFERENCE_TREE)):
-        targets.append("ref")
+    if ref or (ref is None and REFERENCE_TREE and os.path.isdir(REFERENCE_TREE)):
+        targets += ["ref", f"REF={REFERENCE_TREE}"]
     subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
 
 

@@ -37,8 +37,10 @@
 //     N = 192 tokens (96 cycles per MMA) -- P0 | P1 | A0 | A1 then fill
 //     the 512 TMEM columns exactly;
 //   * barrier waits: a try_wait costs ~120 cycles even on a completed phase,
-//     so the MMA warp waits on one barrier per 128-column block (the TMA,
-//     the converters and the epilogue all arrive on it) and commits once.
+//     so the MMA warp waits on two barriers per 128-column block (the TMA's
+//     bytes on one, the converters and the epilogue on the other -- the
+//     TMA's barrier is kept apart so a producer that winds down can wait for
+//     its own copies alone) and commits once.
 //
 // Roles (640 threads; BN = tokens per tile, 192 unless the call is narrower):
 //   warp 0      TMA producer of the activation tile [BN tokens x 128 cols]
@@ -58,9 +60,18 @@
 //               128-column block (the block scale stays out of the MMA
 //               operands, which stay exact), and stores Y after the last block.
 //
-// Every mbarrier wait is bounded; a wait that gives up records
-// Q35CU_ERR_TIMEOUT in the GEMM's device status word and the CTA winds down
-// (the producers wait, bounded, for their copies in flight; TMEM is freed).
+// Every mbarrier wait is bounded (kWaitNs of wall time).  A wait that gives
+// up records Q35CU_ERR_TIMEOUT in the GEMM's device status word (and where:
+// role, CTA, block, thread) and raises the CTA's abort flag; every other
+// role's wait sees the flag and stops too.  The CTA then winds down so that
+// nothing it started can land after it frees its resources:
+//   * each producer waits for the copies it issued on barriers only the TMA
+//     completes (x_full[], w_full[]), so the wait needs no other role;
+//   * each MMA warp commits once more to its own one-shot barrier (fin[]),
+//     which fires when every MMA that warp issued has completed;
+//   * converters and epilogue warps have nothing in flight (their TMEM
+//     stores and loads are waited on where they are made);
+// and only then does the CTA pass its final barrier and free TMEM.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -70,6 +81,9 @@
 namespace q35cu {
 
 __device__ uint32_t g_gemm_status;
+// where the first wait that gave up was (role, CTA, block, thread), written
+// by the launch that set g_gemm_status
+__device__ uint32_t g_gemm_where[4];
 
 namespace {
 
@@ -83,7 +97,13 @@ template <int BN> constexpr int wstages() { return 4; }
 template <int BN> constexpr uint32_t x_tile() { return BN * kBK * 2; }  // f16 activation tile (48 KB at 192)
 constexpr uint32_t kWTile = kBM * kBK;      // 16 KB fp8
 template <int BN> constexpr uint32_t x_atom() { return BN * 128; }  // one 64-column swizzle atom of it
-constexpr uint32_t kSpin = 1u << 22;
+// A wait gives up after kWaitNs of wall time (globaltimer) or kWaitIters
+// polls, whichever comes first; no wait of a working launch lasts more than
+// a few microseconds.
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr uint32_t kWaitIters = 1u << 28;
+// roles recorded with a wait that gave up (g_gemm_where[0])
+enum : uint32_t { kRoleX = 1, kRoleW = 2, kRoleMma = 3, kRoleConv = 4, kRoleEpi = 5, kRoleDrain = 6 };
 constexpr int kWarpX = 0, kWarpMma = 1, kWarpW = 2, kWarpConv = 3;
 constexpr int kConvWarps = 4;                       // one thread per weight row
 constexpr int kWarpEpi = kWarpConv + kConvWarps;    // 7
@@ -104,10 +124,11 @@ template <int BN> constexpr uint32_t tmem_a() { return depth<BN>() * BN; }
 static_assert(depth<kBN>() * (kBN + kACols) <= kTmemCols && depth<64>() * (64 + kACols) <= kTmemCols &&
                   depth<128>() * (128 + kACols) <= kTmemCols && depth<32>() * (32 + kACols) <= kTmemCols,
               "TMEM budget");
-// arrivals that complete stage g: the activation producer (with the copy's
-// bytes), the converter warps (A[g % D] written) and the epilogue warps
-// (P[g % D] drained of block g - D)
-constexpr uint32_t kStageArrivals = 1 + kConvWarps + kEpiWarps;
+// arrivals that complete ready[] for block g: the converter warps (A[g % D]
+// written) and the epilogue warps (P[g % D] drained of block g - D).  The
+// activation tile has its own barrier, x_full[], which only the producer's
+// arrive.expect_tx and the TMA's bytes complete.
+constexpr uint32_t kStageArrivals = kConvWarps + kEpiWarps;
 
 struct GemmArgs {
     const float *S;       // weight scales [ceil(N/128), kblocks]
@@ -122,7 +143,8 @@ struct Smem {  // offsets from the 1024-aligned base (every tile size is a multi
     static constexpr uint32_t x(int s) { return s * x_tile<BN>(); }
     static constexpr uint32_t w(int s) { return stages<BN>() * x_tile<BN>() + s * kWTile; }
     static constexpr uint32_t bars = stages<BN>() * x_tile<BN>() + wstages<BN>() * kWTile;
-    static_assert(2 * stages<BN>() * 8 + 2 * wstages<BN>() * 8 + 4 <= 256, "barriers fit their 256 bytes");
+    // x_full, ready, done [S]; w_full, w_empty [WS]; fin [2]; abort flag; TMEM address
+    static_assert((3 * stages<BN>() + 2 * wstages<BN>() + 2) * 8 + 8 <= 256, "barriers fit their 256 bytes");
     static constexpr uint32_t total = bars + 256;
     static_assert(x_tile<BN>() % 1024 == 0 && x_atom<BN>() % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 };
@@ -149,19 +171,52 @@ __device__ __forceinline__ void bar_arrive(uint64_t *b)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(b)) : "memory");
 }
-__device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity)
+__device__ __forceinline__ bool try_wait(uint64_t *b, uint32_t parity)
 {
-    for (uint32_t i = 0; i < kSpin; ++i) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(sa(b)), "r"(parity)
-            : "memory");
-        if (ok) return true;
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(sa(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t now_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// The slow path of a wait (the phase was not complete at the first poll).
+// abort == nullptr: a wind-down wait, which ignores the CTA's abort flag.
+__device__ __noinline__ bool bar_wait_slow(uint64_t *b, uint32_t parity, volatile uint32_t *abort, uint32_t role,
+                                           uint32_t g)
+{
+    const uint64_t t0 = now_ns();
+    for (uint32_t i = 1; i < kWaitIters; ++i) {
+        if (try_wait(b, parity)) return true;
+        if ((i & 31) == 0) {
+            if (abort && *abort) return false;  // another role gave up: stop without a record of our own
+            if (now_ns() - t0 > kWaitNs) break;
+        }
     }
-    atomicExch(&g_gemm_status, (uint32_t)Q35CU_ERR_TIMEOUT);
+    if (abort) *abort = 1;
+    if (atomicCAS(&g_gemm_status, 0u, (uint32_t)Q35CU_ERR_TIMEOUT) == 0u) {
+        g_gemm_where[0] = role;
+        g_gemm_where[1] = blockIdx.x;
+        g_gemm_where[2] = g;
+        g_gemm_where[3] = threadIdx.x;
+    }
     return false;
+}
+
+// Bounded wait for phase `parity` of b; false = gave up (or the CTA aborts).
+__device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity, volatile uint32_t *abort, uint32_t role,
+                                         uint32_t g)
+{
+    return try_wait(b, parity) || bar_wait_slow(b, parity, abort, role, g);
 }
 
 __device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar,
@@ -175,11 +230,14 @@ __device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int c0
         : "memory");
 }
 
-// wait (bounded) until the last min(issued, stages) copies of a ring have landed
+// Wait (bounded, ignoring the abort flag) until the last min(issued, stages)
+// copies of a ring have landed.  `full` is completed by the TMA's bytes and
+// the producer's own arrive alone, and copy i was issued only after phase
+// i - stages of its slot had completed, so phase i is the one pending.
 __device__ __forceinline__ void drain(uint64_t *full, int stages, uint32_t issued)
 {
     for (uint32_t i = issued > (uint32_t)stages ? issued - stages : 0; i < issued; ++i)
-        bar_wait(&full[i % stages], (i / stages) & 1);
+        bar_wait(&full[i % stages], (i / stages) & 1, nullptr, kRoleDrain, i);
 }
 
 // UMMA shared-memory descriptor: K-major, 128B swizzle, 8-row core groups 1024 B apart
@@ -275,16 +333,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 {
     using Sm = Smem<BN>;
     constexpr int S = stages<BN>(), D = depth<BN>(), WS = wstages<BN>();
+    constexpr uint32_t kFull = 0xffffffffu;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    // stage g uses slot g % S of both arrays:
-    //   ready[s]: activation tile landed + A[g % 2] converted + P[g % 2] free -> MMA
-    //   done[s]:  the MMA of block g completed (tcgen05.commit)          -> all
-    uint64_t *ready = reinterpret_cast<uint64_t *>(sm + Sm::bars);
+    // block g uses slot g % S of the activation rings:
+    //   x_full[s]: the activation tile of block g landed (TMA bytes)        -> MMA
+    //   ready[s]:  A[g % D] converted + P[g % D] free (converters, epilogue) -> MMA
+    //   done[s]:   the MMA of block g completed (tcgen05.commit)           -> all
+    // and slot g % WS of the weight ring (w_full: TMA -> converters,
+    // w_empty: converters -> TMA).  fin[i]: MMA warp i's last commit.
+    uint64_t *x_full = reinterpret_cast<uint64_t *>(sm + Sm::bars);
+    uint64_t *ready = x_full + S;
     uint64_t *done = ready + S;
-    uint64_t *w_full = done + S;            // [4] TMA -> converters
-    uint64_t *w_empty = w_full + WS;        // [WS] converters -> TMA
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_empty + WS);
+    uint64_t *w_full = done + S;
+    uint64_t *w_empty = w_full + WS;
+    uint64_t *fin = w_empty + WS;
+    volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(fin + 2);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 2) + 1;
 
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const uint32_t nkb = a.kblocks;
@@ -297,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (t == 32) {
         for (int i = 0; i < S; ++i) {
+            bar_init(&x_full[i], 1);
             bar_init(&ready[i], kStageArrivals);
             bar_init(&done[i], 1);
         }
@@ -304,6 +370,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             bar_init(&w_full[i], 1);
             bar_init(&w_empty[i], kConvWarps);
         }
+        bar_init(&fin[0], 1);
+        bar_init(&fin[1], 1);
+        *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -311,13 +380,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    // Ordering argument for the shared slot rings (S = D + 1 slots): every
-    // arrival for block g on ready[g % S] comes, in its party's program
-    // order, after that party waited on done(g - S) (the producer directly;
-    // a converter or epilogue thread while handling an earlier block), so the
-    // slot has finished its phase for block g - S; and no waiter on done(h)
-    // can be overtaken by done(h + S), which needs that waiter's own later
-    // arrival first.
+    // Ordering argument for the slot rings (S = D + 1 slots).  Every arrival
+    // for block g on a slot of ready[] / x_full[] comes, in its party's
+    // program order, after that party waited on done(g - S) (the producer
+    // directly, a converter or epilogue thread while handling an earlier
+    // block), so the slot has finished its phase for block g - S.  No waiter
+    // on done(h) can be overtaken by done(h + S), and no waiter on x_full(h)
+    // or ready(h) by phase h + S: each needs that waiter's own later step
+    // first.  Every decision to go on or stop is taken warp-wide (__all_sync),
+    // so the .sync.aligned TMEM instructions always see a converged warp.
     if (warp == kWarpX) {
         // ---------------- activation producer (whole warp) -----------------
         uint32_t g = 0;
@@ -326,16 +397,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m0 = (int)((tile % a.mtiles) * BN);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int s = g % S;
-                if (g >= (uint32_t)S) ok = __all_sync(0xffffffffu, bar_wait(&done[s], ((g / S) - 1) & 1));
+                if (g >= (uint32_t)S)
+                    ok = __all_sync(kFull, bar_wait(&done[s], ((g / S) - 1) & 1, abort, kRoleX, g));
                 if (!ok) break;
-                bar_expect(&ready[s], x_tile<BN>(), leader);
-                tma_2d(sm + Sm::x(s), &map_x, (int)(kb * kBK), m0, &ready[s], leader);
-                tma_2d(sm + Sm::x(s) + x_atom<BN>(), &map_x, (int)(kb * kBK + 64), m0, &ready[s], leader);
+                bar_expect(&x_full[s], x_tile<BN>(), leader);
+                tma_2d(sm + Sm::x(s), &map_x, (int)(kb * kBK), m0, &x_full[s], leader);
+                tma_2d(sm + Sm::x(s) + x_atom<BN>(), &map_x, (int)(kb * kBK + 64), m0, &x_full[s], leader);
             }
         }
-        // wait (bounded) for the copies still in flight
-        for (uint32_t i = g > (uint32_t)S ? g - S : 0; i < g; ++i)
-            bar_wait(&ready[i % S], (i / S) & 1);
+        drain(x_full, S, g);  // g = copies issued
     } else if (warp == kWarpW) {
         // ---------------- weight producer (whole warp) ---------------------
         uint32_t g = 0;
@@ -344,7 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n0 = (int)((tile / a.mtiles) * kBM);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int s = g % WS;
-                if (g >= (uint32_t)WS) ok = __all_sync(0xffffffffu, bar_wait(&w_empty[s], ((g / WS) - 1) & 1));
+                if (g >= (uint32_t)WS)
+                    ok = __all_sync(kFull, bar_wait(&w_empty[s], ((g / WS) - 1) & 1, abort, kRoleW, g));
                 if (!ok) break;
                 bar_expect(&w_full[s], kWTile, leader);
                 tma_2d(sm + Sm::w(s), &map_w, (int)(kb * kBK), n0, &w_full[s], leader);
@@ -358,13 +429,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // idle; two warps take alternate blocks (each block has its own P, A
         // and activation stage) and one warp's wait overlaps the other's MMAs.
         const uint32_t parity = warp == kWarpMma ? 0u : 1u;
-        uint32_t g = 0, last = 0xFFFFFFFFu;
+        uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 if ((g & 1) != parity) continue;
                 const int s = g % S, j = g % D;
-                ok = __all_sync(0xffffffffu, bar_wait(&ready[s], (g / S) & 1));
+                const uint32_t ph = (g / S) & 1;
+                ok = __all_sync(kFull, bar_wait(&x_full[s], ph, abort, kRoleMma, g));
+                if (ok) ok = __all_sync(kFull, bar_wait(&ready[s], ph, abort, kRoleMma, g));
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t xbase = sa(sm + Sm::x(s));
@@ -375,11 +448,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_f16_ts(d, acol + ks * 8, sw128_desc(xbase + off), idesc<BN>(), ks > 0, leader);
                 }
                 mma_commit(&done[s], leader);
-                last = g;
             }
         }
-        // this warp's last block must have completed before the CTA can free TMEM
-        if (ok && last != 0xFFFFFFFFu) bar_wait(&done[last % S], (last / S) & 1);
+        // one more commit, to this warp's own barrier: it arrives once every
+        // MMA the warp issued has completed (TMEM is freed only after that)
+        mma_commit(&fin[parity], leader);
+        __syncwarp();
+        bar_wait(&fin[parity], 0, nullptr, kRoleDrain, g);
     } else if (warp < kWarpEpi) {
         // ---------------- converters: fp8 -> f16 into TMEM -------------------
         // Thread = weight row = TMEM lane (warp w may access lanes 32*(w%4)..).
@@ -395,9 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int s = g % WS, j = g % D;
-                ok = bar_wait(&w_full[s], (g / WS) & 1);
+                bool w = bar_wait(&w_full[s], (g / WS) & 1, abort, kRoleConv, g);
                 // A[g % D] was last read by block g - D
-                if (ok && g >= (uint32_t)D) ok = bar_wait(&done[(g - D) % S], ((g - D) / S) & 1);
+                if (w && g >= (uint32_t)D) w = bar_wait(&done[(g - D) % S], ((g - D) / S) & 1, abort, kRoleConv, g);
+                ok = __all_sync(kFull, w);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint8_t *wrow = sm + Sm::w(s) + r * 128;
@@ -447,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int j = g % D;
                 const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
-                ok = bar_wait(&done[g % S], (g / S) & 1);
+                ok = __all_sync(kFull, bar_wait(&done[g % S], (g / S) & 1, abort, kRoleEpi, g));
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
@@ -483,6 +559,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    // Nothing this CTA started is in flight any more: the producers waited
+    // for their copies, the MMA warps for their MMAs.
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -821,6 +899,13 @@ int gemm_status(uint32_t *status, bool clear)
         const uint32_t z = 0;
         Q35CU_CUDA(cudaMemcpyToSymbol(g_gemm_status, &z, 4));
     }
+    return Q35CU_OK;
+}
+
+// where the wait that set the status gave up (kept until the next one does)
+int gemm_timeout_info(uint32_t out[4])
+{
+    Q35CU_CUDA(cudaMemcpyFromSymbol(out, g_gemm_where, 4 * sizeof(uint32_t)));
     return Q35CU_OK;
 }
 

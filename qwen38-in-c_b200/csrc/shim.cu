@@ -1060,6 +1060,14 @@ Q35_API int q35cu_device_status(uint32_t *status, int clear)
     return device_status(status, clear != 0);
 }
 
+Q35_API int q35cu_gemm_timeout_info(uint32_t out[4])
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!out) return set_error(Q35CU_ERR_ARG, "out is NULL");
+    if (!dev_state()) return t_err;
+    return gemm_timeout_info(out);
+}
+
 // ------------------------------------------------------------------------
 // q35_mm.h: the reference-facing entry points
 // ------------------------------------------------------------------------
@@ -1138,9 +1146,16 @@ __global__ void gather_status_kernel(const uint32_t *a, const uint32_t *b, const
 // a bounded device-side wait that gave up leaves a code in the status word
 int check_device_status()
 {
-    uint32_t st = 0;
-    int rc = device_status(&st, true);
+    uint32_t g = 0, where[4] = {0, 0, 0, 0};
+    int rc = gemm_status(&g, false);
+    if (!rc && g) rc = gemm_timeout_info(where);
     if (rc) return rc;
+    uint32_t st = 0;
+    rc = device_status(&st, true);
+    if (rc) return rc;
+    if (g)
+        return set_error((int)g, "a tensor-core GEMM wait gave up (status %u; role %u, CTA %u, block %u, thread %u)",
+                         g, where[0], where[1], where[2], where[3]);
     if (st) return set_error((int)st, "a device-side wait gave up (status %u)", st);
     return Q35CU_OK;
 }

@@ -106,6 +106,7 @@ _SIGS = [
     ("q35cu_build_info", C.c_char_p, []),
     ("q35cu_launch_count", C.c_uint64, []),
     ("q35cu_device_status", C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
+    ("q35cu_gemm_timeout_info", C.c_int, [C.POINTER(C.c_uint32)]),
 ]
 
 _lib = None
@@ -142,6 +143,28 @@ def check(rc: int) -> None:
     if rc != OK:
         L = load()
         raise Q35Error(rc, L.q35cu_last_error_message().decode(errors="replace"))
+
+
+def device_status(clear: bool = True) -> int:
+    """The device status words (decode GEMV, tensor-core GEMM, peer-memory
+    collectives) of the current device: 0, or the status of a bounded wait
+    that gave up since the last clear.  Read it after a synchronisation."""
+    st = C.c_uint32(0)
+    check(load().q35cu_device_status(C.byref(st), 1 if clear else 0))
+    return int(st.value)
+
+
+def check_device_status() -> None:
+    """Raise Q35Error if a device-side wait gave up since the last check
+    (the GEMM's record of where it gave up goes into the message)."""
+    L = load()
+    where = (C.c_uint32 * 4)()
+    st = device_status(clear=False)
+    if st:
+        check(L.q35cu_gemm_timeout_info(where))
+        device_status(clear=True)
+        raise Q35Error(st, "a device-side wait gave up (GEMM record: role %d, CTA %d, block %d, thread %d)"
+                       % tuple(where))
 
 
 def last_error() -> tuple[int, str]:

@@ -71,6 +71,7 @@ def test_config2_prefill_shapes(gpu, orc, name, rows, cols):
         Y = torch.empty((m, rows), device="cuda")
         q35cu.gemm(w, Xb.view(torch.int16), Y)
         torch.cuda.synchronize()
+        q35cu.check_device_status()
         Yh = Y.cpu().numpy()
         pick = np.random.default_rng(rows).choice(m, 48, replace=False)
         Y64, _ = orc.mm_fp8_f64(Wh, sch, np.ascontiguousarray(X[pick]))
@@ -93,6 +94,7 @@ def test_gemm_deterministic(gpu, orc):
         q35cu.gemm(w, X.view(torch.int16), Y1)
         q35cu.gemm(w, X.view(torch.int16), Y2)
         torch.cuda.synchronize()
+        q35cu.check_device_status()
         assert torch.equal(Y1, Y2)
     finally:
         w.free()

@@ -40,9 +40,12 @@ def test_noalloc_matches_gemm_twice(gpu, orc):
             X = torch.from_numpy(orc.synth_act(seed, (m, 5120))).cuda()
             Y = torch.full((m, 2048), float("nan"), device="cuda")
             q35cu.check(_call_noalloc(w, X, Y))
+            torch.cuda.synchronize()
+            assert q35cu.device_status(clear=True) == 0  # no bounded wait gave up
             Yref = torch.empty((m, 2048), device="cuda")
             q35cu.gemm(w, X.to(torch.bfloat16).view(torch.int16), Yref)
             torch.cuda.synchronize()
+            assert q35cu.device_status(clear=True) == 0
             a, b = Y.cpu().numpy(), Yref.cpu().numpy()
             assert np.isfinite(a).all()
             err = rel_l2(a, b)

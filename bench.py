@@ -85,8 +85,12 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampler running during the timed region."""
+    """SM clock, power and clock-event reasons of one GPU, sampled every 10 ms
+    by NVML in a thread while the timed region runs (nvidia-smi -lms 200 as a
+    fallback when NVML is unavailable).  Only reads the settings."""
 
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -94,9 +98,46 @@ class Clocks:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.out = ""
+        self.thread = None
+        self.samples = []
+        self.stop_ev = threading.Event()
+        self.nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = None
+            try:
+                import torch
+
+                bus = torch.cuda.get_device_properties(index).pci_bus_id
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(("%08x:%02x:%02x.0" % (
+                    torch.cuda.get_device_properties(index).pci_domain_id, bus,
+                    torch.cuda.get_device_properties(index).pci_device_id)).encode())
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.nvml = (pynvml, h)
+        except Exception:
+            self.nvml = None
+
+    def _poll(self):
+        nv, h = self.nvml
+        while not self.stop_ev.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((sm, mx, pw, rs))
+            except Exception:
+                pass
+            self.stop_ev.wait(0.01)
 
     def start(self):
+        if self.nvml:
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -105,17 +146,27 @@ class Clocks:
             self.proc = None
 
     def stop(self) -> dict:
+        if self.thread:
+            self.stop_ev.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "source": "nvml"}
+            reasons = sorted({n for _, _, _, r in self.samples for n, bit in self.REASONS if r & bit})
+            return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                    "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons,
+                    "samples": len(self.samples), "power_w_max": round(max(s[2] for s in self.samples), 1),
+                    "source": "nvml, every 10 ms during the timed region"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         try:
-            self.out, _ = self.proc.communicate(timeout=5)
+            out, _ = self.proc.communicate(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            self.out, _ = self.proc.communicate()
+            out, _ = self.proc.communicate()
         sm, mx, reasons, pw = [], [], set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.out.strip().splitlines():
+        for line in out.strip().splitlines():
             f = [t.strip() for t in line.split(",")]
             if len(f) < 9:
                 continue
@@ -131,7 +182,7 @@ class Clocks:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm), "power_w_max": max(pw) if pw else None}
+                "samples": len(sm), "power_w_max": max(pw) if pw else None, "source": "nvidia-smi -lms 200"}
 
 
 # ---------------------------------------------------------------------------
@@ -850,21 +901,24 @@ def run_ours(args):
                "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4,
                "path": "pinned H2D of the 64 layer inputs + graphed TP step + D2H of the 64 layer outputs"}
 
-    # live roofline of the dominant kernel, this rank.  With the chain the step
-    # is one launch of gemv_chain_kernel: its algorithmic bytes (this rank's
-    # weights + scales + activations) over the launch's event time, i.e. the
-    # timed step itself.  The per-projection standalone launches are timed
-    # one by one as a breakdown.
+    # live roofline of the dominant kernel, this rank.  Every kernel of the
+    # timed step is the decode GEMV (256 PDL-chained launches of
+    # gemv_mma_kernel in the graph, or the one gemv_chain_kernel launch), so
+    # its achieved bandwidth is the step's algorithmic bytes (this rank's
+    # weights + scales + activations) over the step's event time, i.e. the
+    # average launch duration inside the timed region.  The per-projection
+    # standalone launches, each timed alone with events (no PDL overlap), are
+    # listed as a breakdown.
     ach_p, bytes_per_launch_p, s_per_launch_p, nl_p, breakdown = kernel_roofline(q35cu, torch, st, hbm_peak)
+    bytes_step = bytes_per_launch_p * nl_p
+    s_step = main["ms"] * 1e-3
+    ach = bytes_step / s_step / 1e9
     if main_key[0] == "chain":
-        bytes_per_launch = bytes_per_launch_p * nl_p  # every GEMV of one step
-        s_per_launch = main["ms"] * 1e-3
-        ach = bytes_per_launch / s_per_launch / 1e9
-        nl = args.steps
+        bytes_per_launch, s_per_launch, nl = bytes_step, s_step, args.steps
         kernel_name = "gemv_chain_kernel (the whole step: one cooperative launch)"
     else:
-        ach, bytes_per_launch, s_per_launch, nl = ach_p, bytes_per_launch_p, s_per_launch_p, nl_p
-        kernel_name = "gemv_mma_kernel (decode GEMV), all launches of one step"
+        bytes_per_launch, s_per_launch, nl = bytes_step / nl_p, s_step / nl_p, nl_p * args.steps
+        kernel_name = "gemv_mma_kernel (decode GEMV): the step's %d launches, PDL-chained in one CUDA graph" % nl_p
     ach = d.max_over_ranks(-ach) * -1 if world > 1 else ach  # slowest rank
     ratio, ratio_kernel = traffic_ratio()
     traffic = round(ratio * bytes_per_launch) if ratio else None

@@ -1161,12 +1161,14 @@ int check_device_status()
 }
 
 // stage X in, run `fn` (which launches on d->stream into the device output
-// region), stage Y out.  in_bytes / out_bytes are exact byte counts.  The
-// three device status words travel back behind the output in the same copy
-// (one tiny kernel gathers them), so a call costs one H2D, one D2H and one
-// synchronisation; they are cleared only when one is set.
-template <class F>
-int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
+// region), stage the output back and hand the host copy to `deliver` (which
+// copies it into the caller's buffers).  in_bytes / out_bytes are exact byte
+// counts.  The three device status words travel back behind the output in
+// the same copy (one tiny kernel gathers them), so a call costs one H2D, one
+// D2H and one synchronisation; they are read again (and cleared) only when
+// one is set.
+template <class F, class G>
+int host_call_ex(const void *X, size_t in_bytes, size_t out_bytes, F &&fn, G &&deliver)
 {
     DevState *d = dev_state();
     if (!d) return t_err;
@@ -1198,8 +1200,14 @@ int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
         rc = check_device_status();  // reads and clears all three
         if (rc) return rc;
     }
-    memcpy(Y, h + in_al, out_bytes);
+    deliver(static_cast<const char *>(h + in_al));
     return Q35CU_OK;
+}
+
+template <class F>
+int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
+{
+    return host_call_ex(X, in_bytes, out_bytes, fn, [&](const char *out) { memcpy(Y, out, out_bytes); });
 }
 
 }  // namespace
@@ -1305,43 +1313,27 @@ Q35_API void q35_mm_fp8_multi4(const uint8_t *W[4], const uint16_t *sc[4], uint3
     }
     if (!rc) {
         // outputs of the segments packed back to back in the staging area
-        const size_t out_bytes = (size_t)total * 4;
-        DevState *d = dev_state();
-        rc = d ? Q35CU_OK : t_err;
-        if (!rc) {
-            const size_t in_al = ((size_t)cols * 4 + 255) & ~(size_t)255;
-            rc = ensure_stage(d, in_al + out_bytes);
-            if (!rc) {
-                char *h = static_cast<char *>(d->h_stage);
-                char *dv = static_cast<char *>(d->d_stage);
-                memcpy(h, x, (size_t)cols * 4);
+        rc = host_call_ex(
+            x, (size_t)cols * 4, (size_t)total * 4,
+            [&](const float *dx, float *dy, cudaStream_t st) {
                 GemvSeg segs[4];
                 int n = 0;
                 size_t off = 0;
                 for (int s = 0; s < 4; ++s) {
                     if (!ws[s]) continue;
-                    segs[n++] = seg_of(ws[s], reinterpret_cast<float *>(dv + in_al) + off, rows[s]);
+                    segs[n++] = seg_of(ws[s], dy + off, rows[s]);
                     off += rows[s];
                 }
-                cudaError_t e = cudaMemcpyAsync(dv, h, (size_t)cols * 4, cudaMemcpyHostToDevice, d->stream);
-                if (e != cudaSuccess) rc = cuda_error(e, "cudaMemcpyAsync");
-                if (!rc) rc = launch_gemv(0, segs, n, reinterpret_cast<const float *>(dv), cols, cols, 1, d->stream);
-                if (!rc) {
-                    e = cudaMemcpyAsync(h + in_al, dv + in_al, out_bytes, cudaMemcpyDeviceToHost, d->stream);
-                    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
-                    if (e != cudaSuccess) rc = cuda_error(e, "copy-out");
+                return launch_gemv(0, segs, n, dx, cols, cols, 1, st);
+            },
+            [&](const char *out) {
+                size_t off = 0;
+                for (int s = 0; s < 4; ++s) {
+                    if (!ws[s]) continue;
+                    memcpy(y[s], reinterpret_cast<const float *>(out) + off, (size_t)rows[s] * 4);
+                    off += rows[s];
                 }
-                if (!rc) rc = check_device_status();
-                if (!rc) {
-                    off = 0;
-                    for (int s = 0; s < 4; ++s) {
-                        if (!ws[s]) continue;
-                        memcpy(y[s], reinterpret_cast<float *>(h + in_al) + off, (size_t)rows[s] * 4);
-                        off += rows[s];
-                    }
-                }
-            }
-        }
+            });
     }
     if (rc) fail_host(outs, counts, 4);
 }

@@ -48,7 +48,7 @@ sys.path.insert(0, os.path.join(REPO, "qwen38-in-c_b200"))
 METRIC = "FP8 decode GEMV HBM GB/s (% peak); prefill GEMM TFLOP/s; 64-layer ms/token"
 HBM_FALLBACK_GBS = 6650.0
 BF16_FALLBACK_TFLOPS = 1590.0
-EXTRAS = ("c0", "c1", "lm_head", "c2", "c4", "cpu")
+EXTRAS = ("c0", "c1", "lm_head", "c2", "c4", "cpu", "out_batch")
 
 
 def parse(argv=None):
@@ -637,6 +637,50 @@ def time_config4(d: Dist, bf16_peak, m=8192, reps=3, scheme="literal"):
                             "NCCL all-reduce after row-parallel (Megatron pairing: no all-gather)")}
 
 
+def time_out_batching(q35cu, torch, lengths=(512, 2048)):
+    """The prefill caller change (oracle/prefill_batch.py) measured through
+    the reference-facing C-ABI with host buffers: the DeltaNet out_proj
+    (5120 x 6144) of an L-token prefill as L q35_mm_fp8 calls -- the engine's
+    loop, qwen35-c/src/q35_deltanet.c:491-499 -- against one
+    q35_mm_fp8_batch call (the patched engine; the tensor-core GEMM on
+    bf16-rounded activations).  Wall clock of the calls themselves (their
+    arguments prepared beforehand, as a C caller holds them)."""
+    import ctypes as C
+
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    from parity import rel_l2
+
+    w = q35cu.Weight.synth_fp8(4711, 5120, 6144)
+    W, sc = w.download_fp8()
+    w.free()
+    L_ = q35cu.load()
+    wp, sp = W.ctypes.data_as(q35cu._u8p), sc.ctypes.data_as(q35cu._u16p)
+    out = {}
+    for L in lengths:
+        g = torch.Generator().manual_seed(L)
+        X = torch.randn((L, 6144), generator=g).to(torch.bfloat16).float().numpy()
+        Y1 = np.empty((L, 5120), np.float32)
+        xs = [X[t].ctypes.data_as(q35cu._f32p) for t in range(L)]
+        ys = [Y1[t].ctypes.data_as(q35cu._f32p) for t in range(L)]
+        L_.q35_mm_fp8(wp, sp, 5120, 6144, xs[0], ys[0])  # uploads the weight (first touch)
+        t0 = time.perf_counter()
+        for t in range(L):
+            L_.q35_mm_fp8(wp, sp, 5120, 6144, xs[t], ys[t])
+        t_tok = time.perf_counter() - t0
+        Y2 = np.empty((L, 5120), np.float32)
+        L_.q35_mm_fp8_batch(wp, sp, 5120, 6144, L, X.ctypes.data_as(q35cu._f32p), Y2.ctypes.data_as(q35cu._f32p))
+        t0 = time.perf_counter()
+        L_.q35_mm_fp8_batch(wp, sp, 5120, 6144, L, X.ctypes.data_as(q35cu._f32p), Y2.ctypes.data_as(q35cu._f32p))
+        t_b = time.perf_counter() - t0
+        out[str(L)] = {"per_token_ms": round(t_tok * 1e3, 2), "batched_ms": round(t_b * 1e3, 2),
+                       "speedup": round(t_tok / t_b, 1), "rel_l2_batched_vs_per_token": rel_l2(Y2, Y1)}
+    L_.q35cu_release_all()
+    return {"projection": "DeltaNet out_proj 5120x6144", "by_tokens": out,
+            "path": "q35_mm_fp8 x L (host buffers) vs one q35_mm_fp8_batch (host buffers)"}
+
+
 def run_extra(args) -> int:
     """Child-process mode: one extra measurement, printed as one JSON line."""
     if args.extra == "cpu":
@@ -663,6 +707,8 @@ def run_extra(args) -> int:
             r = time_lm_head(q35cu, torch, hbm_peak)
         elif args.extra == "c2":
             r = time_prefill_c2(q35cu, torch, bf16_peak)
+        elif args.extra == "out_batch":
+            r = time_out_batching(q35cu, torch)
         elif args.extra == "c4":
             r = time_config4(d, bf16_peak)
             if d.world > 1:
@@ -941,6 +987,7 @@ def run_ours(args):
             extras["config1_sweep"] = run_child("c1", args)
             extras["lm_head_bf16"] = run_child("lm_head", args)
             extras["config2_prefill"] = run_child("c2", args)
+            extras["prefill_out_batching"] = run_child("out_batch", args)
         c4 = run_child("c4", args)
         if rank == 0:
             extras["config4_prefill"] = c4

@@ -421,6 +421,9 @@ struct alignas(16) MArgs {
     int tp_mode;          // GemvTp::mode (m == 1 only)
     float *gathered;      // all-gather destination [world][total_rows]
     P2PView p2p;          // the ranks' exchange areas
+    uint32_t *sig_count;  // HostSignal (standalone launches; null = none)
+    uint32_t *sig_flag;
+    uint32_t sig_seq;
 };
 
 // one 16-row block of the CTA, resolved once: weight row pointer, the
@@ -805,7 +808,25 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     for (uint32_t i = threadIdx.x; i < kMaxChunks; i += kM2Threads) xflag[i] = 0;  // ordered by the body's first barrier
     const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * a.ipr);
     gemv_body<MT, false>(a, smem, L, xflag, 1, nullptr, 0);
+    if (a.sig_flag) {
+        // host-pointer call: the last CTA out tells the waiting host thread,
+        // through host-mapped memory, that every output is visible
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();  // this CTA's outputs (host-mapped) before its count
+            const uint32_t ctas = gridDim.x * gridDim.y;
+            if (atomicAdd(a.sig_count, 1u) == ctas - 1) {
+                __threadfence_system();
+                *a.sig_count = 0;
+                volatile uint32_t *f = a.sig_flag;
+                f[1] = *reinterpret_cast<volatile uint32_t *>(&g_device_status);
+                __threadfence_system();
+                f[0] = a.sig_seq;
+            }
+        }
+    }
 }
+
 
 // A chain of one-token decode GEMVs in one cooperative launch: every CTA
 // walks the ops in order with a grid barrier before each op after the first,
@@ -977,9 +998,14 @@ int launch_mma(const MArgs &a, dim3 grid, size_t smem, cudaStream_t st)
 }
 
 // FP8 weights with cols % 128 == 0: the tensor-core decode GEMV
-int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp)
+int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp, const HostSignal *sig)
 {
     MArgs a{};
+    if (sig) {
+        a.sig_count = sig->count;
+        a.sig_flag = sig->flag;
+        a.sig_seq = sig->seq;
+    }
     for (int s = 0; s < 4; ++s) a.seg[s] = a0.seg[s];
     a.X = a0.X;
     a.K = a0.K;
@@ -1172,7 +1198,7 @@ int launch_chain(const void *d_ops, uint32_t nops, uint32_t *d_bar, const uint32
 }
 
 int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint32_t K, uint32_t ldx, uint32_t m,
-                cudaStream_t st, const GemvTp &tp)
+                cudaStream_t st, const GemvTp &tp, const HostSignal *sig)
 {
     if (nseg < 1 || nseg > 4 || m == 0 || K == 0) return set_error(Q35CU_ERR_ARG, "gemv: bad launch shape");
     Args a{};
@@ -1194,8 +1220,9 @@ int launch_gemv(int kind, const GemvSeg *segs_in, int nseg, const float *X, uint
     }
     a.total_rows = vb;
     if (vb == 0) return Q35CU_OK;
-    if (vec_ok && kind == 0 && K % 128 == 0 && getenv("Q35CU_GEMV_SIMT") == nullptr) return launch_gemv_mma(a, st, tp);
+    if (vec_ok && kind == 0 && K % 128 == 0 && getenv("Q35CU_GEMV_SIMT") == nullptr) return launch_gemv_mma(a, st, tp, sig);
     if (tp.mode) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: the tensor-parallel epilogue needs the tensor-core GEMV");
+    if (sig) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: the completion signal needs the tensor-core GEMV");
     uint32_t T = 0, P = 0;
     gemv_geometry(kind, K, &T, &P);
     if (P > 4) vec_ok = false;

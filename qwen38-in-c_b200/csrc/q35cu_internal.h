@@ -57,8 +57,20 @@ struct GemvTp {
     int mode = 0;
     float *gathered = nullptr;
 };
+// Completion signal of a host-pointer call: the launch's last CTA to finish
+// writes {seq, the device status word} into flag (host-mapped memory), after
+// every CTA's outputs are visible system-wide; count (device memory, zero
+// between launches) counts the CTAs out.  Only the tensor-core decode GEMV
+// (FP8, cols % 128 == 0, 16-byte aligned) signals: launch_gemv refuses a
+// signal for any other kernel.
+struct HostSignal {
+    uint32_t *count = nullptr;
+    uint32_t *flag = nullptr;
+    uint32_t seq = 0;
+};
 int launch_gemv(int kind, const GemvSeg *segs, int nseg, const float *X,
-                uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st, const GemvTp &tp = GemvTp{});
+                uint32_t K, uint32_t ldx, uint32_t m, cudaStream_t st, const GemvTp &tp = GemvTp{},
+                const HostSignal *sig = nullptr);
 // the decode chain: op descriptors are opaque bytes (chain_op_bytes each)
 size_t chain_op_bytes();
 int chain_build_op(const GemvSeg *segs, int nseg, const float *X, uint32_t K, const GemvTp &tp, void *out);

@@ -19,6 +19,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <ctime>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -93,6 +94,12 @@ struct DevState {
     size_t xbf_cap = 0;
     uint32_t *d_flag = nullptr;  // 4-byte scratch word for upload scans
     uint32_t *status_src[3] = {nullptr, nullptr, nullptr};  // the status words (host_call)
+    void *h_stage_dev = nullptr;  // the device's view of h_stage (host-mapped)
+    // completion signal of host-pointer decode calls (host_call_signal)
+    uint32_t *sig_count = nullptr;  // device: CTAs out of the current launch
+    uint32_t *sig_flag = nullptr;   // host-mapped: {seq, device status}
+    uint32_t *sig_flag_dev = nullptr;
+    uint32_t sig_seq = 0;
 };
 
 struct Key {
@@ -178,8 +185,11 @@ int ensure_stage(DevState *d, size_t bytes)
         d->h_stage = nullptr;
         d->h_cap = 0;
         size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
-        Q35CU_CUDA(cudaMallocHost(&d->h_stage, cap));
+        // mapped: the decode calls' kernels read their input from it and
+        // write their output into it (host_call_signal)
+        Q35CU_CUDA(cudaHostAlloc(&d->h_stage, cap, cudaHostAllocMapped));
         d->h_cap = cap;
+        Q35CU_CUDA(cudaHostGetDevicePointer(&d->h_stage_dev, d->h_stage, 0));
     }
     if (bytes > d->d_cap) {
         if (d->d_stage) dev_free(d->d_stage, d->d_cap);
@@ -1210,6 +1220,95 @@ int host_call(const void *X, size_t in_bytes, void *Y, size_t out_bytes, F &&fn)
     return host_call_ex(X, in_bytes, out_bytes, fn, [&](const char *out) { memcpy(Y, out, out_bytes); });
 }
 
+// The decode calls (q35_mm_fp8, q35_mm_fp8_multi4, small q35_mm_fp8_batch)
+// on a latency budget.  Each is a synchronous round trip, so per call the
+// fixed costs count as much as the kernel: on a B200 host a DMA copy in, a
+// status-gather kernel, a DMA copy out and a stream synchronisation measured
+// ~20 us beyond the kernel's own launch and run.  Here instead
+//   * the input is copied in by one DMA from the pinned staging buffer (a
+//     one-CTA copy kernel reading the mapped buffer instead measured slower);
+//   * the GEMV writes its outputs straight into the mapped staging buffer;
+//   * its last CTA writes {sequence number, device status word} into a
+//     host-mapped flag after every output is visible, and this thread polls
+//     the flag instead of synchronising the stream.
+// A flag that does not arrive within kSignalWaitS seconds ends the wait with
+// the stream's error, or Q35CU_ERR_TIMEOUT.
+constexpr size_t kSignalOutMax = 4 << 20;
+constexpr double kSignalWaitS = 60.0;
+
+double wall_s()
+{
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
+template <class F, class G>
+int host_call_signal(const void *X, size_t in_bytes, size_t out_bytes, F &&launch, G &&deliver)
+{
+    DevState *d = dev_state();
+    if (!d) return t_err;
+    if (!d->sig_count) {
+        void *c = nullptr;
+        int rc = dev_alloc(&c, 256);
+        if (rc) return rc;
+        Q35CU_CUDA(cudaMemset(c, 0, 256));
+        void *f = nullptr;
+        Q35CU_CUDA(cudaHostAlloc(&f, 64, cudaHostAllocMapped));
+        memset(f, 0, 64);
+        Q35CU_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void **>(&d->sig_flag_dev), f, 0));
+        d->sig_flag = static_cast<uint32_t *>(f);
+        d->sig_count = static_cast<uint32_t *>(c);
+    }
+    const size_t in_al = (in_bytes + 255) & ~(size_t)255;
+    const size_t out_al = (out_bytes + 255) & ~(size_t)255;
+    int rc = ensure_stage(d, in_al + out_al);
+    if (rc) return rc;
+    char *h = static_cast<char *>(d->h_stage);
+    char *hdev = static_cast<char *>(d->h_stage_dev);
+    char *dv = static_cast<char *>(d->d_stage);
+    memcpy(h, X, in_bytes);
+    Q35CU_CUDA(cudaMemcpyAsync(dv, h, in_bytes, cudaMemcpyHostToDevice, d->stream));
+    HostSignal sig;
+    sig.count = d->sig_count;
+    sig.flag = d->sig_flag_dev;
+    sig.seq = ++d->sig_seq;
+    if (sig.seq == 0) sig.seq = ++d->sig_seq;  // 0 is the flag's initial value
+    rc = launch(reinterpret_cast<const float *>(dv), reinterpret_cast<float *>(hdev + in_al), d->stream, &sig);
+    if (rc) return rc;
+    volatile uint32_t *flag = d->sig_flag;
+    const double t0 = wall_s();
+    for (uint32_t i = 1; flag[0] != sig.seq; ++i) {
+#if defined(__x86_64__)
+        __builtin_ia32_pause();
+#endif
+        if ((i & 4095) == 0 && wall_s() - t0 > kSignalWaitS) {
+            Q35CU_CUDA(cudaStreamSynchronize(d->stream));
+            if (flag[0] == sig.seq) break;
+            return set_error(Q35CU_ERR_TIMEOUT, "decode call: completion signal not seen after %.0f s", kSignalWaitS);
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    if (flag[1]) {
+        rc = check_device_status();  // reads and clears the status words
+        if (rc) return rc;
+    }
+    deliver(static_cast<const char *>(h + in_al));
+    return Q35CU_OK;
+}
+
+// the decode GEMV with a completion signal takes this call (FP8, cols a
+// multiple of 128, weights 16-byte aligned; the tensor-core GEMV's conditions)
+bool signal_ok(const q35cu_weight *w, uint32_t cols, size_t in_bytes, size_t out_bytes)
+{
+    // read on every call, as launch_gemv reads Q35CU_GEMV_SIMT
+    const bool simt = getenv("Q35CU_GEMV_SIMT") != nullptr;
+    const char *e = getenv("Q35CU_HOST_SIGNAL");
+    const bool off = e && atoi(e) == 0;
+    return !simt && !off && w && w->kind == 0 && cols % 128 == 0 && (uintptr_t)w->d_w % 16 == 0 &&
+           in_bytes <= ((size_t)64 << 20) && out_bytes <= kSignalOutMax;
+}
+
 }  // namespace
 
 Q35_API void q35_mm_fp8(const uint8_t *W, const uint16_t *scale_bf16, uint32_t rows, uint32_t cols,
@@ -1224,7 +1323,15 @@ Q35_API void q35_mm_fp8(const uint8_t *W, const uint16_t *scale_bf16, uint32_t r
     if (!W || !scale_bf16 || !x) rc = set_error(Q35CU_ERR_ARG, "q35_mm_fp8: NULL input");
     q35cu_weight *w = rc ? nullptr : cached_weight(0, W, scale_bf16, rows, cols);
     if (!rc && !w) rc = t_err;
-    if (!rc)
+    if (!rc && signal_ok(w, cols, (size_t)cols * 4, (size_t)rows * 4))
+        rc = host_call_signal(
+            x, (size_t)cols * 4, (size_t)rows * 4,
+            [&](const float *dx, float *dy, cudaStream_t st, const HostSignal *sig) {
+                GemvSeg g = seg_of(w, dy, rows);
+                return launch_gemv(0, &g, 1, dx, cols, cols, 1, st, GemvTp{}, sig);
+            },
+            [&](const char *out) { memcpy(y, out, (size_t)rows * 4); });
+    else if (!rc)
         rc = host_call(x, (size_t)cols * 4, y, (size_t)rows * 4, [&](const float *dx, float *dy, cudaStream_t st) {
             GemvSeg g = seg_of(w, dy, rows);
             return launch_gemv(0, &g, 1, dx, cols, cols, 1, st);
@@ -1274,6 +1381,14 @@ Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
             return launch_gemm_exact(w, dx, n, dy, dev_state()->d_xbf, st);
         });
+    else if (!rc && n <= 65535u * 4u && signal_ok(w, cols, (size_t)n * cols * 4, nout * 4))
+        rc = host_call_signal(
+            X, (size_t)n * cols * 4, nout * 4,
+            [&](const float *dx, float *dy, cudaStream_t st, const HostSignal *sig) {
+                GemvSeg g = seg_of(w, dy, rows);
+                return launch_gemv(0, &g, 1, dx, cols, cols, n, st, GemvTp{}, sig);
+            },
+            [&](const char *out) { memcpy(Y, out, nout * 4); });
     else if (!rc)
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
             GemvSeg g = seg_of(w, dy, rows);
@@ -1313,27 +1428,34 @@ Q35_API void q35_mm_fp8_multi4(const uint8_t *W[4], const uint16_t *sc[4], uint3
     }
     if (!rc) {
         // outputs of the segments packed back to back in the staging area
-        rc = host_call_ex(
-            x, (size_t)cols * 4, (size_t)total * 4,
-            [&](const float *dx, float *dy, cudaStream_t st) {
-                GemvSeg segs[4];
-                int n = 0;
-                size_t off = 0;
-                for (int s = 0; s < 4; ++s) {
-                    if (!ws[s]) continue;
-                    segs[n++] = seg_of(ws[s], dy + off, rows[s]);
-                    off += rows[s];
-                }
-                return launch_gemv(0, segs, n, dx, cols, cols, 1, st);
-            },
-            [&](const char *out) {
-                size_t off = 0;
-                for (int s = 0; s < 4; ++s) {
-                    if (!ws[s]) continue;
-                    memcpy(y[s], reinterpret_cast<const float *>(out) + off, (size_t)rows[s] * 4);
-                    off += rows[s];
-                }
-            });
+        bool sig_ok = true;
+        for (int s = 0; s < 4; ++s)
+            if (ws[s] && !signal_ok(ws[s], cols, (size_t)cols * 4, (size_t)total * 4)) sig_ok = false;
+        auto launch = [&](const float *dx, float *dy, cudaStream_t st, const HostSignal *sig) {
+            GemvSeg segs[4];
+            int n = 0;
+            size_t off = 0;
+            for (int s = 0; s < 4; ++s) {
+                if (!ws[s]) continue;
+                segs[n++] = seg_of(ws[s], dy + off, rows[s]);
+                off += rows[s];
+            }
+            return launch_gemv(0, segs, n, dx, cols, cols, 1, st, GemvTp{}, sig);
+        };
+        auto scatter = [&](const char *out) {
+            size_t off = 0;
+            for (int s = 0; s < 4; ++s) {
+                if (!ws[s]) continue;
+                memcpy(y[s], reinterpret_cast<const float *>(out) + off, (size_t)rows[s] * 4);
+                off += rows[s];
+            }
+        };
+        if (sig_ok)
+            rc = host_call_signal(x, (size_t)cols * 4, (size_t)total * 4, launch, scatter);
+        else
+            rc = host_call_ex(
+                x, (size_t)cols * 4, (size_t)total * 4,
+                [&](const float *dx, float *dy, cudaStream_t st) { return launch(dx, dy, st, nullptr); }, scatter);
     }
     if (rc) fail_host(outs, counts, 4);
 }

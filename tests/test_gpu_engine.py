@@ -13,6 +13,12 @@ they read copied beside them).
   B200, logits against the reference's stored logits) and test_oracle
   (logits of a transformer reference) run on the GPU.
 
+The same programs also run against oracle/_ref/engine_batched: the engine
+with the prefill caller change of oracle/prefill_batch.py (the DeltaNet
+out_proj and the GQA o_proj of a prefill made as one q35_mm_fp8_batch over
+all tokens instead of one q35_mm_fp8 per token), with test_prefill (batch
+prefill against token-by-token decode of the tiny model) on both engines.
+
 The programs' own pass criteria decide; exit code 77 is their "skip".
 The reference's mm fixtures lack the qkvlike_fp8.w8 blob (listed in its
 .MISSING_LARGE_BLOBS): test_mm checks every case up to it and then stops on
@@ -27,12 +33,13 @@ import pytest
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ENG = os.path.join(os.path.dirname(HERE), "oracle", "_ref", "engine")
+ENGB = os.path.join(os.path.dirname(HERE), "oracle", "_ref", "engine_batched")
 
 
-def _run(prog: str, *args: str, timeout: int = 600) -> subprocess.CompletedProcess:
-    exe = os.path.join(ENG, prog)
+def _run(prog: str, *args: str, timeout: int = 600, eng: str = ENG) -> subprocess.CompletedProcess:
+    exe = os.path.join(eng, prog)
     if not os.path.exists(exe):
-        pytest.skip(f"{exe} not built (make -C oracle engine, needs the reference tree)")
+        pytest.skip(f"{exe} not built (make -C oracle engine engine-batched, needs the reference tree)")
     return subprocess.run([exe, *args], cwd=ENG, capture_output=True, text=True, timeout=timeout)
 
 
@@ -89,3 +96,16 @@ def test_engine_model(gpu):
 @pytest.mark.gpu
 def test_engine_oracle(gpu):
     _check(_run("test_oracle", _fix("oracle")))
+
+
+@pytest.mark.gpu
+def test_engine_prefill(gpu):
+    _check(_run("test_prefill", _fix("model")))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prog,fix", [("test_deltanet", "deltanet"), ("test_attn", "attn"), ("test_model", "model"),
+                                      ("test_oracle", "oracle"), ("test_prefill", "model")])
+def test_engine_batched_prefill(gpu, prog, fix):
+    """The reference's own tests on the engine with the batched out/o prefill."""
+    _check(_run(prog, _fix(fix), eng=ENGB))

@@ -136,6 +136,57 @@ struct GemmArgs {
     float *Y;             // [m, N] token-major ([m / 2, N] when pair)
     uint32_t N, K, m, kblocks, mtiles, ntiles;
     uint32_t pair;        // rows 2t, 2t+1 are the hi and lo halves of token t: Y[t] = their sum
+    // Stream-K (sk == 1; narrow token tiles): the launch's U = ntiles x
+    // kblocks (tile, block) units, tile-major, are cut into equal ranges,
+    // CTA c taking [U*c/G, U*(c+1)/G), so every CTA converts and multiplies
+    // the same number of weight blocks whatever the tile count.  A tile cut
+    // by a CTA boundary is finished by segments of several CTAs: each writes
+    // its fp32 accumulator to skpart (slot = the tile's first inner boundary
+    // c1, segment j = CTA - (c1 - 1)); the CTA whose segment completes the
+    // tile's count (skcnt[c1]) adds the segments in order j = 0, 1, ... and
+    // stores Y -- a fixed order, so runs repeat bit for bit.
+    uint32_t sk;
+    uint32_t maxseg;      // segment slots per tile in skpart
+    float *skpart;        // [G][maxseg][BN][128] (rows fastest)
+    uint32_t *skcnt;      // [G] blocks done of a cut tile (zero between launches)
+};
+
+// The (tile, first block, end block) segments a CTA walks, in order: whole
+// tiles blockIdx.x, + gridDim.x, ... or, under stream-K, its unit range.
+// SKOK = false compiles the whole-tile walk alone (the 192-token prefill
+// tile, whose epilogue has no registers to spare for the stream-K state).
+template <bool SKOK>
+struct SegWalk {
+    uint32_t u, u1, nkb, ntiles;
+    bool sk;
+    __device__ __forceinline__ explicit SegWalk(const GemmArgs &a)
+        : nkb(a.kblocks), ntiles(a.ntiles), sk(SKOK && a.sk != 0)
+    {
+        if (sk) {
+            const uint64_t U = (uint64_t)a.ntiles * a.kblocks;
+            u = (uint32_t)(U * blockIdx.x / gridDim.x);
+            u1 = (uint32_t)(U * (blockIdx.x + 1) / gridDim.x);
+        } else {
+            u = blockIdx.x;
+            u1 = a.ntiles;
+        }
+    }
+    __device__ __forceinline__ bool next(uint32_t &tile, uint32_t &kb0, uint32_t &kb1)
+    {
+        if (u >= u1) return false;
+        if (sk) {
+            tile = u / nkb;
+            kb0 = u % nkb;
+            kb1 = nkb - kb0 < u1 - u ? nkb : kb0 + (u1 - u);
+            u += kb1 - kb0;
+        } else {
+            tile = u;
+            kb0 = 0;
+            kb1 = nkb;
+            u += gridDim.x;
+        }
+        return true;
+    }
 };
 
 template <int BN>
@@ -143,8 +194,9 @@ struct Smem {  // offsets from the 1024-aligned base (every tile size is a multi
     static constexpr uint32_t x(int s) { return s * x_tile<BN>(); }
     static constexpr uint32_t w(int s) { return stages<BN>() * x_tile<BN>() + s * kWTile; }
     static constexpr uint32_t bars = stages<BN>() * x_tile<BN>() + wstages<BN>() * kWTile;
-    // x_full, ready, done [S]; w_full, w_empty [WS]; fin [2]; abort flag; TMEM address
-    static_assert((3 * stages<BN>() + 2 * wstages<BN>() + 2) * 8 + 8 <= 256, "barriers fit their 256 bytes");
+    // x_full, ready, done [S]; w_full, w_empty [WS]; fin [2]; abort flag; TMEM address;
+    // stream-K decision word; aborted epilogue warps
+    static_assert((3 * stages<BN>() + 2 * wstages<BN>() + 2) * 8 + 16 <= 256, "barriers fit their 256 bytes");
     static constexpr uint32_t total = bars + 256;
     static_assert(x_tile<BN>() % 1024 == 0 && x_atom<BN>() % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 };
@@ -334,6 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using Sm = Smem<BN>;
     constexpr int S = stages<BN>(), D = depth<BN>(), WS = wstages<BN>();
     constexpr uint32_t kFull = 0xffffffffu;
+    constexpr bool kSK = BN <= 128;  // stream-K is compiled for the narrow token tiles only
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     // block g uses slot g % S of the activation rings:
@@ -350,6 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *fin = w_empty + WS;
     volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(fin + 2);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 2) + 1;
+    volatile uint32_t *sk_state = reinterpret_cast<volatile uint32_t *>(fin + 2) + 2;
+    volatile uint32_t *epi_aborts = reinterpret_cast<volatile uint32_t *>(fin + 2) + 3;
 
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const uint32_t nkb = a.kblocks;
@@ -373,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bar_init(&fin[0], 1);
         bar_init(&fin[1], 1);
         *abort = 0;
+        *epi_aborts = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -391,11 +447,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // so the .sync.aligned TMEM instructions always see a converged warp.
     if (warp == kWarpX) {
         // ---------------- activation producer (whole warp) -----------------
-        uint32_t g = 0;
+        uint32_t g = 0, tile, kb0, kb1;
         bool ok = true;
-        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+        for (SegWalk<kSK> walk(a); ok && walk.next(tile, kb0, kb1);) {
             const int m0 = (int)((tile % a.mtiles) * BN);
-            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+            for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
                 const int s = g % S;
                 if (g >= (uint32_t)S)
                     ok = __all_sync(kFull, bar_wait(&done[s], ((g / S) - 1) & 1, abort, kRoleX, g));
@@ -408,11 +464,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         drain(x_full, S, g);  // g = copies issued
     } else if (warp == kWarpW) {
         // ---------------- weight producer (whole warp) ---------------------
-        uint32_t g = 0;
+        uint32_t g = 0, tile, kb0, kb1;
         bool ok = true;
-        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+        for (SegWalk<kSK> walk(a); ok && walk.next(tile, kb0, kb1);) {
             const int n0 = (int)((tile / a.mtiles) * kBM);
-            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+            for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
                 const int s = g % WS;
                 if (g >= (uint32_t)WS)
                     ok = __all_sync(kFull, bar_wait(&w_empty[s], ((g / WS) - 1) & 1, abort, kRoleW, g));
@@ -429,10 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // idle; two warps take alternate blocks (each block has its own P, A
         // and activation stage) and one warp's wait overlaps the other's MMAs.
         const uint32_t parity = warp == kWarpMma ? 0u : 1u;
-        uint32_t g = 0;
+        uint32_t g = 0, tile, kb0, kb1;
         bool ok = true;
-        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
-            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+        for (SegWalk<kSK> walk(a); ok && walk.next(tile, kb0, kb1);) {
+            for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
                 if ((g & 1) != parity) continue;
                 const int s = g % S, j = g % D;
                 const uint32_t ph = (g / S) & 1;
@@ -465,10 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t r = quad * 32 + lane;
         const uint32_t sw = r & 7;
         const uint32_t lane_base = tmem + ((quad * 32) << 16) + tmem_a<BN>();
-        uint32_t g = 0;
+        uint32_t g = 0, tile, kb0, kb1;
         bool ok = true;
-        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
-            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+        for (SegWalk<kSK> walk(a); ok && walk.next(tile, kb0, kb1);) {
+            for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
                 const int s = g % WS, j = g % D;
                 bool w = bar_wait(&w_full[s], (g / WS) & 1, abort, kRoleConv, g);
                 // A[g % D] was last read by block g - D
@@ -511,48 +567,149 @@ __global__ void __launch_bounds__(kThreads, 1)
         // P[0..D) start out free for blocks 0..D-1
         if (lane == 0)
             for (int i = 0; i < D; ++i) bar_arrive(&ready[i]);
-        uint32_t g = 0;
-        bool ok = true;
-        for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
-            const uint32_t rb = tile / a.mtiles;
-            const uint32_t n = rb * kBM + quad * 32 + lane;               // weight row
-            const uint32_t t0 = (tile % a.mtiles) * BN + grp * 64;        // first token
-            const float *srow = a.S + (size_t)rb * nkb;
-            float acc[64];
-            float sc = __ldg(srow);
-            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int j = g % D;
-                const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
-                ok = __all_sync(kFull, bar_wait(&done[g % S], (g / S) & 1, abort, kRoleEpi, g));
-                if (!ok) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if constexpr (!kSK) {
+            // whole tiles (the 192-token prefill tile)
+            uint32_t g = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
+                const uint32_t rb = tile / a.mtiles;
+                const uint32_t n = rb * kBM + quad * 32 + lane;               // weight row
+                const uint32_t t0 = (tile % a.mtiles) * BN + grp * 64;        // first token
+                const float *srow = a.S + (size_t)rb * nkb;
+                float acc[64];
+                float sc = __ldg(srow);
+                for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                    const int j = g % D;
+                    const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
+                    ok = __all_sync(kFull, bar_wait(&done[g % S], (g / S) & 1, abort, kRoleEpi, g));
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (16 * c < ncol) {  // warp-uniform
-                        uint32_t p[16];
-                        tmem_ld16(tbase + j * BN + c * 16, p);
-                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                        promote16(acc + 16 * c, p, sc, kb == 0);
+                    for (int c = 0; c < 4; ++c) {
+                        if (16 * c < ncol) {  // warp-uniform
+                            uint32_t p[16];
+                            tmem_ld16(tbase + j * BN + c * 16, p);
+                            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                            promote16(acc + 16 * c, p, sc, kb == 0);
+                        }
+                    }
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(&ready[(g + D) % S]);  // P[g % D] is free for block g + D
+                    sc = sc_next;
+                }
+                if (ok && n < a.N) {
+                    if (a.pair) {  // t0 is even: columns (2i, 2i+1) are token (t0 + 2i) / 2's hi and lo
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const uint32_t tok2 = t0 + 2 * i;
+                            if (2 * i < ncol && tok2 < a.m)
+                                a.Y[(size_t)(tok2 >> 1) * a.N + n] = (acc[2 * i] + acc[2 * i + 1]) * __ldg(a.tscale + tok2);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 64; ++i) {
+                            const uint32_t tok = t0 + i;
+                            if (i < ncol && tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                        }
                     }
                 }
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) bar_arrive(&ready[(g + D) % S]);  // P[g % D] is free for block g + D
-                sc = sc_next;
             }
-            if (ok && n < a.N) {
-                if (a.pair) {  // t0 is even: columns (2i, 2i+1) are token (t0 + 2i) / 2's hi and lo
+        } else {
+            // the 12 epilogue warps alone (stream-K hand-off of a cut tile)
+            auto epi_bar = [] { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); };
+            uint32_t g = 0, tile, kb0, kb1;
+            bool ok = true;
+            // every segment is visited even after an abort: the hand-off of a
+            // cut tile needs all 12 warps at its barriers
+            for (SegWalk<kSK> walk(a); walk.next(tile, kb0, kb1);) {
+                const uint32_t rb = tile / a.mtiles;
+                const uint32_t row = quad * 32 + lane;
+                const uint32_t n = rb * kBM + row;                            // weight row
+                const uint32_t t0 = (tile % a.mtiles) * BN + grp * 64;        // first token
+                const float *srow = a.S + (size_t)rb * nkb;
+                float acc[64];
+                float sc = ok ? __ldg(srow + kb0) : 0.f;
+                for (uint32_t kb = kb0; ok && kb < kb1; ++kb, ++g) {
+                    const int j = g % D;
+                    const float sc_next = kb + 1 < kb1 ? __ldg(srow + kb + 1) : 0.f;
+                    ok = __all_sync(kFull, bar_wait(&done[g % S], (g / S) & 1, abort, kRoleEpi, g));
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const uint32_t tok2 = t0 + 2 * i;
-                        if (2 * i < ncol && tok2 < a.m)
-                            a.Y[(size_t)(tok2 >> 1) * a.N + n] = (acc[2 * i] + acc[2 * i + 1]) * __ldg(a.tscale + tok2);
+                    for (int c = 0; c < 4; ++c) {
+                        if (16 * c < ncol) {  // warp-uniform
+                            uint32_t p[16];
+                            tmem_ld16(tbase + j * BN + c * 16, p);
+                            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                            promote16(acc + 16 * c, p, sc, kb == kb0);
+                        }
                     }
-                } else {
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(&ready[(g + D) % S]);  // P[g % D] is free for block g + D
+                    sc = sc_next;
+                }
+                bool store = ok;
+                if (kSK && (kb0 != 0 || kb1 != nkb)) {
+                    // stream-K: this CTA's share of a cut tile.  Slot c1 = the
+                    // tile's first inner CTA boundary, segment j = CTA - (c1 - 1).
+                    const uint64_t U = (uint64_t)a.ntiles * nkb;
+                    const uint32_t c1 = (uint32_t)((((uint64_t)tile * nkb + 1) * gridDim.x + U - 1) / U);
+                    const uint32_t cl = (uint32_t)(((uint64_t)(tile + 1) * nkb * gridDim.x + U - 1) / U) - 1;
+                    float *slot0 = a.skpart + (size_t)c1 * a.maxseg * BN * kBM;
+                    if (ok) {
+                        float *sl = slot0 + (size_t)(blockIdx.x + 1 - c1) * BN * kBM + (size_t)grp * 64 * kBM + row;
 #pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        const uint32_t tok = t0 + i;
-                        if (i < ncol && tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                        for (int i = 0; i < 64; ++i)
+                            if (i < ncol) sl[(size_t)i * kBM] = acc[i];
+                    } else if (lane == 0) {
+                        atomicAdd(const_cast<uint32_t *>(epi_aborts), 1u);
+                    }
+                    epi_bar();
+                    if (warp == kWarpEpi && lane == 0) {
+                        uint32_t st_ = 0;
+                        if (*abort == 0 && *epi_aborts == 0) {
+                            __threadfence();
+                            const uint32_t done_ = atomicAdd(a.skcnt + c1, kb1 - kb0) + (kb1 - kb0);
+                            st_ = 1;
+                            if (done_ == nkb) {  // the tile's last segment: this CTA stores it
+                                __threadfence();
+                                a.skcnt[c1] = 0;  // ready for the next launch
+                                st_ = 3;
+                            }
+                        }
+                        *sk_state = st_;
+                    }
+                    epi_bar();
+                    const uint32_t st_ = *sk_state;
+                    if (!(st_ & 1)) ok = false;
+                    store = (st_ & 2) != 0;
+                    if (store) {
+                        const float *sl = slot0 + (size_t)grp * 64 * kBM + row;
+#pragma unroll
+                        for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+                        for (uint32_t js = 0; js < cl - c1 + 2; ++js, sl += (size_t)BN * kBM) {
+#pragma unroll
+                            for (int i = 0; i < 64; ++i)
+                                if (i < ncol) acc[i] += __ldcg(sl + (size_t)i * kBM);
+                        }
+                    }
+                }
+                if (store && n < a.N) {
+                    if (a.pair) {  // t0 is even: columns (2i, 2i+1) are token (t0 + 2i) / 2's hi and lo
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const uint32_t tok2 = t0 + 2 * i;
+                            if (2 * i < ncol && tok2 < a.m)
+                                a.Y[(size_t)(tok2 >> 1) * a.N + n] = (acc[2 * i] + acc[2 * i + 1]) * __ldg(a.tscale + tok2);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 64; ++i) {
+                            const uint32_t tok = t0 + i;
+                            if (i < ncol && tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                        }
                     }
                 }
             }
@@ -767,6 +924,64 @@ int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *
 
 namespace {
 
+// Stream-K scratch, one per device: counters (kSkCntBytes) then the cut
+// tiles' partial accumulators.  Grown (never shrunk or freed: CUDA graphs
+// may hold its address) when a launch needs more, except under stream
+// capture, where such a launch walks whole tiles instead.  Launches on
+// different streams of one device that run at the same time must not both
+// use it -- the library's own calls run in stream order.
+constexpr size_t kSkCntBytes = 4096;
+struct SkScratch {
+    void *p = nullptr;
+    size_t bytes = 0;
+};
+SkScratch g_sk[64];
+
+// Stream-K for a narrow-tile launch when it cuts the busiest CTA's block
+// count by a tenth or more; fills a's stream-K fields.  false = whole tiles.
+constexpr uint64_t kSkMinBlocks = 8;             // blocks per CTA at least (amortises a cut tile's hand-off)
+constexpr size_t kSkMaxBytes = (size_t)64 << 20;  // scratch cap
+
+template <int BN>
+bool plan_stream_k(GemmArgs &a, uint32_t sms, cudaStream_t st, uint32_t *grid)
+{
+    if (BN > 128 || getenv("Q35CU_GEMM_NO_STREAMK")) return false;
+    const uint64_t U = (uint64_t)a.ntiles * a.kblocks;
+    const uint32_t G = (uint32_t)(U / kSkMinBlocks < sms ? U / kSkMinBlocks : sms);
+    if (G < 2) return false;
+    const uint64_t per = U / G;
+    const uint64_t whole = ((a.ntiles + sms - 1) / sms) * (uint64_t)a.kblocks;
+    const uint64_t sk = (U + G - 1) / G;
+    if (sk * 10 > whole * 9) return false;
+    const uint32_t maxseg = (uint32_t)((a.kblocks + per - 1) / per + 1);
+    const size_t need = kSkCntBytes + (size_t)G * maxseg * BN * kBM * 4;
+    if (G * 4 > kSkCntBytes || need > kSkMaxBytes) return false;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    SkScratch &sc = g_sk[dev];
+    if (sc.bytes < need) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) { cudaGetLastError(); return false; }
+        if (cs != cudaStreamCaptureStatusNone) return false;
+        const size_t bytes = need > ((size_t)16 << 20) ? need : ((size_t)16 << 20);
+        void *p = nullptr;
+        if (dev_alloc(&p, bytes) != Q35CU_OK) { q35cu_clear_error(); return false; }
+        if (cudaMemset(p, 0, kSkCntBytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            cudaGetLastError();
+            dev_free(p, bytes);
+            return false;
+        }
+        sc.p = p;  // an earlier, smaller scratch stays allocated (graphs may hold it)
+        sc.bytes = bytes;
+    }
+    a.sk = 1;
+    a.maxseg = maxseg;
+    *grid = G;
+    a.skcnt = static_cast<uint32_t *>(sc.p);
+    a.skpart = reinterpret_cast<float *>(static_cast<uint8_t *>(sc.p) + kSkCntBytes);
+    return true;
+}
+
 template <int BN>
 int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
                    cudaStream_t st, bool pair)
@@ -779,7 +994,8 @@ int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscal
     if (rc) return rc;
     rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
     if (rc) return rc;
-    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, pair ? 1u : 0u};
+    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, pair ? 1u : 0u,
+               0u, 0u, nullptr, nullptr};
     static bool configured[64] = {};  // per instantiation and device
     int dev = 0, sms = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));
@@ -790,7 +1006,8 @@ int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscal
         Q35CU_CUDA(cudaFuncSetAttribute(gemm_fp8_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured[dev] = true;
     }
-    const uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
+    uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
+    plan_stream_k<BN>(a, (uint32_t)sms, st, &grid);
     gemm_fp8_tc_kernel<BN><<<grid, kThreads, smem, st>>>(mx, mw, a);
     count_launch();
     Q35CU_CUDA(cudaGetLastError());

@@ -299,3 +299,21 @@ def test_cache_detects_reused_address(gpu, orc):
     b = q35cu.mm_fp8(W, sc, x)
     assert np.array_equal(b.view(np.uint32), q35cu.mm_fp8(W2, sc2, x).view(np.uint32))
     assert not np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("rows,cols,n", [(5120, 17408, 16), (5120, 6144, 33), (5120, 6144, 64), (1024, 5120, 40)])
+def test_stream_k_tensor_core_decode(gpu, orc, ref, monkeypatch, rows, cols, n):
+    """Multi-token decode on the tensor cores with few row tiles walks equal
+    ranges of (tile, 128-column block) units per CTA (stream-K); a tile cut
+    by CTA boundaries is finished by adding its segments' accumulators in a
+    fixed order.  Runs repeat bit for bit, and both this walk and the
+    whole-tile walk (Q35CU_GEMM_NO_STREAMK) meet the GEMV bound."""
+    W, sc = _synth(orc, 2100 + rows + n, rows, cols)
+    X = orc.synth_act(2200 + n, (n, cols))
+    Yr = ref.mm_fp8_batch(W, sc, X)
+    Y1 = q35cu.mm_fp8_batch(W, sc, X)
+    Y2 = q35cu.mm_fp8_batch(W, sc, X)
+    assert np.array_equal(Y1.view(np.uint32), Y2.view(np.uint32))
+    _check(orc, W, sc, X, Y1, Yr, f"stream-K {rows}x{cols} n={n}")
+    monkeypatch.setenv("Q35CU_GEMM_NO_STREAMK", "1")
+    _check(orc, W, sc, X, q35cu.mm_fp8_batch(W, sc, X), Yr, f"whole tiles {rows}x{cols} n={n}")

@@ -22,7 +22,13 @@ projections is not part of the matmul path and is not run.
 Tensor parallelism (world > 1): "literal" all-gathers each column-parallel
 output ([M, N/p] fp32 per rank) and all-reduces each row-parallel partial
 ([M, 5120] fp32) with NCCL; "paired" (Megatron) drops the all-gathers -- the
-row-parallel projection consumes the local shard.
+row-parallel projection consumes the local shard.  Under TP the tokens are
+cut into `slabs` row slabs (a slab's rows are contiguous in every [M, N]
+buffer): each projection runs slab by slab on the compute stream, and each
+slab's collective runs on a second stream as soon as that slab's GEMM is
+done, so the exchange of slab i overlaps the GEMMs of slab i + 1 onwards;
+a GEMM that consumes an all-reduced output (gate/up after out/o) waits for
+that slab's all-reduce only.
 """
 from __future__ import annotations
 
@@ -33,12 +39,16 @@ import stack
 class PrefillLayers:
     """Device buffers for M tokens through one layer of each kind of `st`."""
 
-    def __init__(self, st: "stack.Stack", m: int = 8192, scheme: str = "literal", seed: int = 4321):
+    def __init__(self, st: "stack.Stack", m: int = 8192, scheme: str = "literal", seed: int = 4321,
+                 slabs: int | None = None):
         import torch
 
         assert scheme in ("literal", "paired")
         self.st, self.m, self.scheme = st, m, scheme
         self.world = st.world
+        self.slabs = (4 if st.world > 1 else 1) if slabs is None else slabs
+        assert m % self.slabs == 0
+        self.comm = torch.cuda.Stream(device=st.dev) if st.world > 1 else None
         self.dn = next(L for L in st.layers if L.kind == "dn")
         self.gqa = next(L for L in st.layers if L.kind == "gqa")
         dev = st.dev
@@ -68,32 +78,74 @@ class PrefillLayers:
         return self.xb[:n].view(src.shape[0], -1)
 
     def layer(self, L, stream=None, keep=None) -> None:
-        """Issue one layer's projections (asynchronous on `stream`).  `keep`, a
-        dict, receives clones of every GEMM's bf16 input (for checks)."""
-        literal = self.scheme == "literal" and self.world > 1
+        """Issue one layer's projections (asynchronous on `stream`, the
+        current stream if None; the collectives of a TP run go on the
+        second stream, joined back before this returns).  `keep`, a dict,
+        receives clones of every GEMM's bf16 input (for checks)."""
+        import torch
 
-        def run(w, xin, yout, name):
+        literal = self.scheme == "literal" and self.world > 1
+        cs = stream if stream is not None else torch.cuda.current_stream(self.st.dev)
+        S = self.slabs
+        ms = self.m // S
+        rows = [slice(i * ms, (i + 1) * ms) for i in range(S)]
+        if self.comm is not None:
+            self.comm.wait_stream(cs)  # buffers written before this layer
+
+        def gemm(w, xin, yout, name):
+            """the GEMM slab by slab on cs; the event after each slab"""
             if keep is not None:
                 keep[name] = xin.clone()
-            q35cu.gemm(w, xin, yout, self.work, stream)
+            evs = []
+            for r in rows:
+                q35cu.gemm(w, xin[r], yout[r], self.work, cs)  # one workspace: slabs in order on cs
+                if self.comm is not None:
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    evs.append(ev)
+            return evs
+
+        def exchange(evs, buf, out=None):
+            """each slab's all-gather (out given) or all-reduce on the second
+            stream, after that slab's GEMM; the events after each"""
+            done = []
+            per = buf.numel() // S
+            for i, r in enumerate(rows):
+                self.comm.wait_event(evs[i])
+                if out is not None:
+                    q35cu.allgather(buf[r], out[i * per * self.world:(i + 1) * per * self.world], self.comm)
+                else:
+                    q35cu.allreduce(buf[r], self.comm)
+                ev = torch.cuda.Event()
+                ev.record(self.comm)
+                done.append(ev)
+            return done
 
         for p in L.col_in:
-            run(p.w, self.x, self.col[p.name], p.name)
+            evs = gemm(p.w, self.x, self.col[p.name], p.name)
             if literal:
-                q35cu.allgather(self.col[p.name], self.gath[p.name], stream)
+                exchange(evs, self.col[p.name], self.gath[p.name])
         src = self.col["z"] if L.kind == "dn" else self.attn
-        run(L.attn_out.w, self.bf16(src, stream), self.o, L.attn_out.name)
+        evs = gemm(L.attn_out.w, self.bf16(src, cs), self.o, L.attn_out.name)
+        xo = self.xb[:self.o.numel()].view(self.m, -1)
         if self.world > 1:
-            q35cu.allreduce(self.o, stream)
-        xo = self.bf16(self.o, stream)
-        run(L.gate.w, xo, self.gu["gate"], "gate")
-        run(L.up.w, xo, self.gu["up"], "up")
+            # gate / up of slab i wait for that slab's all-reduce only
+            done = exchange(evs, self.o)
+            for i, r in enumerate(rows):
+                cs.wait_event(done[i])
+                q35cu.f32_to_bf16(self.o[r], xo[r], cs)
+        else:
+            q35cu.f32_to_bf16(self.o, xo, cs)
+        g_evs = gemm(L.gate.w, xo, self.gu["gate"], "gate")
         if literal:
-            for n in ("gate", "up"):
-                q35cu.allgather(self.gu[n], self.gu_g[n], stream)
-        run(L.down.w, self.bf16(self.gu["gate"], stream), self.y, "down")
+            exchange(g_evs, self.gu["gate"], self.gu_g["gate"])
+        u_evs = gemm(L.up.w, xo, self.gu["up"], "up")
+        if literal:
+            exchange(u_evs, self.gu["up"], self.gu_g["up"])
+        evs = gemm(L.down.w, self.bf16(self.gu["gate"], cs), self.y, "down")
         if self.world > 1:
-            q35cu.allreduce(self.y, stream)
+            exchange(evs, self.y)
+            cs.wait_stream(self.comm)
 
     def flops(self, L) -> float:
         """This rank's GEMM flops for one layer of L's kind."""

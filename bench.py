@@ -67,8 +67,10 @@ def parse(argv=None):
     ap.add_argument("--profile-c2", action="store_true",
                     help="only the configuration-2 gate projection at M=2048 through the GEMM (for ncu captures)")
     ap.add_argument("--profile-c1-tc", type=int, default=0, metavar="M",
-                    help="only the 17408x5120 projection at M tokens through the tensor cores on exact "
-                         "activations (q35cu_gemv_fp8_tc), --steps calls (for ncu captures)")
+                    help="only one projection (--profile-shape, default 17408x5120) at M tokens through the "
+                         "tensor cores on exact activations (q35cu_gemv_fp8_tc), --steps calls (for ncu captures)")
+    ap.add_argument("--profile-shape", default="17408x5120", metavar="ROWSxCOLS",
+                    help="the projection shape of --profile-c1-tc")
     ap.add_argument("--profile-lm-head", type=int, default=0, metavar="ROWS",
                     help="only the bf16 lm_head matvec on ROWS x 5120, --steps calls (for ncu captures)")
     return ap.parse_args(argv)
@@ -1095,18 +1097,21 @@ def run_profile_c1_tc(args):
     L = q35cu.load()
     q35cu.check(L.q35cu_set_device(0))
     m = args.profile_c1_tc
-    w = q35cu.Weight.synth_fp8(1000, 17408, 5120)
+    rows, cols = (int(v) for v in args.profile_shape.lower().split("x"))
+    w = q35cu.Weight.synth_fp8(1000, rows, cols)
     try:
-        X = torch.randn((m, 5120), device="cuda")
-        Y = torch.empty((m, 17408), device="cuda")
-        work = torch.empty(L.q35cu_gemv_fp8_tc_workspace_bytes(m, 5120), dtype=torch.uint8, device="cuda")
+        X = torch.randn((m, cols), device="cuda")
+        Y = torch.empty((m, rows), device="cuda")
+        work = torch.empty(L.q35cu_gemv_fp8_tc_workspace_bytes(m, cols), dtype=torch.uint8, device="cuda")
         for _ in range(max(1, args.steps)):
             q35cu.gemv_tc(w, X, Y, work)
         torch.cuda.synchronize()
+        q35cu.check_device_status()
         ok = bool(torch.isfinite(Y).all())
     finally:
         w.free()
-    print(json.dumps({"config1_tc": "ok" if ok else "non-finite", "m": m, "launches": max(1, args.steps)}), flush=True)
+    print(json.dumps({"config1_tc": "ok" if ok else "non-finite", "m": m, "shape": [rows, cols],
+                      "launches": max(1, args.steps)}), flush=True)
     return 0 if ok else 1
 
 

@@ -601,7 +601,7 @@ def time_config4(d: Dist, bf16_peak, m=8192, reps=3, scheme="literal"):
         pf = prefill.PrefillLayers(st, m=m, scheme=scheme)
         out = {}
         for name, L in (("dn", pf.dn), ("gqa", pf.gqa)):
-            pf.layer(L)  # warm-up
+            pf.layer_reserved(L)  # warm-up
             torch.cuda.synchronize()
             q35cu.check_device_status()
             d.barrier()
@@ -609,7 +609,7 @@ def time_config4(d: Dist, bf16_peak, m=8192, reps=3, scheme="literal"):
             for _ in range(reps):
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-                pf.layer(L)
+                pf.layer_reserved(L)
                 e1.record()
                 torch.cuda.synchronize()
                 ts.append(e0.elapsed_time(e1))

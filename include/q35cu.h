@@ -170,6 +170,12 @@ int q35cu_gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m
 size_t q35cu_gemv_fp8_tc_workspace_bytes(uint32_t m, uint32_t cols);
 int q35cu_gemv_fp8_tc(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
                       size_t workspace_bytes, void *stream);
+/* The tensor-core GEMM is persistent (one CTA per SM).  When a caller runs
+ * other work beside it -- a collective on another stream overlapping the
+ * next token slab's GEMM -- a CTA that finds its SM busy starts late and
+ * holds up its share of the tiles.  q35cu_gemm_reserve_sms(n) makes later
+ * GEMM launches of this process use n SMs fewer (0 = all; the default). */
+int q35cu_gemm_reserve_sms(int n);
 /* fp32 -> bf16 (nearest even) conversion of n values. */
 int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream);
 /* y[rows] = W x for a bf16 weight (q35_mm_bf16). */

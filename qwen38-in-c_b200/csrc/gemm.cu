@@ -76,6 +76,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
+
 #include "q35cu_internal.h"
 
 namespace q35cu {
@@ -867,6 +869,9 @@ int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_
     return Q35CU_OK;
 }
 
+// SMs the persistent GEMM leaves free (q35cu_gemm_reserve_sms)
+std::atomic<int> g_gemm_reserved_sms{0};
+
 // SM count of the current device, looked up once per device
 int sm_count_of(int dev, int *out)
 {
@@ -1001,6 +1006,9 @@ int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscal
     Q35CU_CUDA(cudaGetDevice(&dev));
     rc = sm_count_of(dev, &sms);
     if (rc) return rc;
+    // leave SMs to kernels that run beside the GEMM (a collective on another stream)
+    const int reserve = g_gemm_reserved_sms.load();
+    if (reserve > 0 && reserve < sms) sms -= reserve;
     const size_t smem = Smem<BN>::total + 1024;
     if (!configured[dev]) {
         Q35CU_CUDA(cudaFuncSetAttribute(gemm_fp8_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -1101,6 +1109,13 @@ int gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m, floa
     rc = launch_gemm_prep(X, true, m, w->cols, xh, ts, st);
     if (rc) return rc;
     return launch_gemm_fp8(w, xh, ts, m, Y, st);
+}
+
+int gemm_reserve_sms(int n)
+{
+    if (n < 0) return set_error(Q35CU_ERR_ARG, "gemm_reserve_sms: %d", n);
+    g_gemm_reserved_sms.store(n);
+    return Q35CU_OK;
 }
 
 uint32_t *gemm_status_word()

@@ -95,6 +95,7 @@ int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *
                       cudaStream_t st);
 int launch_f32_to_bf16(const float *x, uint16_t *y, size_t n, cudaStream_t st);
 int gemm_status(uint32_t *status, bool clear);
+int gemm_reserve_sms(int n);
 // role, CTA, block and thread of the GEMM wait that last gave up
 int gemm_timeout_info(uint32_t out[4]);
 // device addresses of the three status words (GEMV and generic kernels,

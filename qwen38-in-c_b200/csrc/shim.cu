@@ -1036,6 +1036,8 @@ Q35_API int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m
     return launch_gemm_fp8(w, xh, ts, m, Y, st);
 }
 
+Q35_API int q35cu_gemm_reserve_sms(int n) { return gemm_reserve_sms(n); }
+
 Q35_API int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream)
 {
     if (!x || !y) return set_error(Q35CU_ERR_ARG, "f32_to_bf16: NULL");

@@ -49,6 +49,15 @@ class PrefillLayers:
         self.slabs = (4 if st.world > 1 else 1) if slabs is None else slabs
         assert m % self.slabs == 0
         self.comm = torch.cuda.Stream(device=st.dev) if st.world > 1 else None
+        # Under TP the collectives run beside the GEMMs, which are persistent
+        # (one CTA per SM): a GEMM CTA whose SM a collective holds starts late
+        # and holds up its tiles.  The literal scheme, whose all-gathers keep
+        # NCCL busy through most of a layer, leaves NCCL 32 SMs (measured at
+        # TP 2, M = 8192: 347 -> 294 ms per pass); the paired scheme's two
+        # all-reduces per layer cost less than 32 SMs of GEMM (262 ms with
+        # none reserved, 278 with 32).  Q35_PREFILL_RESERVE_SMS overrides.
+        default = "32" if scheme == "literal" else "0"
+        self.reserve = int(__import__("os").environ.get("Q35_PREFILL_RESERVE_SMS", default)) if st.world > 1 else 0
         self.dn = next(L for L in st.layers if L.kind == "dn")
         self.gqa = next(L for L in st.layers if L.kind == "gqa")
         dev = st.dev
@@ -70,6 +79,15 @@ class PrefillLayers:
         self.gu_g = {n: torch.empty((self.world * m * g_n,), **f32) for n in self.gu} if literal else {}
         # stands in for the local heads' attention output
         self.attn = torch.randn((m, self.gqa.attn_out.window[3]), device=dev, generator=g)
+
+    def layer_reserved(self, L, stream=None, keep=None) -> None:
+        """layer() with this scheme's SM reservation in force for its GEMMs."""
+        lib = q35cu.load()
+        q35cu.check(lib.q35cu_gemm_reserve_sms(self.reserve))
+        try:
+            self.layer(L, stream, keep)
+        finally:
+            q35cu.check(lib.q35cu_gemm_reserve_sms(0))
 
     def bf16(self, src, stream=None):
         """bf16(src) into the shared conversion buffer, as [rows, cols]."""

@@ -80,6 +80,7 @@ _SIGS = [
     ("q35cu_gemm_fp8", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8_f32_noalloc", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
     ("q35cu_f32_to_bf16", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
+    ("q35cu_gemm_reserve_sms", C.c_int, [C.c_int]),
     ("q35cu_swiglu", C.c_int, [_vp, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemv_bf16", C.c_int, [_vp, _vp, _vp, _vp]),
     ("q35cu_shard_window", C.c_int, [_u32, _u32, C.c_int, C.c_int, C.c_int, C.POINTER(_u32),

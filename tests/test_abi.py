@@ -116,3 +116,14 @@ def test_no_device_is_reported_not_crashed(lib):
     rc = lib.q35cu_weight_upload_fp8(W.ctypes.data_as(C.POINTER(C.c_uint8)), sc.ctypes.data_as(C.POINTER(C.c_uint16)),
                                      128, 128, C.byref(out))
     assert rc == q35cu.ERR_NODEV
+
+
+def test_gemm_reserve_sms_argument(lib):
+    """q35cu_gemm_reserve_sms is host state only: a count of SMs the
+    persistent GEMM leaves free; a negative count is refused."""
+    import q35cu
+
+    lib.q35cu_clear_error()
+    assert lib.q35cu_gemm_reserve_sms(-1) == q35cu.ERR_ARG
+    assert lib.q35cu_gemm_reserve_sms(16) == q35cu.OK
+    assert lib.q35cu_gemm_reserve_sms(0) == q35cu.OK

@@ -517,7 +517,9 @@ def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
     return {"m": m, "flops": tot_f, "ms": round(tot_t * 1e3, 3), "TFLOPs": round(ach, 1),
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": bf16_peak, "unit": "TFLOP/s",
                          "frac": round(ach / bf16_peak, 4),
-                         "kernel": "gemm_prep_kernel + gemm_fp8_tc_kernel (one q35cu_gemm_fp8 call, L2 flushed before each)",
+                         "kernel": ("gemm_prep_kernel + gemm_fp8_tc_kernel (f16 operands)" if os.environ.get("Q35CU_GEMM_F16")
+                                    else "gemm_prep_e4m3_kernel + gemm_e4m3_tc_kernel (e4m3 operands)")
+                         + " -- one q35cu_gemm_fp8 call, L2 flushed before each",
                          "peak_source": "measured bf16_tflops (burst, MEASURED_PEAKS.json)"},
             "by_projection": per}
 

@@ -75,6 +75,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include <atomic>
 
@@ -236,12 +237,33 @@ __device__ __forceinline__ bool try_wait(uint64_t *b, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (up to ns) until it completes instead of returning at once, so
+// waiting warps do not take issue slots from the working ones
+__device__ __forceinline__ bool try_wait_sleep(uint64_t *b, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(sa(b)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+constexpr uint32_t kSuspendNs = 20000;  // per try: the abort flag and the deadline are checked between tries
+
 __device__ __forceinline__ uint64_t now_ns()
 {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+
+// Programmatic dependent launch: a GEMM is launched right after the kernel
+// that prepares its activations and may start before that kernel ends; only
+// the reads of the prepared activations (and their scales) wait for it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // The slow path of a wait (the phase was not complete at the first poll).
 // abort == nullptr: a wind-down wait, which ignores the CTA's abort flag.
@@ -250,11 +272,9 @@ __device__ __noinline__ bool bar_wait_slow(uint64_t *b, uint32_t parity, volatil
 {
     const uint64_t t0 = now_ns();
     for (uint32_t i = 1; i < kWaitIters; ++i) {
-        if (try_wait(b, parity)) return true;
-        if ((i & 31) == 0) {
-            if (abort && *abort) return false;  // another role gave up: stop without a record of our own
-            if (now_ns() - t0 > kWaitNs) break;
-        }
+        if (try_wait_sleep(b, parity, kSuspendNs)) return true;
+        if (abort && *abort) return false;  // another role gave up: stop without a record of our own
+        if (now_ns() - t0 > kWaitNs) break;
     }
     if (abort) *abort = 1;
     if (atomicCAS(&g_gemm_status, 0u, (uint32_t)Q35CU_ERR_TIMEOUT) == 0u) {
@@ -364,15 +384,22 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
         : "r"(taddr));
 }
 
-// ACC[i] (+)= s * P[i] for 16 columns; the first block starts the accumulator
+// ACC[i] (+)= s * P[i] for 16 columns; the first block starts the accumulator.
+// Packed fma.rn.f32x2 (two independent fp32 FMAs, each rounded as fmaf):
+// the promotion is most of the epilogue's issued instructions.  The first
+// block adds to zero, which leaves the rounded product s * P[i] unchanged.
 __device__ __forceinline__ void promote16(float *acc, const uint32_t (&p)[16], float s, bool first)
 {
-    if (first) {
+    uint64_t ss;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(s));
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = s * __uint_as_float(p[i]);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = fmaf(s, __uint_as_float(p[i]), acc[i]);
+    for (int i = 0; i < 8; ++i) {
+        uint64_t a, pv;
+        const float a0 = first ? 0.f : acc[2 * i], a1 = first ? 0.f : acc[2 * i + 1];
+        asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(pv) : "r"(p[2 * i]), "r"(p[2 * i + 1]));
+        asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(ss), "l"(pv));
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[2 * i]), "=f"(acc[2 * i + 1]) : "l"(a));
     }
 }
 
@@ -449,6 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // so the .sync.aligned TMEM instructions always see a converged warp.
     if (warp == kWarpX) {
         // ---------------- activation producer (whole warp) -----------------
+        pdl_wait();  // the prepared activations and scales are complete and visible
         uint32_t g = 0, tile, kb0, kb1;
         bool ok = true;
         for (SegWalk<kSK> walk(a); ok && walk.next(tile, kb0, kb1);) {
@@ -755,6 +783,7 @@ template <bool F32>
 __global__ void __launch_bounds__(kPrepThreads) gemm_prep_kernel(const void *X, uint32_t K, uint16_t *Xh,
                                                                  float *tscale)
 {
+    pdl_trigger();  // the GEMM after this kernel may start streaming weights
     __shared__ float red[kPrepThreads / 32];
     const size_t row = blockIdx.x;
     const uint32_t k4 = K / 4;  // K % 16 == 0
@@ -796,6 +825,7 @@ __global__ void __launch_bounds__(kPrepThreads) gemm_prep_kernel(const void *X, 
 __global__ void __launch_bounds__(kPrepThreads) gemm_prep_split_kernel(const float *X, uint32_t K, uint16_t *Xh,
                                                                        float *tscale)
 {
+    pdl_trigger();  // the GEMM after this kernel may start streaming weights
     __shared__ float red[kPrepThreads / 32];
     const size_t row = blockIdx.x;
     const uint32_t k4 = K / 4;
@@ -929,6 +959,27 @@ int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *
 
 namespace {
 
+// launch a GEMM kernel as the programmatic dependent of the preparation
+// kernel just issued on st
+template <typename Kern>
+int launch_after_prep(Kern k, uint32_t grid, uint32_t threads, size_t smem, cudaStream_t st,
+                      const CUtensorMap &mx, const CUtensorMap &mw, const GemmArgs &a)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q35CU_CUDA(cudaLaunchKernelEx(&cfg, k, mx, mw, a));
+    count_launch();
+    return Q35CU_OK;
+}
+
 // Stream-K scratch, one per device: counters (kSkCntBytes) then the cut
 // tiles' partial accumulators.  Grown (never shrunk or freed: CUDA graphs
 // may hold its address) when a launch needs more, except under stream
@@ -1016,10 +1067,7 @@ int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscal
     }
     uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
     plan_stream_k<BN>(a, (uint32_t)sms, st, &grid);
-    gemm_fp8_tc_kernel<BN><<<grid, kThreads, smem, st>>>(mx, mw, a);
-    count_launch();
-    Q35CU_CUDA(cudaGetLastError());
-    return Q35CU_OK;
+    return launch_after_prep(gemm_fp8_tc_kernel<BN>, grid, kThreads, smem, st, mx, mw, a);
 }
 
 }  // namespace
@@ -1037,6 +1085,386 @@ int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tsca
     if (m <= 64) return launch_gemm_bn<64>(w, Xh, tscale, m, Y, st, pair);
     if (m <= 128) return launch_gemm_bn<128>(w, Xh, tscale, m, Y, st, pair);
     return launch_gemm_bn<kBN>(w, Xh, tscale, m, Y, st, pair);
+}
+
+// ---------------------------------------------------------------------------
+// Prefill GEMM on fp8 operands: tcgen05.mma kind::mxf8f6f4.block_scale,
+// e4m3 x e4m3 with UE8M0 scale factors.
+//
+// The weight tile goes to the tensor cores as the TMA lands it (e4m3, 128
+// rows x 128 bytes, 128B swizzle): no conversion, no TMEM operand.  Each
+// bf16-valued activation row is carried by two e4m3 terms: with 2^-e
+// putting the row's largest magnitude in [2^7, 2^8),
+//     x 2^-e = t0 + t1 / 16,  t0 = e4m3(x 2^-e),  t1 = e4m3(16 (x 2^-e - t0)),
+// exact for every element of magnitude 2^-6 or more after scaling, so for
+// every element down to 2^-13 of the row's largest (below that the error is
+// at most 2^-21 of it: half of e4m3's 2^-9 subnormal step in t1, over 16);
+// e4m3 keeps 4 significant bits, a bf16 value 8.  The prepared activations
+// hold two planes, t0 [m, K] then t1 [m, K].
+//
+// Each 32-column step of a block is two block-scaled MMAs on the same
+// weight slice: one with the t0 tile and B scale factor 2^0, one with the
+// t1 tile and scale factor 2^-4 (A's factor is 2^0).  The tensor cores thus
+// accumulate W (t0 + t1 / 16) in one fp32 column per token; the scale
+// factors are constants, written once into TMEM (every byte of their
+// columns, so no layout detail of the factors matters).  The epilogue is the
+// f16 kernel's: ACC += s[n/128, kb] * P per 128-column block, Y = ACC * 2^e.
+// Against that kernel: no converter warps and no f16 weight in TMEM, the
+// same tensor-core time per token (8 fp8 MMAs of K = 32 per block instead of
+// 8 f16 MMAs of K = 16) and the same shared-memory bytes per token.
+//
+// Roles (480 threads), tile 128 weight rows x 192 tokens:
+//   warp 0      TMA producer: the t0 and t1 tiles [192 x 128 B each] and the
+//               weight tile [128 x 128 B] of a block into one stage, 3 stages;
+//   warps 1, 2  lane 0 issues the block's 8 MMAs into TMEM P[g % 2]
+//               (192 columns), warp 1 the even blocks, warp 2 the odd ones,
+//               and commits to the stage's empty[] and P's tfull[];
+//   warps 3-14  epilogue: warp w owns TMEM lanes 32*(w%4).. (one weight row
+//               per thread) and 64 of the 192 token columns.
+// Waits, abort flag and wind-down as in the f16 kernel: the producer drains
+// its copies on TMA-only barriers, each MMA warp waits on its own last
+// commit (fin[]), then the CTA frees TMEM.
+// ---------------------------------------------------------------------------
+namespace {
+
+namespace e4 {
+constexpr int kBN = 192;                       // tokens per tile (MMA N)
+constexpr int kS = 3;                          // stages
+constexpr int kD = 2;                          // TMEM accumulators
+constexpr uint32_t kXTile = kBN * kBK;         // one term plane's tile, 24 KB
+constexpr uint32_t kStage = 2 * kXTile + kWTile;  // t0, t1, weights: 64 KB
+constexpr int kWarpMmaA = 1, kWarpMmaB = 2, kWarpEpi0 = 3, kEpiWarps = 12;
+constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+constexpr uint32_t kBars = kS * kStage;
+// TMEM columns: P[0..D) then the scale factors (A reads 4 columns for
+// M = 128, B 8 for N <= 256), each region 8 columns filled, 32-aligned
+constexpr uint32_t kSfA = kD * kBN, kSfB0 = kSfA + 32, kSfB1 = kSfB0 + 32;
+constexpr uint32_t kSfCols = 72;
+constexpr uint32_t kUe8m0One = 0x7F7F7F7Fu, kUe8m0Sixteenth = 0x7B7B7B7Bu;  // 2^0, 2^-4 in every byte
+// full, empty [S]; tfull, tempty [D]; fin [2]; abort flag; TMEM address
+static_assert((2 * kS + 2 * kD + 2) * 8 + 8 <= 256, "barriers fit their 256 bytes");
+constexpr uint32_t kSmem = kBars + 256;
+static_assert(kSfA + kSfCols <= kTmemCols, "TMEM budget");
+static_assert(kStage % 1024 == 0 && kXTile % 1024 == 0, "swizzle atoms need 1024-byte alignment");
+}  // namespace e4
+
+// D[tmem] (+)= (A * sfa)[smem descriptor] * (B * sfb)[smem descriptor], e4m3 x e4m3 -> f32
+__device__ __forceinline__ void mma_mx_e4m3(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc_, uint32_t sfa,
+                                            uint32_t sfb, uint32_t acc, uint32_t leader)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %6, 0;\n\tsetp.ne.b32 e, %7, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_), "r"(sfa), "r"(sfb), "r"(acc), "r"(leader)
+        : "memory");
+}
+
+// Block-scaled instruction descriptor: B scale-factor byte 0 (bits 4-5), A
+// and B e4m3 (bits 7-9, 10-12 = 0), both K-major, N (bits 17-22 = N/8),
+// scale factors UE8M0 (bit 23), M = 128 (bits 24-28 = M/16), A
+// scale-factor byte 0 (bits 29-30), K = 32 (bit 31 = 0).  D is fp32.
+constexpr uint32_t kIdescMx = ((uint32_t)(e4::kBN >> 3) << 17) | (1u << 23) | ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, uint32_t v)
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(e4::kThreads, 1)
+    gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                        const __grid_constant__ GemmArgs a)
+{
+    constexpr uint32_t kFull = 0xffffffffu;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // block g: stage g % S (full: TMA bytes landed -> MMA; empty: its MMAs
+    // completed -> producer), accumulator g % D (tfull: MMAs completed ->
+    // epilogue; tempty: drained by the epilogue warps -> MMA)
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + e4::kBars);
+    uint64_t *empty = full + e4::kS;
+    uint64_t *tfull = empty + e4::kS;
+    uint64_t *tempty = tfull + e4::kD;
+    uint64_t *fin = tempty + e4::kD;
+    volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(fin + 2);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 2) + 1;
+
+    const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const uint32_t nkb = a.kblocks;
+    const uint32_t leader = lane == 0;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (t == 32) {
+        for (int i = 0; i < e4::kS; ++i) {
+            bar_init(&full[i], 1);
+            bar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < e4::kD; ++i) {
+            bar_init(&tfull[i], 1);
+            bar_init(&tempty[i], e4::kEpiWarps);
+        }
+        bar_init(&fin[0], 1);
+        bar_init(&fin[1], 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    // the constant scale factors, every byte of their columns, all 128 lanes
+    if (warp >= e4::kWarpEpi0 && warp < e4::kWarpEpi0 + 4) {
+        const uint32_t lanes = tmem + (((warp & 3) * 32) << 16);
+        tmem_st8(lanes + e4::kSfA, e4::kUe8m0One);
+        tmem_st8(lanes + e4::kSfB0, e4::kUe8m0One);
+        tmem_st8(lanes + e4::kSfB1, e4::kUe8m0Sixteenth);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+
+    if (warp == 0) {
+        // ---------------- producer (whole warp) ------------------------------
+        pdl_wait();  // the prepared activations and scales are complete and visible
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
+            const int m0 = (int)((tile % a.mtiles) * e4::kBN);
+            const int n0 = (int)((tile / a.mtiles) * kBM);
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                const int s = g % e4::kS;
+                if (g >= (uint32_t)e4::kS)
+                    ok = __all_sync(kFull, bar_wait(&empty[s], ((g / e4::kS) - 1) & 1, abort, kRoleX, g));
+                if (!ok) break;
+                uint8_t *stage = sm + s * e4::kStage;
+                bar_expect(&full[s], e4::kStage, leader);
+                tma_2d(stage, &map_x, (int)(kb * kBK), m0, &full[s], leader);                          // t0
+                tma_2d(stage + e4::kXTile, &map_x, (int)(kb * kBK), (int)a.m + m0, &full[s], leader);  // t1
+                tma_2d(stage + 2 * e4::kXTile, &map_w, (int)(kb * kBK), n0, &full[s], leader);
+            }
+        }
+        drain(full, e4::kS, g);
+    } else if (warp == e4::kWarpMmaA || warp == e4::kWarpMmaB) {
+        // ---------------- MMA issuers (whole warp, lane 0 issues) -----------
+        const uint32_t parity = warp == e4::kWarpMmaA ? 0u : 1u;
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                if ((g & 1) != parity) continue;
+                const int s = g % e4::kS, j = g % e4::kD;
+                ok = __all_sync(kFull, bar_wait(&full[s], (g / e4::kS) & 1, abort, kRoleMma, g));
+                if (ok && g >= (uint32_t)e4::kD)
+                    ok = __all_sync(kFull, bar_wait(&tempty[j], ((g / e4::kD) - 1) & 1, abort, kRoleMma, g));
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t x0 = sa(sm + s * e4::kStage), x1 = x0 + e4::kXTile, wb = x0 + 2 * e4::kXTile;
+                const uint32_t d = tmem + j * e4::kBN;
+#pragma unroll
+                for (int ks = 0; ks < kBK / 32; ++ks) {
+                    const uint64_t wd = sw128_desc(wb + ks * 32);
+                    mma_mx_e4m3(d, wd, sw128_desc(x0 + ks * 32), kIdescMx, tmem + e4::kSfA, tmem + e4::kSfB0, ks > 0,
+                                leader);
+                    mma_mx_e4m3(d, wd, sw128_desc(x1 + ks * 32), kIdescMx, tmem + e4::kSfA, tmem + e4::kSfB1, 1,
+                                leader);
+                }
+                mma_commit(&empty[s], leader);
+                mma_commit(&tfull[j], leader);
+            }
+        }
+        mma_commit(&fin[parity], leader);
+        __syncwarp();
+        bar_wait(&fin[parity], 0, nullptr, kRoleDrain, g);
+    } else {
+        // ---------------- epilogue ----------------------------------------
+        const uint32_t quad = warp & 3;                  // TMEM lanes this warp may touch
+        const uint32_t grp = (warp - e4::kWarpEpi0) >> 2;  // token columns 64*grp ..
+        const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * 64;
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
+            const uint32_t rb = tile / a.mtiles;
+            const uint32_t n = rb * kBM + quad * 32 + lane;                   // weight row
+            const uint32_t tok0 = (tile % a.mtiles) * e4::kBN + grp * 64;     // first token
+            const float *srow = a.S + (size_t)rb * nkb;
+            float acc[64];
+            float sc = __ldg(srow);
+            for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
+                const int j = g % e4::kD;
+                const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
+                ok = __all_sync(kFull, bar_wait(&tfull[j], (g / e4::kD) & 1, abort, kRoleEpi, g));
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t p[16];
+                    tmem_ld16(tbase + j * e4::kBN + c * 16, p);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    promote16(acc + 16 * c, p, sc, kb == 0);
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(&tempty[j]);  // P[j] is free for block g + D
+                sc = sc_next;
+            }
+            if (ok && n < a.N) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const uint32_t tok = tok0 + i;
+                    if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                }
+            }
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// four floats -> four e4m3 bytes (byte 0 = a), nearest even, saturating
+__device__ __forceinline__ uint32_t to_e4m3x4(float a, float b, float c, float d)
+{
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+    return lo | (hi << 16);
+}
+
+// Activation terms: one CTA per token row.  xb = bf16(x) (nearest even);
+// e = floor(log2(max |xb|)) - 7 (kept in [-126, 127]; 0 for a row of zeros
+// or one whose largest magnitude is not finite), so max |xb 2^-e| < 2^8 <
+// 448, the e4m3 limit.  Row r of plane 0 (Xq[r]): t0 = e4m3(xb 2^-e); row r
+// of plane 1 (Xq[m + r]): t1 = e4m3(16 (xb 2^-e - t0)) (the difference and
+// the factor are exact in fp32).  A non-finite element becomes the e4m3 NaN
+// code (0x7F) in t0 and 0 in t1, so its token's outputs are NaN (an
+// infinity included).
+template <bool F32>
+__global__ void __launch_bounds__(kPrepThreads) gemm_prep_e4m3_kernel(const void *X, uint32_t K, uint32_t m,
+                                                                      uint8_t *Xq, float *tscale)
+{
+    pdl_trigger();  // the GEMM after this kernel may start streaming weights
+    __shared__ float red[kPrepThreads / 32];
+    const size_t row = blockIdx.x;
+    const uint32_t k4 = K / 4;  // K % 16 == 0
+    const size_t base4 = row * k4;
+    float mx = 0.f;
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = prep_load<F32>(X, base4 + i);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < kPrepThreads / 32; ++i) mx = fmaxf(mx, red[i]);
+    const int eb = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+    int e = 0;
+    if (eb == 0 && mx > 0.f) e = -126;  // subnormal maximum
+    else if (eb > 0 && eb < 255) e = max(eb - 127 - 7, -126);
+    const float down = __uint_as_float((uint32_t)(127 - e) << 23);
+    uint32_t *t0 = reinterpret_cast<uint32_t *>(Xq + row * K);
+    uint32_t *t1 = reinterpret_cast<uint32_t *>(Xq + ((size_t)m + row) * K);
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = prep_load<F32>(X, base4 + i);
+        const float xs[4] = {v.x * down, v.y * down, v.z * down, v.w * down};
+        const uint32_t q0 = to_e4m3x4(xs[0], xs[1], xs[2], xs[3]);
+        uint32_t h01, h23;
+        e4m3x4_to_f16x4(q0, h01, h23);
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&h01));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&h23));
+        const float back[4] = {f01.x, f01.y, f23.x, f23.y};
+        float r[4];
+        uint32_t nan_mask = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const bool fin_ = fabsf(xs[j]) <= 3.402823466e38f;
+            r[j] = fin_ ? (xs[j] - back[j]) * 16.f : 0.f;
+            if (!fin_) nan_mask |= 0xFFu << (8 * j);
+        }
+        t0[i] = (q0 & ~nan_mask) | (0x7F7F7F7Fu & nan_mask);
+        t1[i] = to_e4m3x4(r[0], r[1], r[2], r[3]);
+    }
+    if (threadIdx.x == 0) tscale[row] = __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
+int launch_gemm_e4m3(const q35cu_weight *w, const uint8_t *Xq, const float *tscale, uint32_t m, float *Y,
+                     cudaStream_t st)
+{
+    const uint32_t N = w->rows, K = w->cols;
+    const uint64_t mtiles = (m + e4::kBN - 1) / e4::kBN, ntiles = mtiles * ((N + kBM - 1) / kBM);
+    if (ntiles > 0x7FFFFFFFu || (uint64_t)m * 2 > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: shape too large");
+    CUtensorMap mx, mw;
+    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, Xq, K, (uint64_t)m * 2, K, 128, e4::kBN);
+    if (rc) return rc;
+    rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
+    if (rc) return rc;
+    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, 0u,
+               0u, 0u, nullptr, nullptr};
+    static bool configured[64] = {};
+    int dev = 0, sms = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    rc = sm_count_of(dev, &sms);
+    if (rc) return rc;
+    const int reserve = g_gemm_reserved_sms.load();
+    if (reserve > 0 && reserve < sms) sms -= reserve;
+    const size_t smem = e4::kSmem + 1024;
+    if (!configured[dev]) {
+        Q35CU_CUDA(cudaFuncSetAttribute(gemm_e4m3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured[dev] = true;
+    }
+    const uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
+    return launch_after_prep(gemm_e4m3_tc_kernel, grid, e4::kThreads, smem, st, mx, mw, a);
+}
+
+// the fp8-operand kernel unless Q35CU_GEMM_F16 asks for the f16 one
+bool use_e4m3() { return getenv("Q35CU_GEMM_F16") == nullptr; }
+
+// preparation into acts (2 m K bytes) and ts (m scales), then the GEMM
+int gemm_bf16_into(const q35cu_weight *w, const void *X, bool f32, uint32_t m, float *Y, void *acts, float *ts,
+                   cudaStream_t st)
+{
+    const uint32_t K = w->cols;
+    if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
+    if ((uintptr_t)X % 16 || (uintptr_t)acts % 16 || (uintptr_t)ts % 4 || (uintptr_t)w->d_w % 16)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned activations, weight or workspace");
+    if (!use_e4m3()) {
+        uint16_t *xh = static_cast<uint16_t *>(acts);
+        int rc = launch_gemm_prep(X, f32, m, K, xh, ts, st);
+        if (rc) return rc;
+        return launch_gemm_fp8(w, xh, ts, m, Y, st);
+    }
+    uint8_t *xq = static_cast<uint8_t *>(acts);
+    if (f32)
+        gemm_prep_e4m3_kernel<true><<<m, kPrepThreads, 0, st>>>(X, K, m, xq, ts);
+    else
+        gemm_prep_e4m3_kernel<false><<<m, kPrepThreads, 0, st>>>(X, K, m, xq, ts);
+    count_launch();
+    Q35CU_CUDA(cudaGetLastError());
+    return launch_gemm_e4m3(w, xq, ts, m, Y, st);
+}
+
+}  // namespace
+
+// Prefill GEMM on bf16-valued activations (X bf16 bits, or fp32 rounded to
+// bf16 when f32): prepares the activations into `workspace`
+// (gemm_workspace_bytes(m, K): 2 m K bytes of prepared values, then m
+// scales) and runs the tensor-core GEMM.
+int launch_gemm_bf16(const q35cu_weight *w, const void *X, bool f32, uint32_t m, float *Y, void *workspace,
+                     cudaStream_t st)
+{
+    if (!m) return Q35CU_OK;
+    const size_t need = gemm_workspace_bytes(m, w->cols);
+    float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + need - (size_t)m * 4);
+    return gemm_bf16_into(w, X, f32, m, Y, workspace, ts, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -1106,9 +1534,7 @@ int gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m, floa
     float *ts = nullptr;
     int rc = noalloc_scratch(&xh, &ts);
     if (rc) return rc;
-    rc = launch_gemm_prep(X, true, m, w->cols, xh, ts, st);
-    if (rc) return rc;
-    return launch_gemm_fp8(w, xh, ts, m, Y, st);
+    return gemm_bf16_into(w, X, true, m, Y, xh, ts, st);
 }
 
 int gemm_reserve_sms(int n)

@@ -89,6 +89,12 @@ int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *
                      cudaStream_t st);
 int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tscale, uint32_t m, float *Y,
                     cudaStream_t st, bool pair = false);
+// the prefill GEMM on bf16-valued activations (X bf16 bits, or fp32 rounded
+// to bf16 when f32): activation preparation into workspace (at least
+// gemm_workspace_bytes(m, K) bytes, 16-byte aligned) + the tensor-core GEMM
+// (fp8 operands by default; Q35CU_GEMM_F16 selects the f16-operand kernel)
+int launch_gemm_bf16(const q35cu_weight *w, const void *X, bool f32, uint32_t m, float *Y, void *workspace,
+                     cudaStream_t st);
 // multi-token decode on the tensor cores, fp32 activations split hi/lo
 size_t gemm_exact_workspace_bytes(uint32_t m, uint32_t K);
 int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,

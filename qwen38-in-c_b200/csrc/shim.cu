@@ -1028,12 +1028,7 @@ Q35_API int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m
     const size_t need = gemm_workspace_bytes(m, w->cols);
     if (!workspace || workspace_bytes < need)
         return set_error(Q35CU_ERR_ARG, "gemm_fp8: workspace of %zu bytes, %zu needed", workspace_bytes, need);
-    uint16_t *xh = static_cast<uint16_t *>(workspace);
-    float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + need - (size_t)m * 4);
-    cudaStream_t st = pick(stream);
-    int rc = launch_gemm_prep(Xb, false, m, w->cols, xh, ts, st);
-    if (rc) return rc;
-    return launch_gemm_fp8(w, xh, ts, m, Y, st);
+    return launch_gemm_bf16(w, Xb, false, m, Y, workspace, pick(stream));
 }
 
 Q35_API int q35cu_gemm_reserve_sms(int n) { return gemm_reserve_sms(n); }
@@ -1371,13 +1366,7 @@ Q35_API void q35_mm_fp8_batch(const uint8_t *W, const uint16_t *scale_bf16, uint
     }
     if (!rc && tc)
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {
-            DevState *d = dev_state();
-            uint16_t *xh = static_cast<uint16_t *>(d->d_xbf);
-            float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(d->d_xbf) + gemm_workspace_bytes(n, cols) -
-                                                  (size_t)n * 4);
-            int r = launch_gemm_prep(dx, true, n, cols, xh, ts, st);
-            if (r) return r;
-            return launch_gemm_fp8(w, xh, ts, n, dy, st);
+            return launch_gemm_bf16(w, dx, true, n, dy, dev_state()->d_xbf, st);
         });
     else if (!rc && tc_exact)
         rc = host_call(X, (size_t)n * cols * 4, Y, nout * 4, [&](const float *dx, float *dy, cudaStream_t st) {

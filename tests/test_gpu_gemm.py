@@ -2,10 +2,14 @@
 
 Contract (prefill): activations rounded to bf16, relative L2 error of Y
 against the reference's own matmul on the same bf16-valued X <= 5e-3.
-The kernel converts e4m3 -> bf16 exactly and promotes each 128-column
-block's fp32 partial with its scale, so the error is fp32 accumulation
-order only; the tests also hold it to a tight sanity bound (1e-5) to catch
-layout or indexing mistakes that a loose bound would hide.
+Two kernels serve it.  The default multiplies e4m3 weights by each
+activation carried as two e4m3 terms (block-scaled MMAs); the other
+(Q35CU_GEMM_F16) converts the weights to f16 and carries the activations
+exactly in f16.  Both promote each 128-column block's fp32 partial with its
+scale, so the error is fp32 accumulation order plus, for the terms, at most
+2^-21 of a row's largest magnitude on its smallest elements; the tests
+also hold both to a tight sanity bound (1e-5) to catch layout or indexing
+mistakes that a loose bound would hide.
 """
 from __future__ import annotations
 
@@ -98,6 +102,106 @@ def test_gemm_deterministic(gpu, orc):
         assert torch.equal(Y1, Y2)
     finally:
         w.free()
+
+
+def _e4m3_table():
+    """float value of every e4m3 code (0x7F / 0xFF: NaN)"""
+    v = np.empty(256, np.float64)
+    for c in range(256):
+        sgn = -1.0 if c & 0x80 else 1.0
+        e, mt = (c >> 3) & 0xF, c & 7
+        v[c] = sgn * (mt / 8.0 * 2.0 ** -6 if e == 0 else (1 + mt / 8.0) * 2.0 ** (e - 7))
+    v[0x7F] = v[0xFF] = np.nan
+    return v
+
+
+def test_e4m3_activation_terms_carry_bf16(gpu, orc):
+    """The fp8-operand GEMM's prepared activations (left in the caller's
+    workspace): per token a power of two 2^e and two e4m3 rows t0, t1 (two
+    planes [m, K]) with
+    x = (t0 + t1 / 16) 2^e exactly for every element down to 2^-13 of the
+    row's largest, and within 2^-21 of it below; the largest lies in
+    [2^7, 2^8) after scaling.  Rows span magnitudes over 2^40."""
+    import torch
+
+    m, k = 130, 512
+    rng = np.random.default_rng(7)
+    X = orc.synth_act(77, (m, k)) * np.exp2(rng.integers(-20, 20, (m, 1))).astype(np.float32)
+    X[5] = 0.0
+    X[6, ::3] *= 2.0 ** -30  # tiny elements beside normal ones
+    X = oracle.bf16_round(X)
+    w = q35cu.Weight.synth_fp8(78, 256, k)
+    try:
+        Xb = torch.from_numpy(X).to(torch.bfloat16).cuda()
+        Y = torch.empty((m, 256), device="cuda")
+        work = torch.zeros(q35cu.gemm_workspace_bytes(m, k), dtype=torch.uint8, device="cuda")
+        q35cu.gemm(w, Xb.view(torch.int16), Y, work)
+        torch.cuda.synchronize()
+        q35cu.check_device_status()
+        raw = work.cpu().numpy()
+        terms = raw[:2 * m * k].reshape(2, m, k)  # plane 0: t0 [m, k], plane 1: t1 [m, k]
+        ts = raw[len(raw) - 4 * m:].view(np.float32).astype(np.float64)
+        tab = _e4m3_table()
+        rec = (tab[terms[0]] + tab[terms[1]] / 16.0) * ts[:, None]
+        x64 = X.astype(np.float64)
+        mx = np.abs(x64).max(axis=1, keepdims=True)
+        assert np.isfinite(rec).all()
+        err = np.abs(rec - x64)
+        big = np.abs(x64) >= mx * 2.0 ** -13
+        assert (err[big] == 0).all()
+        assert (err <= mx * 2.0 ** -21).all()
+        live = mx[:, 0] > 0
+        assert ((mx[live, 0] / ts[live] >= 128) & (mx[live, 0] / ts[live] < 256)).all()
+        assert (rec[5] == 0).all()
+    finally:
+        w.free()
+
+
+@pytest.mark.parametrize("rows,cols,n", [(17408, 5120, 300), (5120, 17408, 256), (300, 512, 130), (256, 144, 128)])
+def test_fp8_and_f16_kernels_agree(gpu, orc, monkeypatch, rows, cols, n):
+    """The fp8-operand kernel (default) and the f16-operand one
+    (Q35CU_GEMM_F16) both meet the tight bound against fp64 on the same
+    bf16 activations."""
+    import torch
+
+    w = q35cu.Weight.synth_fp8(9000 + rows + cols, rows, cols)
+    try:
+        Wh, sch = w.download_fp8()
+        X = _bf16_x(orc, 9100 + n, n, cols)
+        Xb = torch.from_numpy(X).to(torch.bfloat16).cuda()
+        outs = {}
+        for kern in ("fp8", "f16"):
+            if kern == "f16":
+                monkeypatch.setenv("Q35CU_GEMM_F16", "1")
+            Y = torch.full((n, rows), float("nan"), device="cuda")
+            q35cu.gemm(w, Xb.view(torch.int16), Y)
+            torch.cuda.synchronize()
+            q35cu.check_device_status()
+            outs[kern] = Y.cpu().numpy()
+        pick = np.unique(np.concatenate([np.random.default_rng(rows).choice(n, 24, replace=False), [0, n - 1]]))
+        Y64, _ = orc.mm_fp8_f64(Wh, sch, np.ascontiguousarray(X[pick]))
+        for kern, Y in outs.items():
+            assert np.isfinite(Y).all(), kern
+            err = rel_l2(Y[pick], Y64)
+            assert err <= TIGHT, (kern, err)
+    finally:
+        w.free()
+
+
+def test_gemm_nonfinite_activation(gpu, orc, monkeypatch):
+    """A token holding an infinity or a NaN gets non-finite outputs (the fp8
+    kernel: NaN); every other token is unchanged."""
+    W, sc = orc.synth_fp8(95, 256, 256)
+    X = _bf16_x(orc, 96, 140, 256)
+    base = q35cu.mm_fp8_batch(W, sc, X)
+    X2 = X.copy()
+    X2[3, 10] = np.inf
+    X2[7, 0] = np.nan
+    Y = q35cu.mm_fp8_batch(W, sc, X2)
+    assert not np.isfinite(Y[3]).any() and not np.isfinite(Y[7]).any()
+    keep = np.ones(140, bool)
+    keep[[3, 7]] = False
+    assert np.array_equal(Y[keep], base[keep])
 
 
 def test_gemm_nan_code_propagates(gpu, orc, ref):

@@ -152,6 +152,7 @@ struct GemmArgs {
     uint32_t maxseg;      // segment slots per tile in skpart
     float *skpart;        // [G][maxseg][BN][128] (rows fastest)
     uint32_t *skcnt;      // [G] blocks done of a cut tile (zero between launches)
+    uint32_t gm;          // token tiles per raster group (tile_rc); mtiles = one group
 };
 
 // The (tile, first block, end block) segments a CTA walks, in order: whole
@@ -191,6 +192,22 @@ struct SegWalk {
         return true;
     }
 };
+
+// (row block, token tile) of tile index `tile`.  Token tiles are walked in
+// groups of gm: inside a group its token tiles go fastest, then the row
+// blocks, so the tiles running at once share a band of at most gm token
+// tiles -- prepared activations that stay in L2 -- across many weight row
+// blocks.  gm == mtiles is one group: token tile fastest over all of them.
+__device__ __forceinline__ void tile_rc(uint32_t tile, const GemmArgs &a, uint32_t &rb, uint32_t &mt)
+{
+    const uint32_t nrb = a.ntiles / a.mtiles;
+    const uint32_t span = a.gm * nrb;
+    const uint32_t grp = tile / span, in = tile - grp * span;
+    const uint32_t g0 = grp * a.gm;
+    const uint32_t w = a.mtiles - g0 < a.gm ? a.mtiles - g0 : a.gm;  // token tiles of this group
+    rb = in / w;
+    mt = g0 + in % w;
+}
 
 template <int BN>
 struct Smem {  // offsets from the 1024-aligned base (every tile size is a multiple of 1024 B)
@@ -385,9 +402,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
 }
 
 // ACC[i] (+)= s * P[i] for 16 columns; the first block starts the accumulator.
-// Packed fma.rn.f32x2 (two independent fp32 FMAs, each rounded as fmaf):
-// the promotion is most of the epilogue's issued instructions.  The first
-// block adds to zero, which leaves the rounded product s * P[i] unchanged.
+// Packed fma.rn.f32x2 (two independent fp32 FMAs, each rounded as fmaf): in
+// the e4m3 kernel, whose epilogue bounds it, 1079 against 999 TFLOP/s with
+// scalar FMAs (configuration 2, same box); neutral in the f16 kernel.  The
+// first block adds to zero, which leaves the rounded product s * P[i].
 __device__ __forceinline__ void promote16(float *acc, const uint32_t (&p)[16], float s, bool first)
 {
     uint64_t ss;
@@ -480,7 +498,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t g = 0, tile, kb0, kb1;
         bool ok = true;
         for (SegWalk<kSK> walk(a); ok && walk.next(tile, kb0, kb1);) {
-            const int m0 = (int)((tile % a.mtiles) * BN);
+            uint32_t rb_, mt_;
+            tile_rc(tile, a, rb_, mt_);
+            const int m0 = (int)(mt_ * BN);
             for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
                 const int s = g % S;
                 if (g >= (uint32_t)S)
@@ -497,7 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t g = 0, tile, kb0, kb1;
         bool ok = true;
         for (SegWalk<kSK> walk(a); ok && walk.next(tile, kb0, kb1);) {
-            const int n0 = (int)((tile / a.mtiles) * kBM);
+            uint32_t rb_, mt_;
+            tile_rc(tile, a, rb_, mt_);
+            const int n0 = (int)(rb_ * kBM);
             for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
                 const int s = g % WS;
                 if (g >= (uint32_t)WS)
@@ -602,9 +624,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t g = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; tile < a.ntiles && ok; tile += gridDim.x) {
-                const uint32_t rb = tile / a.mtiles;
+                uint32_t rb, mt;
+                tile_rc(tile, a, rb, mt);
                 const uint32_t n = rb * kBM + quad * 32 + lane;               // weight row
-                const uint32_t t0 = (tile % a.mtiles) * BN + grp * 64;        // first token
+                const uint32_t t0 = mt * BN + grp * 64;                       // first token
                 const float *srow = a.S + (size_t)rb * nkb;
                 float acc[64];
                 float sc = __ldg(srow);
@@ -653,10 +676,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // every segment is visited even after an abort: the hand-off of a
             // cut tile needs all 12 warps at its barriers
             for (SegWalk<kSK> walk(a); walk.next(tile, kb0, kb1);) {
-                const uint32_t rb = tile / a.mtiles;
+                uint32_t rb, mt;
+                tile_rc(tile, a, rb, mt);
                 const uint32_t row = quad * 32 + lane;
                 const uint32_t n = rb * kBM + row;                            // weight row
-                const uint32_t t0 = (tile % a.mtiles) * BN + grp * 64;        // first token
+                const uint32_t t0 = mt * BN + grp * 64;                       // first token
                 const float *srow = a.S + (size_t)rb * nkb;
                 float acc[64];
                 float sc = ok ? __ldg(srow + kb0) : 0.f;
@@ -959,6 +983,22 @@ int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *
 
 namespace {
 
+// Token tiles per raster group: the prepared activations of a group (2
+// bytes per value in both kernels) within kGroupBytes, so they stay in L2
+// while the running tiles sweep the weight row blocks.  Q35CU_GEMM_GROUP
+// overrides (0 = one group).
+constexpr uint64_t kGroupBytes = (uint64_t)48 << 20;
+uint32_t raster_group(uint32_t mtiles, uint32_t bn, uint32_t K)
+{
+    if (const char *e = getenv("Q35CU_GEMM_GROUP")) {
+        const long v = strtol(e, nullptr, 10);
+        return v <= 0 || (uint64_t)v >= mtiles ? mtiles : (uint32_t)v;
+    }
+    const uint64_t per = (uint64_t)bn * K * 2;
+    const uint64_t gm = kGroupBytes / per;
+    return gm < 1 ? 1u : (gm >= mtiles ? mtiles : (uint32_t)gm);
+}
+
 // launch a GEMM kernel as the programmatic dependent of the preparation
 // kernel just issued on st
 template <typename Kern>
@@ -1051,7 +1091,8 @@ int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscal
     rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
     if (rc) return rc;
     GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, pair ? 1u : 0u,
-               0u, 0u, nullptr, nullptr};
+               0u, 0u, nullptr, nullptr, 0u};
+    a.gm = raster_group((uint32_t)mtiles, BN, K);
     static bool configured[64] = {};  // per instantiation and device
     int dev = 0, sms = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));
@@ -1133,8 +1174,12 @@ constexpr int kS = 3;                          // stages
 constexpr int kD = 2;                          // TMEM accumulators
 constexpr uint32_t kXTile = kBN * kBK;         // one term plane's tile, 24 KB
 constexpr uint32_t kStage = 2 * kXTile + kWTile;  // t0, t1, weights: 64 KB
-constexpr int kWarpMmaA = 1, kWarpMmaB = 2, kWarpEpi0 = 3, kEpiWarps = 12;
+// token columns per epilogue warp: 64 (12 warps), read 32 at a time; 32
+// (24 warps of fewer registers) measured slower (965 vs 1060 TFLOP/s)
+constexpr int kEpiCols = 64;
+constexpr int kWarpMmaA = 1, kWarpMmaB = 2, kWarpEpi0 = 3, kEpiWarps = 4 * kBN / kEpiCols;
 constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+static_assert(kBN % kEpiCols == 0 && kEpiCols % 32 == 0, "epilogue warps load their columns 32 at a time");
 constexpr uint32_t kBars = kS * kStage;
 // TMEM columns: P[0..D) then the scale factors (A reads 4 columns for
 // M = 128, B 8 for N <= 256), each region 8 columns filled, 32-aligned
@@ -1234,8 +1279,10 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
-            const int m0 = (int)((tile % a.mtiles) * e4::kBN);
-            const int n0 = (int)((tile / a.mtiles) * kBM);
+            uint32_t rb_, mt_;
+            tile_rc(tile, a, rb_, mt_);
+            const int m0 = (int)(mt_ * e4::kBN);
+            const int n0 = (int)(rb_ * kBM);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int s = g % e4::kS;
                 if (g >= (uint32_t)e4::kS)
@@ -1283,16 +1330,17 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
     } else {
         // ---------------- epilogue ----------------------------------------
         const uint32_t quad = warp & 3;                  // TMEM lanes this warp may touch
-        const uint32_t grp = (warp - e4::kWarpEpi0) >> 2;  // token columns 64*grp ..
-        const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * 64;
+        const uint32_t grp = (warp - e4::kWarpEpi0) >> 2;  // token columns kEpiCols*grp ..
+        const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * e4::kEpiCols;
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
-            const uint32_t rb = tile / a.mtiles;
+            uint32_t rb, mt;
+            tile_rc(tile, a, rb, mt);
             const uint32_t n = rb * kBM + quad * 32 + lane;                   // weight row
-            const uint32_t tok0 = (tile % a.mtiles) * e4::kBN + grp * 64;     // first token
+            const uint32_t tok0 = mt * e4::kBN + grp * e4::kEpiCols;                    // first token
             const float *srow = a.S + (size_t)rb * nkb;
-            float acc[64];
+            float acc[e4::kEpiCols];
             float sc = __ldg(srow);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int j = g % e4::kD;
@@ -1301,11 +1349,13 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t p[16];
-                    tmem_ld16(tbase + j * e4::kBN + c * 16, p);
+                for (int c = 0; c < e4::kEpiCols / 32; ++c) {  // two loads in flight per wait
+                    uint32_t p0[16], p1[16];
+                    tmem_ld16(tbase + j * e4::kBN + c * 32, p0);
+                    tmem_ld16(tbase + j * e4::kBN + c * 32 + 16, p1);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    promote16(acc + 16 * c, p, sc, kb == 0);
+                    promote16(acc + 32 * c, p0, sc, kb == 0);
+                    promote16(acc + 32 * c + 16, p1, sc, kb == 0);
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
@@ -1314,7 +1364,7 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
             }
             if (ok && n < a.N) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
+                for (int i = 0; i < e4::kEpiCols; ++i) {
                     const uint32_t tok = tok0 + i;
                     if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
                 }
@@ -1408,7 +1458,8 @@ int launch_gemm_e4m3(const q35cu_weight *w, const uint8_t *Xq, const float *tsca
     rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
     if (rc) return rc;
     GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, 0u,
-               0u, 0u, nullptr, nullptr};
+               0u, 0u, nullptr, nullptr, 0u};
+    a.gm = raster_group((uint32_t)mtiles, e4::kBN, K);
     static bool configured[64] = {};
     int dev = 0, sms = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));

@@ -1169,28 +1169,44 @@ int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tsca
 namespace {
 
 namespace e4 {
-constexpr int kBN = 192;                       // tokens per tile (MMA N)
-constexpr int kS = 3;                          // stages
-constexpr int kD = 2;                          // TMEM accumulators
-constexpr uint32_t kXTile = kBN * kBK;         // one term plane's tile, 24 KB
-constexpr uint32_t kStage = 2 * kXTile + kWTile;  // t0, t1, weights: 64 KB
-// token columns per epilogue warp: 64 (12 warps), read 32 at a time; 32
-// (24 warps of fewer registers) measured slower (965 vs 1060 TFLOP/s)
-constexpr int kEpiCols = 64;
-constexpr int kWarpMmaA = 1, kWarpMmaB = 2, kWarpEpi0 = 3, kEpiWarps = 4 * kBN / kEpiCols;
-constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
-static_assert(kBN % kEpiCols == 0 && kEpiCols % 32 == 0, "epilogue warps load their columns 32 at a time");
-constexpr uint32_t kBars = kS * kStage;
-// TMEM columns: P[0..D) then the scale factors (A reads 4 columns for
-// M = 128, B 8 for N <= 256), each region 8 columns filled, 32-aligned
-constexpr uint32_t kSfA = kD * kBN, kSfB0 = kSfA + 32, kSfB1 = kSfB0 + 32;
-constexpr uint32_t kSfCols = 72;
+// Tile geometry: BN tokens per tile (MMA N), S stages, D TMEM accumulators,
+// EC token columns per epilogue warp (4 * BN / EC epilogue warps); EARLY =
+// an epilogue warp loads all its columns, releases the accumulator to the
+// MMA, then promotes (else it promotes 32 columns at a time and releases
+// after the last).
+template <int BN_, int S_, int D_, int EC_, bool EARLY_>
+struct Cfg {
+    static constexpr int kBN = BN_, kS = S_, kD = D_, kEpiCols = EC_;
+    static constexpr bool kEarly = EARLY_;
+    static constexpr uint32_t kXTile = kBN * kBK;                // one term plane's tile
+    static constexpr uint32_t kStage = 2 * kXTile + kWTile;      // t0, t1, weights
+    static constexpr int kWarpMmaA = 1, kWarpMmaB = 2, kWarpEpi0 = 3, kEpiWarps = 4 * kBN / kEpiCols;
+    static constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+    static constexpr uint32_t kBars = kS * kStage;
+    // TMEM columns: P[0..D) then the scale factors (A reads 4 columns for
+    // M = 128, B one per 32 rows of N), 8 columns filled each
+    static constexpr uint32_t kSfA = kD * kBN, kSfB0 = kSfA + 8, kSfB1 = kSfB0 + 8;
+    static constexpr uint32_t kSmem = kBars + 256;
+    // Block-scaled instruction descriptor: B scale-factor byte 0 (bits 4-5),
+    // A and B e4m3 (bits 7-9, 10-12 = 0), both K-major, N (bits 17-22 =
+    // N/8), scale factors UE8M0 (bit 23), M = 128 (bits 24-28 = M/16), A
+    // scale-factor byte 0 (bits 29-30), K = 32 (bit 31 = 0).  D is fp32.
+    static constexpr uint32_t kIdesc = ((uint32_t)(kBN >> 3) << 17) | (1u << 23) | ((uint32_t)(kBM >> 4) << 24);
+    static_assert(kBN % 16 == 0 && kBN <= 256, "M = 128 MMAs take N = 16..256 in steps of 16");
+    static_assert(kBN % kEpiCols == 0 && kEpiCols % 32 == 0 && (kEarly || kEpiCols % 32 == 0), "epilogue columns");
+    // full, empty [S]; tfull, tempty [D]; fin [2]; abort flag; TMEM address
+    static_assert((2 * kS + 2 * kD + 2) * 8 + 8 <= 256, "barriers fit their 256 bytes");
+    static_assert(kSfB1 + 8 <= kTmemCols, "TMEM budget");
+    static_assert(kStage % 1024 == 0 && kXTile % 1024 == 0, "swizzle atoms need 1024-byte alignment");
+    static_assert(kSmem + 1024 <= 232448, "shared memory");
+};
 constexpr uint32_t kUe8m0One = 0x7F7F7F7Fu, kUe8m0Sixteenth = 0x7B7B7B7Bu;  // 2^0, 2^-4 in every byte
-// full, empty [S]; tfull, tempty [D]; fin [2]; abort flag; TMEM address
-static_assert((2 * kS + 2 * kD + 2) * 8 + 8 <= 256, "barriers fit their 256 bytes");
-constexpr uint32_t kSmem = kBars + 256;
-static_assert(kSfA + kSfCols <= kTmemCols, "TMEM budget");
-static_assert(kStage % 1024 == 0 && kXTile % 1024 == 0, "swizzle atoms need 1024-byte alignment");
+// 192 tokens, 3 stages, 2 accumulators, 12 epilogue warps of 64 columns.
+// Measured slower (configuration-2 projections, same box): 160 tokens with
+// 4 stages, 3 accumulators and 20 early-releasing epilogue warps of 32
+// columns -- 1034 vs 1067 TFLOP/s at M = 2048, 1053 vs 1110 at M = 8192
+// (faster only on gate / up at M = 2048: 1174 vs 1113).
+using Wide = Cfg<192, 3, 2, 64, false>;
 }  // namespace e4
 
 // D[tmem] (+)= (A * sfa)[smem descriptor] * (B * sfb)[smem descriptor], e4m3 x e4m3 -> f32
@@ -1204,11 +1220,6 @@ __device__ __forceinline__ void mma_mx_e4m3(uint32_t d_tmem, uint64_t a, uint64_
         : "memory");
 }
 
-// Block-scaled instruction descriptor: B scale-factor byte 0 (bits 4-5), A
-// and B e4m3 (bits 7-9, 10-12 = 0), both K-major, N (bits 17-22 = N/8),
-// scale factors UE8M0 (bit 23), M = 128 (bits 24-28 = M/16), A
-// scale-factor byte 0 (bits 29-30), K = 32 (bit 31 = 0).  D is fp32.
-constexpr uint32_t kIdescMx = ((uint32_t)(e4::kBN >> 3) << 17) | (1u << 23) | ((uint32_t)(kBM >> 4) << 24);
 
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, uint32_t v)
 {
@@ -1216,7 +1227,8 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, uint32_t v)
                  : "memory");
 }
 
-__global__ void __launch_bounds__(e4::kThreads, 1)
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
     gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                         const __grid_constant__ GemmArgs a)
 {
@@ -1226,11 +1238,11 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
     // block g: stage g % S (full: TMA bytes landed -> MMA; empty: its MMAs
     // completed -> producer), accumulator g % D (tfull: MMAs completed ->
     // epilogue; tempty: drained by the epilogue warps -> MMA)
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + e4::kBars);
-    uint64_t *empty = full + e4::kS;
-    uint64_t *tfull = empty + e4::kS;
-    uint64_t *tempty = tfull + e4::kD;
-    uint64_t *fin = tempty + e4::kD;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + C::kBars);
+    uint64_t *empty = full + C::kS;
+    uint64_t *tfull = empty + C::kS;
+    uint64_t *tempty = tfull + C::kD;
+    uint64_t *fin = tempty + C::kD;
     volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(fin + 2);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 2) + 1;
 
@@ -1244,13 +1256,13 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (t == 32) {
-        for (int i = 0; i < e4::kS; ++i) {
+        for (int i = 0; i < C::kS; ++i) {
             bar_init(&full[i], 1);
             bar_init(&empty[i], 1);
         }
-        for (int i = 0; i < e4::kD; ++i) {
+        for (int i = 0; i < C::kD; ++i) {
             bar_init(&tfull[i], 1);
-            bar_init(&tempty[i], e4::kEpiWarps);
+            bar_init(&tempty[i], C::kEpiWarps);
         }
         bar_init(&fin[0], 1);
         bar_init(&fin[1], 1);
@@ -1262,11 +1274,11 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
     // the constant scale factors, every byte of their columns, all 128 lanes
-    if (warp >= e4::kWarpEpi0 && warp < e4::kWarpEpi0 + 4) {
+    if (warp >= C::kWarpEpi0 && warp < C::kWarpEpi0 + 4) {
         const uint32_t lanes = tmem + (((warp & 3) * 32) << 16);
-        tmem_st8(lanes + e4::kSfA, e4::kUe8m0One);
-        tmem_st8(lanes + e4::kSfB0, e4::kUe8m0One);
-        tmem_st8(lanes + e4::kSfB1, e4::kUe8m0Sixteenth);
+        tmem_st8(lanes + C::kSfA, e4::kUe8m0One);
+        tmem_st8(lanes + C::kSfB0, e4::kUe8m0One);
+        tmem_st8(lanes + C::kSfB1, e4::kUe8m0Sixteenth);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -1281,43 +1293,43 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
         for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
             uint32_t rb_, mt_;
             tile_rc(tile, a, rb_, mt_);
-            const int m0 = (int)(mt_ * e4::kBN);
+            const int m0 = (int)(mt_ * C::kBN);
             const int n0 = (int)(rb_ * kBM);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int s = g % e4::kS;
-                if (g >= (uint32_t)e4::kS)
-                    ok = __all_sync(kFull, bar_wait(&empty[s], ((g / e4::kS) - 1) & 1, abort, kRoleX, g));
+                const int s = g % C::kS;
+                if (g >= (uint32_t)C::kS)
+                    ok = __all_sync(kFull, bar_wait(&empty[s], ((g / C::kS) - 1) & 1, abort, kRoleX, g));
                 if (!ok) break;
-                uint8_t *stage = sm + s * e4::kStage;
-                bar_expect(&full[s], e4::kStage, leader);
+                uint8_t *stage = sm + s * C::kStage;
+                bar_expect(&full[s], C::kStage, leader);
                 tma_2d(stage, &map_x, (int)(kb * kBK), m0, &full[s], leader);                          // t0
-                tma_2d(stage + e4::kXTile, &map_x, (int)(kb * kBK), (int)a.m + m0, &full[s], leader);  // t1
-                tma_2d(stage + 2 * e4::kXTile, &map_w, (int)(kb * kBK), n0, &full[s], leader);
+                tma_2d(stage + C::kXTile, &map_x, (int)(kb * kBK), (int)a.m + m0, &full[s], leader);  // t1
+                tma_2d(stage + 2 * C::kXTile, &map_w, (int)(kb * kBK), n0, &full[s], leader);
             }
         }
-        drain(full, e4::kS, g);
-    } else if (warp == e4::kWarpMmaA || warp == e4::kWarpMmaB) {
+        drain(full, C::kS, g);
+    } else if (warp == C::kWarpMmaA || warp == C::kWarpMmaB) {
         // ---------------- MMA issuers (whole warp, lane 0 issues) -----------
-        const uint32_t parity = warp == e4::kWarpMmaA ? 0u : 1u;
+        const uint32_t parity = warp == C::kWarpMmaA ? 0u : 1u;
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 if ((g & 1) != parity) continue;
-                const int s = g % e4::kS, j = g % e4::kD;
-                ok = __all_sync(kFull, bar_wait(&full[s], (g / e4::kS) & 1, abort, kRoleMma, g));
-                if (ok && g >= (uint32_t)e4::kD)
-                    ok = __all_sync(kFull, bar_wait(&tempty[j], ((g / e4::kD) - 1) & 1, abort, kRoleMma, g));
+                const int s = g % C::kS, j = g % C::kD;
+                ok = __all_sync(kFull, bar_wait(&full[s], (g / C::kS) & 1, abort, kRoleMma, g));
+                if (ok && g >= (uint32_t)C::kD)
+                    ok = __all_sync(kFull, bar_wait(&tempty[j], ((g / C::kD) - 1) & 1, abort, kRoleMma, g));
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t x0 = sa(sm + s * e4::kStage), x1 = x0 + e4::kXTile, wb = x0 + 2 * e4::kXTile;
-                const uint32_t d = tmem + j * e4::kBN;
+                const uint32_t x0 = sa(sm + s * C::kStage), x1 = x0 + C::kXTile, wb = x0 + 2 * C::kXTile;
+                const uint32_t d = tmem + j * C::kBN;
 #pragma unroll
                 for (int ks = 0; ks < kBK / 32; ++ks) {
                     const uint64_t wd = sw128_desc(wb + ks * 32);
-                    mma_mx_e4m3(d, wd, sw128_desc(x0 + ks * 32), kIdescMx, tmem + e4::kSfA, tmem + e4::kSfB0, ks > 0,
+                    mma_mx_e4m3(d, wd, sw128_desc(x0 + ks * 32), C::kIdesc, tmem + C::kSfA, tmem + C::kSfB0, ks > 0,
                                 leader);
-                    mma_mx_e4m3(d, wd, sw128_desc(x1 + ks * 32), kIdescMx, tmem + e4::kSfA, tmem + e4::kSfB1, 1,
+                    mma_mx_e4m3(d, wd, sw128_desc(x1 + ks * 32), C::kIdesc, tmem + C::kSfA, tmem + C::kSfB1, 1,
                                 leader);
                 }
                 mma_commit(&empty[s], leader);
@@ -1330,41 +1342,55 @@ __global__ void __launch_bounds__(e4::kThreads, 1)
     } else {
         // ---------------- epilogue ----------------------------------------
         const uint32_t quad = warp & 3;                  // TMEM lanes this warp may touch
-        const uint32_t grp = (warp - e4::kWarpEpi0) >> 2;  // token columns kEpiCols*grp ..
-        const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * e4::kEpiCols;
+        const uint32_t grp = (warp - C::kWarpEpi0) >> 2;  // token columns kEpiCols*grp ..
+        const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * C::kEpiCols;
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
             uint32_t rb, mt;
             tile_rc(tile, a, rb, mt);
             const uint32_t n = rb * kBM + quad * 32 + lane;                   // weight row
-            const uint32_t tok0 = mt * e4::kBN + grp * e4::kEpiCols;                    // first token
+            const uint32_t tok0 = mt * C::kBN + grp * C::kEpiCols;                    // first token
             const float *srow = a.S + (size_t)rb * nkb;
-            float acc[e4::kEpiCols];
+            float acc[C::kEpiCols];
             float sc = __ldg(srow);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
-                const int j = g % e4::kD;
+                const int j = g % C::kD;
                 const float sc_next = kb + 1 < nkb ? __ldg(srow + kb + 1) : 0.f;
-                ok = __all_sync(kFull, bar_wait(&tfull[j], (g / e4::kD) & 1, abort, kRoleEpi, g));
+                ok = __all_sync(kFull, bar_wait(&tfull[j], (g / C::kD) & 1, abort, kRoleEpi, g));
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                if constexpr (C::kEarly) {
+                    // all of the warp's columns into registers; P[j] goes back
+                    // to the MMA before the promotion runs
+                    uint32_t p[C::kEpiCols / 16][16];
 #pragma unroll
-                for (int c = 0; c < e4::kEpiCols / 32; ++c) {  // two loads in flight per wait
-                    uint32_t p0[16], p1[16];
-                    tmem_ld16(tbase + j * e4::kBN + c * 32, p0);
-                    tmem_ld16(tbase + j * e4::kBN + c * 32 + 16, p1);
+                    for (int c = 0; c < C::kEpiCols / 16; ++c) tmem_ld16(tbase + j * C::kBN + c * 16, p[c]);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    promote16(acc + 32 * c, p0, sc, kb == 0);
-                    promote16(acc + 32 * c + 16, p1, sc, kb == 0);
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(&tempty[j]);  // P[j] is free for block g + D
+#pragma unroll
+                    for (int c = 0; c < C::kEpiCols / 16; ++c) promote16(acc + 16 * c, p[c], sc, kb == 0);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < C::kEpiCols / 32; ++c) {  // two loads in flight per wait
+                        uint32_t p0[16], p1[16];
+                        tmem_ld16(tbase + j * C::kBN + c * 32, p0);
+                        tmem_ld16(tbase + j * C::kBN + c * 32 + 16, p1);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        promote16(acc + 32 * c, p0, sc, kb == 0);
+                        promote16(acc + 32 * c + 16, p1, sc, kb == 0);
+                    }
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) bar_arrive(&tempty[j]);  // P[j] is free for block g + D
                 }
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) bar_arrive(&tempty[j]);  // P[j] is free for block g + D
                 sc = sc_next;
             }
             if (ok && n < a.N) {
 #pragma unroll
-                for (int i = 0; i < e4::kEpiCols; ++i) {
+                for (int i = 0; i < C::kEpiCols; ++i) {
                     const uint32_t tok = tok0 + i;
                     if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
                 }
@@ -1446,34 +1472,41 @@ __global__ void __launch_bounds__(kPrepThreads) gemm_prep_e4m3_kernel(const void
     if (threadIdx.x == 0) tscale[row] = __uint_as_float((uint32_t)(127 + e) << 23);
 }
 
-int launch_gemm_e4m3(const q35cu_weight *w, const uint8_t *Xq, const float *tscale, uint32_t m, float *Y,
-                     cudaStream_t st)
+template <class C>
+int launch_gemm_e4m3_cfg(const q35cu_weight *w, const uint8_t *Xq, const float *tscale, uint32_t m, float *Y,
+                         cudaStream_t st)
 {
     const uint32_t N = w->rows, K = w->cols;
-    const uint64_t mtiles = (m + e4::kBN - 1) / e4::kBN, ntiles = mtiles * ((N + kBM - 1) / kBM);
+    const uint64_t mtiles = (m + C::kBN - 1) / C::kBN, ntiles = mtiles * ((N + kBM - 1) / kBM);
     if (ntiles > 0x7FFFFFFFu || (uint64_t)m * 2 > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: shape too large");
     CUtensorMap mx, mw;
-    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, Xq, K, (uint64_t)m * 2, K, 128, e4::kBN);
+    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, Xq, K, (uint64_t)m * 2, K, 128, C::kBN);
     if (rc) return rc;
     rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
     if (rc) return rc;
     GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, 0u,
                0u, 0u, nullptr, nullptr, 0u};
-    a.gm = raster_group((uint32_t)mtiles, e4::kBN, K);
-    static bool configured[64] = {};
+    a.gm = raster_group((uint32_t)mtiles, C::kBN, K);
+    static bool configured[64] = {};  // per configuration and device
     int dev = 0, sms = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));
     rc = sm_count_of(dev, &sms);
     if (rc) return rc;
     const int reserve = g_gemm_reserved_sms.load();
     if (reserve > 0 && reserve < sms) sms -= reserve;
-    const size_t smem = e4::kSmem + 1024;
+    const size_t smem = C::kSmem + 1024;
     if (!configured[dev]) {
-        Q35CU_CUDA(cudaFuncSetAttribute(gemm_e4m3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        Q35CU_CUDA(cudaFuncSetAttribute(gemm_e4m3_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured[dev] = true;
     }
     const uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
-    return launch_after_prep(gemm_e4m3_tc_kernel, grid, e4::kThreads, smem, st, mx, mw, a);
+    return launch_after_prep(gemm_e4m3_tc_kernel<C>, grid, C::kThreads, smem, st, mx, mw, a);
+}
+
+int launch_gemm_e4m3(const q35cu_weight *w, const uint8_t *Xq, const float *tscale, uint32_t m, float *Y,
+                     cudaStream_t st)
+{
+    return launch_gemm_e4m3_cfg<e4::Wide>(w, Xq, tscale, m, Y, st);
 }
 
 // the fp8-operand kernel unless Q35CU_GEMM_F16 asks for the f16 one

@@ -943,12 +943,20 @@ size_t gemm_workspace_bytes(uint32_t m, uint32_t K)
     return (((size_t)m * K * 2 + 255) & ~(size_t)255) + (size_t)m * 4;
 }
 
-size_t gemm_exact_workspace_bytes(uint32_t m, uint32_t K) { return gemm_workspace_bytes(2 * m, K); }
+// multi-token decode on the tensor cores with exact fp32 activations: room
+// for either preparation -- five e4m3 term rows per token (the default
+// kernel) or two f16 rows (the hi/lo kernel) -- with the scales at the end
+size_t gemm_exact_workspace_bytes(uint32_t m, uint32_t K)
+{
+    const size_t terms = (((size_t)m * K * 5 + 255) & ~(size_t)255) + (size_t)m * 4;
+    const size_t hilo = gemm_workspace_bytes(2 * m, K);
+    return terms > hilo ? terms : hilo;
+}
 
-// multi-token decode on the tensor cores with exact fp32 activations:
-// split prep (2m f16 rows) + the GEMM in pair mode
-int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
-                      cudaStream_t st)
+namespace {
+// the hi/lo kernel: split prep (2m f16 rows) + the f16 GEMM in pair mode
+int launch_gemm_exact_f16(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
+                          cudaStream_t st)
 {
     if (!m) return Q35CU_OK;
     const uint32_t K = w->cols;
@@ -964,6 +972,7 @@ int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *
     Q35CU_CUDA(cudaGetLastError());
     return launch_gemm_fp8(w, xh, ts, 2 * m, Y, st, true);
 }
+}  // namespace
 
 int launch_gemm_prep(const void *X, bool f32, uint32_t m, uint32_t K, uint16_t *Xh, float *tscale,
                      cudaStream_t st)
@@ -1036,12 +1045,12 @@ SkScratch g_sk[64];
 // Stream-K for a narrow-tile launch when it cuts the busiest CTA's block
 // count by a tenth or more; fills a's stream-K fields.  false = whole tiles.
 constexpr uint64_t kSkMinBlocks = 8;             // blocks per CTA at least (amortises a cut tile's hand-off)
-constexpr size_t kSkMaxBytes = (size_t)64 << 20;  // scratch cap
+constexpr size_t kSkMaxBytes = (size_t)128 << 20;  // scratch cap (48-token e4m3-term tiles: ~91 MB)
 
-template <int BN>
-bool plan_stream_k(GemmArgs &a, uint32_t sms, cudaStream_t st, uint32_t *grid)
+// cols: accumulator columns a cut tile hands off (BN of the f16 kernel)
+bool plan_stream_k(GemmArgs &a, uint32_t cols, uint32_t sms, cudaStream_t st, uint32_t *grid)
 {
-    if (BN > 128 || getenv("Q35CU_GEMM_NO_STREAMK")) return false;
+    if (getenv("Q35CU_GEMM_NO_STREAMK")) return false;
     const uint64_t U = (uint64_t)a.ntiles * a.kblocks;
     const uint32_t G = (uint32_t)(U / kSkMinBlocks < sms ? U / kSkMinBlocks : sms);
     if (G < 2) return false;
@@ -1050,7 +1059,7 @@ bool plan_stream_k(GemmArgs &a, uint32_t sms, cudaStream_t st, uint32_t *grid)
     const uint64_t sk = (U + G - 1) / G;
     if (sk * 10 > whole * 9) return false;
     const uint32_t maxseg = (uint32_t)((a.kblocks + per - 1) / per + 1);
-    const size_t need = kSkCntBytes + (size_t)G * maxseg * BN * kBM * 4;
+    const size_t need = kSkCntBytes + (size_t)G * maxseg * cols * kBM * 4;
     if (G * 4 > kSkCntBytes || need > kSkMaxBytes) return false;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
@@ -1107,7 +1116,7 @@ int launch_gemm_bn(const q35cu_weight *w, const uint16_t *Xh, const float *tscal
         configured[dev] = true;
     }
     uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
-    plan_stream_k<BN>(a, (uint32_t)sms, st, &grid);
+    if (BN <= 128) plan_stream_k(a, BN, (uint32_t)sms, st, &grid);
     return launch_after_prep(gemm_fp8_tc_kernel<BN>, grid, kThreads, smem, st, mx, mw, a);
 }
 
@@ -1509,6 +1518,381 @@ int launch_gemm_e4m3(const q35cu_weight *w, const uint8_t *Xq, const float *tsca
     return launch_gemm_e4m3_cfg<e4::Wide>(w, Xq, tscale, m, Y, st);
 }
 
+// ---------------------------------------------------------------------------
+// Multi-token decode on e4m3 operands (16..127 tokens, exact fp32
+// activations): tcgen05.mma kind::f8f6f4, e4m3 x e4m3.
+//
+// Each fp32 token row x is carried by five e4m3 terms: with 2^-e putting the
+// row's largest magnitude in [2^7, 2^8),
+//     r0 = x 2^-e,  t_j = e4m3(r_j),  r_{j+1} = 16 (r_j - t_j)
+// (every difference and product exact in fp32), so x 2^-e = sum_j t_j 16^-j
+// up to the last residual: 1.2e-10 of the row's largest at most (a CPU check
+// of the split over N(0, 1) rows; an fp32 value has 24 significant bits, a
+// term 4).  Rows 5t .. 5t+4 of the prepared activations are token t's terms,
+// so one MMA with N = 5 x tokens multiplies them all with the weight slice as
+// the TMA landed it -- no conversion, no TMEM operand.  The epilogue keeps
+// the term columns apart through the K loop (ACC += s[n/128, kb] * P per
+// 128-column block) and stores Y = (sum_j ACC_j 16^-j) 2^e.
+//
+// Tiles: 128 weight rows x 16, 32 or 48 tokens (MMA N = 80, 160, 240).
+// Stream-K over (tile, 128-column block) units when the row tiles are few,
+// as in the f16 kernel: a tile cut by CTA boundaries is finished from its
+// segments' accumulators in a fixed order (runs repeat bit for bit).
+// Roles: warp 0 producer (a block's activation terms and weight tile into
+// one stage), warps 1 and 2 MMA (even / odd blocks; commits release the
+// stage and fill the accumulator), warps 3.. epilogue: 4 lane quadrants x
+// groups of 16 tokens (80 term columns each).
+// ---------------------------------------------------------------------------
+namespace dec {
+constexpr int kTerms = 5;
+constexpr int kTokPerWarp = 16;
+constexpr int kColsPerWarp = kTerms * kTokPerWarp;  // 80 term columns per epilogue warp (16-aligned loads)
+template <int TOK>
+struct Cfg {
+    static constexpr int kTok = TOK;                        // tokens per tile
+    static constexpr int kN = kTerms * TOK;                 // MMA N
+    static constexpr int kGroups = TOK / kTokPerWarp;
+    static constexpr int kStride = kN;                      // accumulator column stride
+    static constexpr int kD = TOK == 16 ? 4 : (TOK == 32 ? 3 : 2);
+    static constexpr uint32_t kXTile = (uint32_t)kN * kBK;
+    static constexpr uint32_t kStage = kXTile + kWTile;
+    static constexpr int kS = TOK == 16 ? 8 : (TOK == 32 ? 6 : 4);
+    static constexpr int kWarpMmaA = 1, kWarpMmaB = 2, kWarpEpi0 = 3, kEpiWarps = 4 * kGroups;
+    static constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+    static constexpr uint32_t kBars = kS * kStage;
+    static constexpr uint32_t kSmem = kBars + 256;
+    static constexpr uint32_t kSkCols = kN;                  // stream-K slot columns
+    static_assert(TOK % kTokPerWarp == 0, "whole epilogue groups");
+    // kind::f8f6f4: D f32 (bits 4-5 = 1), A and B e4m3 (0), K-major, N, M = 128
+    static constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+    static_assert(kN % 16 == 0 && kN <= 256, "M = 128 MMAs take N = 16..256 in steps of 16");
+    static_assert(kD * kStride <= (int)kTmemCols, "TMEM budget");
+    static_assert(kStage % 1024 == 0, "swizzle atoms need 1024-byte alignment");
+    static_assert((2 * kS + 2 * kD + 2) * 8 + 16 <= 256, "barriers fit their 256 bytes");
+    static_assert(kSmem + 1024 <= 232448, "shared memory");
+};
+}  // namespace dec
+
+// D[tmem] (+)= A[smem descriptor] * B[smem descriptor], e4m3 x e4m3 -> f32
+__device__ __forceinline__ void mma_e4m3_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc_, uint32_t acc,
+                                            uint32_t leader)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 e, %5, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc_), "r"(acc), "r"(leader)
+        : "memory");
+}
+
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
+    gemm_dec_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                    const __grid_constant__ GemmArgs a)
+{
+    constexpr uint32_t kFull = 0xffffffffu;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // block g: stage g % S (full: TMA bytes landed -> MMA; empty: its MMAs
+    // completed -> producer), accumulator g % D (tfull: MMAs completed ->
+    // epilogue; tempty: drained by the epilogue warps -> MMA)
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + C::kBars);
+    uint64_t *empty = full + C::kS;
+    uint64_t *tfull = empty + C::kS;
+    uint64_t *tempty = tfull + C::kD;
+    uint64_t *fin = tempty + C::kD;
+    volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(fin + 2);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 2) + 1;
+    volatile uint32_t *sk_state = reinterpret_cast<volatile uint32_t *>(fin + 2) + 2;
+    volatile uint32_t *epi_aborts = reinterpret_cast<volatile uint32_t *>(fin + 2) + 3;
+
+    const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const uint32_t nkb = a.kblocks;
+    const uint32_t leader = lane == 0;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (t == 32) {
+        for (int i = 0; i < C::kS; ++i) {
+            bar_init(&full[i], 1);
+            bar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < C::kD; ++i) {
+            bar_init(&tfull[i], 1);
+            bar_init(&tempty[i], C::kEpiWarps);
+        }
+        bar_init(&fin[0], 1);
+        bar_init(&fin[1], 1);
+        *abort = 0;
+        *epi_aborts = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer (whole warp) ------------------------------
+        pdl_wait();  // the prepared activations and scales are complete and visible
+        uint32_t g = 0, tile, kb0, kb1;
+        bool ok = true;
+        for (SegWalk<true> walk(a); ok && walk.next(tile, kb0, kb1);) {
+            uint32_t rb, mt;
+            tile_rc(tile, a, rb, mt);
+            const int m0 = (int)(mt * C::kN), n0 = (int)(rb * kBM);
+            for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
+                const int s = g % C::kS;
+                if (g >= (uint32_t)C::kS)
+                    ok = __all_sync(kFull, bar_wait(&empty[s], ((g / C::kS) - 1) & 1, abort, kRoleX, g));
+                if (!ok) break;
+                uint8_t *stage = sm + s * C::kStage;
+                bar_expect(&full[s], C::kStage, leader);
+                tma_2d(stage, &map_x, (int)(kb * kBK), m0, &full[s], leader);
+                tma_2d(stage + C::kXTile, &map_w, (int)(kb * kBK), n0, &full[s], leader);
+            }
+        }
+        drain(full, C::kS, g);
+    } else if (warp == C::kWarpMmaA || warp == C::kWarpMmaB) {
+        // ---------------- MMA issuers (whole warp, lane 0 issues) -----------
+        const uint32_t parity = warp == C::kWarpMmaA ? 0u : 1u;
+        uint32_t g = 0, tile, kb0, kb1;
+        bool ok = true;
+        for (SegWalk<true> walk(a); ok && walk.next(tile, kb0, kb1);) {
+            for (uint32_t kb = kb0; kb < kb1; ++kb, ++g) {
+                if ((g & 1) != parity) continue;
+                const int s = g % C::kS, j = g % C::kD;
+                ok = __all_sync(kFull, bar_wait(&full[s], (g / C::kS) & 1, abort, kRoleMma, g));
+                if (ok && g >= (uint32_t)C::kD)
+                    ok = __all_sync(kFull, bar_wait(&tempty[j], ((g / C::kD) - 1) & 1, abort, kRoleMma, g));
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t xb = sa(sm + s * C::kStage), wb = xb + C::kXTile;
+                const uint32_t d = tmem + j * C::kStride;
+#pragma unroll
+                for (int ks = 0; ks < kBK / 32; ++ks)
+                    mma_e4m3_ss(d, sw128_desc(wb + ks * 32), sw128_desc(xb + ks * 32), C::kIdesc, ks > 0, leader);
+                mma_commit(&empty[s], leader);
+                mma_commit(&tfull[j], leader);
+            }
+        }
+        mma_commit(&fin[parity], leader);
+        __syncwarp();
+        bar_wait(&fin[parity], 0, nullptr, kRoleDrain, g);
+    } else {
+        // ---------------- epilogue ----------------------------------------
+        const uint32_t quad = warp & 3;                      // TMEM lanes this warp may touch
+        const uint32_t grp = (warp - C::kWarpEpi0) >> 2;     // tokens 16*grp .. of the tile
+        const uint32_t tbase = tmem + ((quad * 32) << 16) + grp * dec::kColsPerWarp;
+        const uint32_t row = quad * 32 + lane;
+        auto epi_bar = [] { asm volatile("bar.sync 1, %0;" ::"n"(C::kEpiWarps * 32) : "memory"); };
+        uint32_t g = 0, tile, kb0, kb1;
+        bool ok = true;
+        // every segment is visited even after an abort: the hand-off of a cut
+        // tile needs all epilogue warps at its barriers
+        for (SegWalk<true> walk(a); walk.next(tile, kb0, kb1);) {
+            uint32_t rb, mt;
+            tile_rc(tile, a, rb, mt);
+            const uint32_t n = rb * kBM + row;                                       // weight row
+            const uint32_t tok0 = mt * C::kTok + grp * dec::kTokPerWarp;            // first token
+            const float *srow = a.S + (size_t)rb * nkb;
+            float acc[dec::kColsPerWarp];
+            float sc = ok ? __ldg(srow + kb0) : 0.f;
+            for (uint32_t kb = kb0; ok && kb < kb1; ++kb, ++g) {
+                const int j = g % C::kD;
+                const float sc_next = kb + 1 < kb1 ? __ldg(srow + kb + 1) : 0.f;
+                ok = __all_sync(kFull, bar_wait(&tfull[j], (g / C::kD) & 1, abort, kRoleEpi, g));
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t tcol = tbase + j * C::kStride;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {  // two loads in flight per wait
+                    uint32_t p0[16], p1[16];
+                    tmem_ld16(tcol + c * 32, p0);
+                    tmem_ld16(tcol + c * 32 + 16, p1);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    promote16(acc + 32 * c, p0, sc, kb == kb0);
+                    promote16(acc + 32 * c + 16, p1, sc, kb == kb0);
+                }
+                {
+                    uint32_t p0[16];
+                    tmem_ld16(tcol + 64, p0);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    promote16(acc + 64, p0, sc, kb == kb0);
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(&tempty[j]);  // the accumulator is free for block g + D
+                sc = sc_next;
+            }
+            bool store = ok;
+            if (kb0 != 0 || kb1 != nkb) {
+                // stream-K: this CTA's share of a cut tile.  Slot c1 = the
+                // tile's first inner CTA boundary, segment = CTA - (c1 - 1).
+                const uint64_t U = (uint64_t)a.ntiles * nkb;
+                const uint32_t c1 = (uint32_t)((((uint64_t)tile * nkb + 1) * gridDim.x + U - 1) / U);
+                const uint32_t cl = (uint32_t)(((uint64_t)(tile + 1) * nkb * gridDim.x + U - 1) / U) - 1;
+                float *slot0 = a.skpart + (size_t)c1 * a.maxseg * C::kSkCols * kBM;
+                if (ok) {
+                    float *sl = slot0 + (size_t)(blockIdx.x + 1 - c1) * C::kSkCols * kBM + (size_t)grp * dec::kColsPerWarp * kBM + row;
+#pragma unroll
+                    for (int i = 0; i < dec::kColsPerWarp; ++i) sl[(size_t)i * kBM] = acc[i];
+                } else if (lane == 0) {
+                    atomicAdd(const_cast<uint32_t *>(epi_aborts), 1u);
+                }
+                epi_bar();
+                if (warp == C::kWarpEpi0 && lane == 0) {
+                    uint32_t st_ = 0;
+                    if (*abort == 0 && *epi_aborts == 0) {
+                        __threadfence();
+                        const uint32_t done_ = atomicAdd(a.skcnt + c1, kb1 - kb0) + (kb1 - kb0);
+                        st_ = 1;
+                        if (done_ == nkb) {  // the tile's last segment: this CTA stores it
+                            __threadfence();
+                            a.skcnt[c1] = 0;  // ready for the next launch
+                            st_ = 3;
+                        }
+                    }
+                    *sk_state = st_;
+                }
+                epi_bar();
+                const uint32_t st_ = *sk_state;
+                if (!(st_ & 1)) ok = false;
+                store = (st_ & 2) != 0;
+                if (store) {
+                    const float *sl = slot0 + (size_t)grp * dec::kColsPerWarp * kBM + row;
+#pragma unroll
+                    for (int i = 0; i < dec::kColsPerWarp; ++i) acc[i] = 0.f;
+                    for (uint32_t js = 0; js < cl - c1 + 2; ++js, sl += (size_t)C::kSkCols * kBM) {
+#pragma unroll
+                        for (int i = 0; i < dec::kColsPerWarp; ++i) acc[i] += __ldcg(sl + (size_t)i * kBM);
+                    }
+                }
+            }
+            if (store && n < a.N) {
+#pragma unroll
+                for (int i = 0; i < dec::kTokPerWarp; ++i) {
+                    const uint32_t tok = tok0 + i;
+                    if (tok < a.m) {
+                        const float *q = acc + dec::kTerms * i;
+                        float y = q[4] * 0.0625f + q[3];  // the terms' sum, smallest first: y = q0 + q1/16 + ...
+                        y = fmaf(y, 0.0625f, q[2]);
+                        y = fmaf(y, 0.0625f, q[1]);
+                        y = fmaf(y, 0.0625f, q[0]);
+                        a.Y[(size_t)tok * a.N + n] = y * __ldg(a.tscale + tok);
+                    }
+                }
+            }
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// Five e4m3 terms of an exact fp32 token row: one CTA per token.  e =
+// floor(log2(max |x|)) - 7 (kept in [-126, 127]; 0 for a row of zeros or one
+// whose largest magnitude is not finite); r0 = x 2^-e, t_j = e4m3(r_j),
+// r_{j+1} = 16 (r_j - t_j); row 5r + j of Xq holds t_j.  A non-finite
+// element becomes the NaN code in t0 and 0 in the other terms.
+__global__ void __launch_bounds__(kPrepThreads) gemm_prep_terms_kernel(const float *X, uint32_t K, uint8_t *Xq,
+                                                                       float *tscale)
+{
+    pdl_trigger();  // the GEMM after this kernel may start streaming weights
+    __shared__ float red[kPrepThreads / 32];
+    const size_t row = blockIdx.x;
+    const uint32_t k4 = K / 4;
+    const float4 *x4 = reinterpret_cast<const float4 *>(X) + row * k4;
+    float mx = 0.f;
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = __ldg(x4 + i);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < kPrepThreads / 32; ++i) mx = fmaxf(mx, red[i]);
+    const int eb = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+    int e = 0;
+    if (eb == 0 && mx > 0.f) e = -126;
+    else if (eb > 0 && eb < 255) e = max(eb - 127 - 7, -126);
+    const float down = __uint_as_float((uint32_t)(127 - e) << 23);
+    uint32_t *out = reinterpret_cast<uint32_t *>(Xq + dec::kTerms * row * K);
+    for (uint32_t i = threadIdx.x; i < k4; i += kPrepThreads) {
+        const float4 v = __ldg(x4 + i);
+        float r[4] = {v.x * down, v.y * down, v.z * down, v.w * down};
+        uint32_t nan_mask = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (!(fabsf(r[q]) <= 3.402823466e38f)) {
+                nan_mask |= 0xFFu << (8 * q);
+                r[q] = 0.f;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < dec::kTerms; ++j) {
+            const uint32_t tq = to_e4m3x4(r[0], r[1], r[2], r[3]);
+            out[(size_t)j * k4 + i] = j == 0 ? (tq & ~nan_mask) | (0x7F7F7F7Fu & nan_mask) : tq;
+            if (j + 1 < dec::kTerms) {
+                uint32_t h01, h23;
+                e4m3x4_to_f16x4(tq, h01, h23);
+                const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&h01));
+                const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&h23));
+                r[0] = (r[0] - f01.x) * 16.f;
+                r[1] = (r[1] - f01.y) * 16.f;
+                r[2] = (r[2] - f23.x) * 16.f;
+                r[3] = (r[3] - f23.y) * 16.f;
+            }
+        }
+    }
+    if (threadIdx.x == 0) tscale[row] = __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
+template <class C>
+int launch_gemm_dec_cfg(const q35cu_weight *w, const uint8_t *Xq, const float *tscale, uint32_t m, float *Y,
+                        cudaStream_t st)
+{
+    const uint32_t N = w->rows, K = w->cols;
+    const uint64_t mtiles = (m + C::kTok - 1) / C::kTok, ntiles = mtiles * ((N + kBM - 1) / kBM);
+    if (ntiles > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: shape too large");
+    CUtensorMap mx, mw;
+    // the term rows of every token tile: mtiles * kN rows (the last tile's
+    // rows past 5m read zeros)
+    int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, Xq, K, (uint64_t)m * dec::kTerms, K, 128, C::kN);
+    if (rc) return rc;
+    rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
+    if (rc) return rc;
+    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, 0u,
+               0u, 0u, nullptr, nullptr, 0u};
+    a.gm = (uint32_t)mtiles;  // token tile fastest: a row block's token tiles share its weight stream
+    static bool configured[64] = {};  // per configuration and device
+    int dev = 0, sms = 0;
+    Q35CU_CUDA(cudaGetDevice(&dev));
+    rc = sm_count_of(dev, &sms);
+    if (rc) return rc;
+    const int reserve = g_gemm_reserved_sms.load();
+    if (reserve > 0 && reserve < sms) sms -= reserve;
+    const size_t smem = C::kSmem + 1024;
+    if (!configured[dev]) {
+        Q35CU_CUDA(cudaFuncSetAttribute(gemm_dec_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured[dev] = true;
+    }
+    uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
+    plan_stream_k(a, C::kSkCols, (uint32_t)sms, st, &grid);
+    return launch_after_prep(gemm_dec_kernel<C>, grid, C::kThreads, smem, st, mx, mw, a);
+}
+
+// the f16 hi/lo kernel for multi-token decode when Q35CU_GEMV_TC_F16 is set
+bool dec_use_f16() { return getenv("Q35CU_GEMV_TC_F16") != nullptr; }
+
 // the fp8-operand kernel unless Q35CU_GEMM_F16 asks for the f16 one
 bool use_e4m3() { return getenv("Q35CU_GEMM_F16") == nullptr; }
 
@@ -1542,6 +1926,29 @@ int gemm_bf16_into(const q35cu_weight *w, const void *X, bool f32, uint32_t m, f
 // bf16 when f32): prepares the activations into `workspace`
 // (gemm_workspace_bytes(m, K): 2 m K bytes of prepared values, then m
 // scales) and runs the tensor-core GEMM.
+int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
+                      cudaStream_t st)
+{
+    if (!m) return Q35CU_OK;
+    if (dec_use_f16()) return launch_gemm_exact_f16(w, X, m, Y, workspace, st);
+    const uint32_t K = w->cols;
+    if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
+    if ((uintptr_t)X % 16 || (uintptr_t)workspace % 16 || (uintptr_t)w->d_w % 16)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned activations, weight or workspace");
+    if ((uint64_t)m * dec::kTerms > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: too many tokens");
+    const size_t need = gemm_exact_workspace_bytes(m, K);
+    uint8_t *xq = static_cast<uint8_t *>(workspace);
+    float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + need - (size_t)m * 4);
+    gemm_prep_terms_kernel<<<m, kPrepThreads, 0, st>>>(X, K, xq, ts);
+    count_launch();
+    Q35CU_CUDA(cudaGetLastError());
+    // token tiles of 16, 32 or 48: as few tiles as 48 allow, each as narrow as it can be
+    const uint32_t mtiles = (m + 47) / 48, per = (m + mtiles - 1) / mtiles;
+    if (per <= 16) return launch_gemm_dec_cfg<dec::Cfg<16>>(w, xq, ts, m, Y, st);
+    if (per <= 32) return launch_gemm_dec_cfg<dec::Cfg<32>>(w, xq, ts, m, Y, st);
+    return launch_gemm_dec_cfg<dec::Cfg<48>>(w, xq, ts, m, Y, st);
+}
+
 int launch_gemm_bf16(const q35cu_weight *w, const void *X, bool f32, uint32_t m, float *Y, void *workspace,
                      cudaStream_t st)
 {

@@ -74,14 +74,85 @@ def test_config1_batch_sweep(gpu, orc, ref, shape, m):
     _check(orc, W, sc, X, Y, ref.mm_fp8_batch(W, sc, X), f"C1 {shape} m={m}")
 
 
-@pytest.mark.parametrize("n", [16, 17, 32, 33, 64, 65, 127])
+@pytest.mark.parametrize("n", [16, 17, 32, 33, 48, 49, 64, 65, 100, 127])
 def test_exact_tensor_core_tile_widths(gpu, orc, ref, n):
     """q35_mm_fp8_batch with 16..127 tokens runs the tensor cores on exact
-    (hi/lo split) activations, 2n rows: a 32-, 64-, 128- or 192-row token
-    tile (n = 16 | 17..32 | 33..64 | 65..127), each within the GEMV bound."""
+    activations: each token as five e4m3 terms (the default kernel: token
+    tiles of 16, 32 or 48, as few tiles as 48 allow), or as f16 hi/lo rows
+    (Q35CU_GEMV_TC_F16: 32-, 64-, 128- or 192-row tiles).  Both within the
+    GEMV bound, on ragged tile fills too."""
     W, sc = _synth(orc, 70 + n, 1000, 5120)
     X = orc.synth_act(90 + n, (n, 5120))
-    _check(orc, W, sc, X, q35cu.mm_fp8_batch(W, sc, X), ref.mm_fp8_batch(W, sc, X), f"n={n}")
+    Yr = ref.mm_fp8_batch(W, sc, X)
+    _check(orc, W, sc, X, q35cu.mm_fp8_batch(W, sc, X), Yr, f"e4m3 terms n={n}")
+
+
+def _e4m3_values():
+    """float value of every e4m3 code (0x7F / 0xFF: NaN)"""
+    v = np.empty(256, np.float64)
+    for c in range(256):
+        sgn = -1.0 if c & 0x80 else 1.0
+        e, mt = (c >> 3) & 0xF, c & 7
+        v[c] = sgn * (mt / 8.0 * 2.0 ** -6 if e == 0 else (1 + mt / 8.0) * 2.0 ** (e - 7))
+    v[0x7F] = v[0xFF] = np.nan
+    return v
+
+
+def test_e4m3_decode_terms_carry_fp32(gpu, orc):
+    """The multi-token decode preparation (left in the caller's workspace):
+    per token 2^e and five e4m3 rows t0..t4 with x = sum_j t_j 16^-j 2^e to
+    within 2^-32 of the row's largest magnitude (fp32 rows spanning 2^40,
+    tiny elements beside large ones), the largest in [2^7, 2^8) after
+    scaling."""
+    import torch
+
+    m, k = 20, 512
+    rng = np.random.default_rng(11)
+    X = orc.synth_act(111, (m, k)) * np.exp2(rng.integers(-20, 20, (m, 1))).astype(np.float32)
+    X[3] = 0.0
+    X[4, ::5] *= np.float32(2.0 ** -25)
+    w = q35cu.Weight.synth_fp8(112, 256, k)
+    try:
+        Xd = torch.from_numpy(X).cuda()
+        Y = torch.empty((m, 256), device="cuda")
+        need = int(q35cu.load().q35cu_gemv_fp8_tc_workspace_bytes(m, k))
+        work = torch.zeros(need, dtype=torch.uint8, device="cuda")
+        q35cu.gemv_tc(w, Xd, Y, work)
+        torch.cuda.synchronize()
+        q35cu.check_device_status()
+        raw = work.cpu().numpy()
+        terms = raw[:5 * m * k].reshape(m, 5, k)
+        ts = raw[len(raw) - 4 * m:].view(np.float32).astype(np.float64)
+        tab = _e4m3_values()
+        rec = sum(tab[terms[:, j]] * 16.0 ** -j for j in range(5)) * ts[:, None]
+        x64 = X.astype(np.float64)
+        mx = np.abs(x64).max(axis=1, keepdims=True)
+        assert np.isfinite(rec).all()
+        assert (np.abs(rec - x64) <= mx * 2.0 ** -32).all()
+        live = mx[:, 0] > 0
+        assert ((mx[live, 0] / ts[live] >= 128) & (mx[live, 0] / ts[live] < 256)).all()
+        assert (rec[3] == 0).all()
+    finally:
+        w.free()
+
+
+@pytest.mark.parametrize("rows,cols,n", [(17408, 5120, 16), (5120, 17408, 32), (5120, 6144, 100)])
+def test_exact_decode_kernels_agree(gpu, orc, ref, monkeypatch, rows, cols, n):
+    """The e4m3-term kernel and the f16 hi/lo kernel (Q35CU_GEMV_TC_F16) on
+    the same multi-token decode: both within the GEMV bound of the
+    reference, runs repeat bit for bit, and their difference is of the order
+    of fp32 accumulation (max 2^-16 of sum |w s x|)."""
+    W, sc = _synth(orc, 2500 + rows + n, rows, cols)
+    X = orc.synth_act(2600 + n, (n, cols))
+    Yr = ref.mm_fp8_batch(W, sc, X)
+    Ye = q35cu.mm_fp8_batch(W, sc, X)
+    assert np.array_equal(Ye.view(np.uint32), q35cu.mm_fp8_batch(W, sc, X).view(np.uint32))
+    _check(orc, W, sc, X, Ye, Yr, f"e4m3 terms {rows}x{cols} n={n}")
+    monkeypatch.setenv("Q35CU_GEMV_TC_F16", "1")
+    Yf = q35cu.mm_fp8_batch(W, sc, X)
+    _check(orc, W, sc, X, Yf, Yr, f"hi/lo {rows}x{cols} n={n}")
+    _, abs_sum = orc.mm_fp8_f64(W, sc, X)
+    assert (np.abs(Ye.astype(np.float64) - Yf) <= 2.0 ** -16 * abs_sum).all()
 
 
 def test_batch_equals_single_bitwise(gpu, orc):

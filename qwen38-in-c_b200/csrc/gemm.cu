@@ -1892,6 +1892,7 @@ int launch_gemm_dec_cfg(const q35cu_weight *w, const uint8_t *Xq, const float *t
 
 // the f16 hi/lo kernel for multi-token decode when Q35CU_GEMV_TC_F16 is set
 bool dec_use_f16() { return getenv("Q35CU_GEMV_TC_F16") != nullptr; }
+constexpr uint32_t kDecMaxTokens = 48;  // larger batches take the hi/lo kernel
 
 // the fp8-operand kernel unless Q35CU_GEMM_F16 asks for the f16 one
 bool use_e4m3() { return getenv("Q35CU_GEMM_F16") == nullptr; }
@@ -1930,7 +1931,11 @@ int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *
                       cudaStream_t st)
 {
     if (!m) return Q35CU_OK;
-    if (dec_use_f16()) return launch_gemm_exact_f16(w, X, m, Y, workspace, st);
+    // e4m3 terms up to 48 tokens; above, two f16 rows per token beat five
+    // e4m3 rows (CUDA-graph timing, 17408x5120: 16 / 32 / 48 tokens 22.6 /
+    // 27.6 / 35.6 us against 25.6 / 32.4 / 37.3; 64 / 100 tokens 44.7 / 84.7
+    // against 37.3 / 64.0)
+    if (m > kDecMaxTokens || dec_use_f16()) return launch_gemm_exact_f16(w, X, m, Y, workspace, st);
     const uint32_t K = w->cols;
     if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
     if ((uintptr_t)X % 16 || (uintptr_t)workspace % 16 || (uintptr_t)w->d_w % 16)
@@ -1942,10 +1947,9 @@ int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *
     gemm_prep_terms_kernel<<<m, kPrepThreads, 0, st>>>(X, K, xq, ts);
     count_launch();
     Q35CU_CUDA(cudaGetLastError());
-    // token tiles of 16, 32 or 48: as few tiles as 48 allow, each as narrow as it can be
-    const uint32_t mtiles = (m + 47) / 48, per = (m + mtiles - 1) / mtiles;
-    if (per <= 16) return launch_gemm_dec_cfg<dec::Cfg<16>>(w, xq, ts, m, Y, st);
-    if (per <= 32) return launch_gemm_dec_cfg<dec::Cfg<32>>(w, xq, ts, m, Y, st);
+    // one token tile of 16, 32 or 48
+    if (m <= 16) return launch_gemm_dec_cfg<dec::Cfg<16>>(w, xq, ts, m, Y, st);
+    if (m <= 32) return launch_gemm_dec_cfg<dec::Cfg<32>>(w, xq, ts, m, Y, st);
     return launch_gemm_dec_cfg<dec::Cfg<48>>(w, xq, ts, m, Y, st);
 }
 

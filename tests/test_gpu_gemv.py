@@ -77,10 +77,10 @@ def test_config1_batch_sweep(gpu, orc, ref, shape, m):
 @pytest.mark.parametrize("n", [16, 17, 32, 33, 48, 49, 64, 65, 100, 127])
 def test_exact_tensor_core_tile_widths(gpu, orc, ref, n):
     """q35_mm_fp8_batch with 16..127 tokens runs the tensor cores on exact
-    activations: each token as five e4m3 terms (the default kernel: token
-    tiles of 16, 32 or 48, as few tiles as 48 allow), or as f16 hi/lo rows
-    (Q35CU_GEMV_TC_F16: 32-, 64-, 128- or 192-row tiles).  Both within the
-    GEMV bound, on ragged tile fills too."""
+    activations: up to 48 tokens each token as five e4m3 terms (one token
+    tile of 16, 32 or 48), above that (or with Q35CU_GEMV_TC_F16) as f16
+    hi/lo rows (32-, 64-, 128- or 192-row tiles).  Within the GEMV bound,
+    on ragged tile fills too."""
     W, sc = _synth(orc, 70 + n, 1000, 5120)
     X = orc.synth_act(90 + n, (n, 5120))
     Yr = ref.mm_fp8_batch(W, sc, X)
@@ -136,7 +136,7 @@ def test_e4m3_decode_terms_carry_fp32(gpu, orc):
         w.free()
 
 
-@pytest.mark.parametrize("rows,cols,n", [(17408, 5120, 16), (5120, 17408, 32), (5120, 6144, 100)])
+@pytest.mark.parametrize("rows,cols,n", [(17408, 5120, 16), (5120, 17408, 32), (5120, 6144, 48)])
 def test_exact_decode_kernels_agree(gpu, orc, ref, monkeypatch, rows, cols, n):
     """The e4m3-term kernel and the f16 hi/lo kernel (Q35CU_GEMV_TC_F16) on
     the same multi-token decode: both within the GEMV bound of the

@@ -78,6 +78,7 @@
 #include <cuda_fp8.h>
 
 #include <atomic>
+#include <cstring>
 
 #include "q35cu_internal.h"
 
@@ -161,15 +162,17 @@ struct GemmArgs {
 // tile, whose epilogue has no registers to spare for the stream-K state).
 template <bool SKOK>
 struct SegWalk {
-    uint32_t u, u1, nkb, ntiles;
-    bool sk;
+    uint32_t u, u1, nkb, ntiles, mode, nsplit;
     __device__ __forceinline__ explicit SegWalk(const GemmArgs &a)
-        : nkb(a.kblocks), ntiles(a.ntiles), sk(SKOK && a.sk != 0)
+        : nkb(a.kblocks), ntiles(a.ntiles), mode(SKOK ? a.sk : 0u), nsplit(a.maxseg)
     {
-        if (sk) {
+        if (mode == 1) {  // stream-K: this CTA's range of (tile, block) units
             const uint64_t U = (uint64_t)a.ntiles * a.kblocks;
             u = (uint32_t)(U * blockIdx.x / gridDim.x);
             u1 = (uint32_t)(U * (blockIdx.x + 1) / gridDim.x);
+        } else if (mode == 2) {  // split-K: one of a tile's nsplit equal block ranges
+            u = blockIdx.x;
+            u1 = blockIdx.x < a.ntiles * nsplit ? blockIdx.x + 1 : blockIdx.x;
         } else {
             u = blockIdx.x;
             u1 = a.ntiles;
@@ -178,11 +181,17 @@ struct SegWalk {
     __device__ __forceinline__ bool next(uint32_t &tile, uint32_t &kb0, uint32_t &kb1)
     {
         if (u >= u1) return false;
-        if (sk) {
+        if (mode == 1) {
             tile = u / nkb;
             kb0 = u % nkb;
             kb1 = nkb - kb0 < u1 - u ? nkb : kb0 + (u1 - u);
             u += kb1 - kb0;
+        } else if (mode == 2) {
+            tile = u / nsplit;
+            const uint32_t part = u % nsplit;
+            kb0 = part * nkb / nsplit;
+            kb1 = (part + 1) * nkb / nsplit;
+            u = u1;
         } else {
             tile = u;
             kb0 = 0;
@@ -192,6 +201,23 @@ struct SegWalk {
         return true;
     }
 };
+
+// Where a cut tile's segments meet: the scratch slot, this CTA's segment in
+// it and the number of segments.  Stream-K: slot = the tile's first inner
+// CTA boundary c1, segment = CTA - (c1 - 1); split-K: slot = the tile,
+// segment = its part.
+struct SkSlot {
+    uint32_t slot, seg, nseg;
+};
+__device__ __forceinline__ SkSlot sk_slot(const GemmArgs &a, uint32_t tile)
+{
+    const uint32_t nkb = a.kblocks;
+    if (a.sk == 2) return SkSlot{tile, blockIdx.x % a.maxseg, a.maxseg};
+    const uint64_t U = (uint64_t)a.ntiles * nkb;
+    const uint32_t c1 = (uint32_t)((((uint64_t)tile * nkb + 1) * gridDim.x + U - 1) / U);
+    const uint32_t cl = (uint32_t)(((uint64_t)(tile + 1) * nkb * gridDim.x + U - 1) / U) - 1;
+    return SkSlot{c1, blockIdx.x + 1 - c1, cl - c1 + 2};
+}
 
 // (row block, token tile) of tile index `tile`.  Token tiles are walked in
 // groups of gm: inside a group its token tiles go fastest, then the row
@@ -708,12 +734,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kSK && (kb0 != 0 || kb1 != nkb)) {
                     // stream-K: this CTA's share of a cut tile.  Slot c1 = the
                     // tile's first inner CTA boundary, segment j = CTA - (c1 - 1).
-                    const uint64_t U = (uint64_t)a.ntiles * nkb;
-                    const uint32_t c1 = (uint32_t)((((uint64_t)tile * nkb + 1) * gridDim.x + U - 1) / U);
-                    const uint32_t cl = (uint32_t)(((uint64_t)(tile + 1) * nkb * gridDim.x + U - 1) / U) - 1;
-                    float *slot0 = a.skpart + (size_t)c1 * a.maxseg * BN * kBM;
+                    const SkSlot ss = sk_slot(a, tile);
+                    float *slot0 = a.skpart + (size_t)ss.slot * a.maxseg * BN * kBM;
                     if (ok) {
-                        float *sl = slot0 + (size_t)(blockIdx.x + 1 - c1) * BN * kBM + (size_t)grp * 64 * kBM + row;
+                        float *sl = slot0 + (size_t)ss.seg * BN * kBM + (size_t)grp * 64 * kBM + row;
 #pragma unroll
                         for (int i = 0; i < 64; ++i)
                             if (i < ncol) sl[(size_t)i * kBM] = acc[i];
@@ -725,11 +749,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t st_ = 0;
                         if (*abort == 0 && *epi_aborts == 0) {
                             __threadfence();
-                            const uint32_t done_ = atomicAdd(a.skcnt + c1, kb1 - kb0) + (kb1 - kb0);
+                            const uint32_t done_ = atomicAdd(a.skcnt + ss.slot, kb1 - kb0) + (kb1 - kb0);
                             st_ = 1;
                             if (done_ == nkb) {  // the tile's last segment: this CTA stores it
                                 __threadfence();
-                                a.skcnt[c1] = 0;  // ready for the next launch
+                                a.skcnt[ss.slot] = 0;  // ready for the next launch
                                 st_ = 3;
                             }
                         }
@@ -743,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float *sl = slot0 + (size_t)grp * 64 * kBM + row;
 #pragma unroll
                         for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-                        for (uint32_t js = 0; js < cl - c1 + 2; ++js, sl += (size_t)BN * kBM) {
+                        for (uint32_t js = 0; js < ss.nseg; ++js, sl += (size_t)BN * kBM) {
 #pragma unroll
                             for (int i = 0; i < 64; ++i)
                                 if (i < ncol) acc[i] += __ldcg(sl + (size_t)i * kBM);
@@ -1042,24 +1066,53 @@ struct SkScratch {
 };
 SkScratch g_sk[64];
 
-// Stream-K for a narrow-tile launch when it cuts the busiest CTA's block
-// count by a tenth or more; fills a's stream-K fields.  false = whole tiles.
+// Work split of a launch with few row tiles, fills a's fields (false =
+// whole tiles).  Three ways, costed in 128-column block periods of the
+// busiest CTA (fitted to B200 timings of multi-token decode: a hand-off of
+// a cut tile -- partials out, fence, counter -- ~4.6 periods; each segment
+// the tile's finishing CTA adds, ~3; CUDA-graph timing, 16 tokens: `down`
+// split-K 31.5 / stream-K 35.6 / whole 52.7 us, 5120x6144 17.8 / 21.3 /
+// 22.6, 1024x5120 17.2 (10 parts) / 15.1 / 18.5):
+//   whole tiles  ceil(tiles / SMs) * K-blocks;
+//   split-K      each tile cut into s = SMs / tiles equal block ranges, one
+//                per CTA: ceil(K-blocks / s) + one hand-off + s additions;
+//   stream-K     equal (tile, block) unit ranges over G = min(SMs, U / 8)
+//                CTAs: a range usually cuts two tiles, so two hand-offs.
+// Q35CU_GEMM_SPLIT = whole | split | streamk forces one (comparison).
 constexpr uint64_t kSkMinBlocks = 8;             // blocks per CTA at least (amortises a cut tile's hand-off)
 constexpr size_t kSkMaxBytes = (size_t)128 << 20;  // scratch cap (48-token e4m3-term tiles: ~91 MB)
+constexpr double kHandoff = 4.6, kSegAdd = 3.0;
 
 // cols: accumulator columns a cut tile hands off (BN of the f16 kernel)
 bool plan_stream_k(GemmArgs &a, uint32_t cols, uint32_t sms, cudaStream_t st, uint32_t *grid)
 {
     if (getenv("Q35CU_GEMM_NO_STREAMK")) return false;
-    const uint64_t U = (uint64_t)a.ntiles * a.kblocks;
-    const uint32_t G = (uint32_t)(U / kSkMinBlocks < sms ? U / kSkMinBlocks : sms);
-    if (G < 2) return false;
-    const uint64_t per = U / G;
-    const uint64_t whole = ((a.ntiles + sms - 1) / sms) * (uint64_t)a.kblocks;
-    const uint64_t sk = (U + G - 1) / G;
-    if (sk * 10 > whole * 9) return false;
-    const uint32_t maxseg = (uint32_t)((a.kblocks + per - 1) / per + 1);
-    const size_t need = kSkCntBytes + (size_t)G * maxseg * cols * kBM * 4;
+    const char *force = getenv("Q35CU_GEMM_SPLIT");
+    const uint64_t nkb = a.kblocks, U = (uint64_t)a.ntiles * nkb;
+    const double whole = (double)((a.ntiles + sms - 1) / sms) * nkb;
+    double best = whole;
+    uint32_t mode = 0, G = 0, maxseg = 0;
+    // split-K: at least 4 blocks per part
+    const uint64_t s_max = a.ntiles ? sms / a.ntiles : 0;
+    const uint64_t s = s_max < nkb / 4 ? s_max : nkb / 4;
+    if (s >= 2 && a.ntiles <= kSkCntBytes / 4) {
+        const double c = (double)((nkb + s - 1) / s) + kHandoff + kSegAdd * s;
+        if (c < best * 0.9) { best = c; mode = 2; G = (uint32_t)(a.ntiles * s); maxseg = (uint32_t)s; }
+    }
+    const uint32_t Gk = (uint32_t)(U / kSkMinBlocks < sms ? U / kSkMinBlocks : sms);
+    if (Gk >= 2) {
+        const uint64_t per = U / Gk;
+        const uint32_t ms = (uint32_t)((nkb + per - 1) / per + 1);
+        const double c = (double)((U + Gk - 1) / Gk) + 2 * kHandoff + kSegAdd * ms;
+        if (c < best * 0.9 || (force && !strcmp(force, "streamk"))) { best = c; mode = 1; G = Gk; maxseg = ms; }
+    }
+    if (force && !strcmp(force, "whole")) mode = 0;
+    if (force && !strcmp(force, "split")) {
+        if (s >= 2 && a.ntiles <= kSkCntBytes / 4) { mode = 2; G = (uint32_t)(a.ntiles * s); maxseg = (uint32_t)s; }
+        else mode = 0;
+    }
+    if (mode == 0) return false;
+    const size_t need = kSkCntBytes + (size_t)(mode == 2 ? a.ntiles : G) * maxseg * cols * kBM * 4;
     if (G * 4 > kSkCntBytes || need > kSkMaxBytes) return false;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
@@ -1079,7 +1132,7 @@ bool plan_stream_k(GemmArgs &a, uint32_t cols, uint32_t sms, cudaStream_t st, ui
         sc.p = p;  // an earlier, smaller scratch stays allocated (graphs may hold it)
         sc.bytes = bytes;
     }
-    a.sk = 1;
+    a.sk = mode;
     a.maxseg = maxseg;
     *grid = G;
     a.skcnt = static_cast<uint32_t *>(sc.p);
@@ -1731,12 +1784,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
             if (kb0 != 0 || kb1 != nkb) {
                 // stream-K: this CTA's share of a cut tile.  Slot c1 = the
                 // tile's first inner CTA boundary, segment = CTA - (c1 - 1).
-                const uint64_t U = (uint64_t)a.ntiles * nkb;
-                const uint32_t c1 = (uint32_t)((((uint64_t)tile * nkb + 1) * gridDim.x + U - 1) / U);
-                const uint32_t cl = (uint32_t)(((uint64_t)(tile + 1) * nkb * gridDim.x + U - 1) / U) - 1;
-                float *slot0 = a.skpart + (size_t)c1 * a.maxseg * C::kSkCols * kBM;
+                const SkSlot ss = sk_slot(a, tile);
+                float *slot0 = a.skpart + (size_t)ss.slot * a.maxseg * C::kSkCols * kBM;
                 if (ok) {
-                    float *sl = slot0 + (size_t)(blockIdx.x + 1 - c1) * C::kSkCols * kBM + (size_t)grp * dec::kColsPerWarp * kBM + row;
+                    float *sl = slot0 + (size_t)ss.seg * C::kSkCols * kBM + (size_t)grp * dec::kColsPerWarp * kBM + row;
 #pragma unroll
                     for (int i = 0; i < dec::kColsPerWarp; ++i) sl[(size_t)i * kBM] = acc[i];
                 } else if (lane == 0) {
@@ -1747,11 +1798,11 @@ __global__ void __launch_bounds__(C::kThreads, 1)
                     uint32_t st_ = 0;
                     if (*abort == 0 && *epi_aborts == 0) {
                         __threadfence();
-                        const uint32_t done_ = atomicAdd(a.skcnt + c1, kb1 - kb0) + (kb1 - kb0);
+                        const uint32_t done_ = atomicAdd(a.skcnt + ss.slot, kb1 - kb0) + (kb1 - kb0);
                         st_ = 1;
                         if (done_ == nkb) {  // the tile's last segment: this CTA stores it
                             __threadfence();
-                            a.skcnt[c1] = 0;  // ready for the next launch
+                            a.skcnt[ss.slot] = 0;  // ready for the next launch
                             st_ = 3;
                         }
                     }
@@ -1765,7 +1816,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
                     const float *sl = slot0 + (size_t)grp * dec::kColsPerWarp * kBM + row;
 #pragma unroll
                     for (int i = 0; i < dec::kColsPerWarp; ++i) acc[i] = 0.f;
-                    for (uint32_t js = 0; js < cl - c1 + 2; ++js, sl += (size_t)C::kSkCols * kBM) {
+                    for (uint32_t js = 0; js < ss.nseg; ++js, sl += (size_t)C::kSkCols * kBM) {
 #pragma unroll
                         for (int i = 0; i < dec::kColsPerWarp; ++i) acc[i] += __ldcg(sl + (size_t)i * kBM);
                     }

@@ -372,6 +372,25 @@ def test_cache_detects_reused_address(gpu, orc):
     assert not np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("kernel", ["e4m3", "f16"])
+@pytest.mark.parametrize("mode", ["split", "streamk", "whole"])
+@pytest.mark.parametrize("rows,cols,n", [(5120, 17408, 16), (5120, 6144, 40), (1024, 5120, 32)])
+def test_tensor_core_decode_work_splits(gpu, orc, ref, monkeypatch, kernel, mode, rows, cols, n):
+    """Each way of dividing a few-tile decode launch among the CTAs --
+    split-K (each tile's blocks cut into equal ranges, one per CTA),
+    stream-K (equal unit ranges) and whole tiles -- with either kernel:
+    within the GEMV bound and repeating bit for bit."""
+    monkeypatch.setenv("Q35CU_GEMM_SPLIT", mode)
+    if kernel == "f16":
+        monkeypatch.setenv("Q35CU_GEMV_TC_F16", "1")
+    W, sc = _synth(orc, 2700 + rows + n, rows, cols)
+    X = orc.synth_act(2800 + n, (n, cols))
+    Y1 = q35cu.mm_fp8_batch(W, sc, X)
+    Y2 = q35cu.mm_fp8_batch(W, sc, X)
+    assert np.array_equal(Y1.view(np.uint32), Y2.view(np.uint32))
+    _check(orc, W, sc, X, Y1, ref.mm_fp8_batch(W, sc, X), f"{kernel} {mode} {rows}x{cols} n={n}")
+
+
 @pytest.mark.parametrize("rows,cols,n", [(5120, 17408, 16), (5120, 6144, 33), (5120, 6144, 64), (1024, 5120, 40)])
 def test_stream_k_tensor_core_decode(gpu, orc, ref, monkeypatch, rows, cols, n):
     """Multi-token decode on the tensor cores with few row tiles walks equal

@@ -346,40 +346,59 @@ def gemv_bytes(rows, cols, m=1):
     return rows * cols + 4 * ((rows + 127) // 128) * ((cols + 127) // 128) + 4 * m * (rows + cols)
 
 
-def time_gemv_rotating(q35cu, torch, rows, cols, m, copies=5, rounds=20, path="gemv"):
+def time_gemv_rotating(q35cu, torch, rows, cols, m, copies=5, rounds=20, path="gemv", graph=False):
     """Isolated GEMV: `copies` distinct weights cycled so none is L2-resident.
     path "gemv": the CUDA-core decode GEMV (q35cu_gemv_fp8); "tc": the tensor
     cores with exact fp32 activations (q35cu_gemv_fp8_tc, the path
-    q35_mm_fp8_batch takes for 16..127 tokens)."""
+    q35_mm_fp8_batch takes for 16..127 tokens).  graph: one call per weight
+    captured in a CUDA graph and replayed (device time without the Python
+    and launch overhead of eager calls)."""
     ws = [q35cu.Weight.synth_fp8(1000 + i, rows, cols) for i in range(copies)]
     try:
         X = torch.randn((m, cols), device="cuda")
         Y = torch.empty((m, rows), device="cuda")
         work = torch.empty(q35cu.load().q35cu_gemv_fp8_tc_workspace_bytes(m, cols), dtype=torch.uint8, device="cuda")
 
-        def call(w):
+        def call(w, stream=None):
             if path == "tc":
-                q35cu.gemv_tc(w, X, Y, work)
+                q35cu.gemv_tc(w, X, Y, work, stream)
             else:
-                q35cu.gemv(w, X, Y, m)
+                q35cu.gemv(w, X, Y, m, stream)
 
         for w in ws:
-            call(w)
+            call(w)  # eager first: the multi-token path allocates its split scratch here
         torch.cuda.synchronize()
+        g = None
+        if graph:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    for w in ws:
+                        call(w, s)
+            torch.cuda.current_stream().wait_stream(s)
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(rounds):
-            for w in ws:
-                call(w)
+            if g is not None:
+                g.replay()
+            else:
+                for w in ws:
+                    call(w)
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (rounds * copies)
+        del g
     finally:
         for w in ws:
             w.free()
     b = gemv_bytes(rows, cols, m)
-    return {"rows": rows, "cols": cols, "m": m, "path": path, "us": round(us, 2), "GBps": round(b / us / 1e3, 1),
-            "TFLOPs": round(2 * m * rows * cols / us / 1e6, 3)}
+    return {"rows": rows, "cols": cols, "m": m, "path": path, "timing": "cuda graph" if graph else "eager",
+            "us": round(us, 2), "GBps": round(b / us / 1e3, 1), "TFLOPs": round(2 * m * rows * cols / us / 1e6, 3)}
 
 
 def bf16_weight(q35cu, torch, rows, cols, seed=4242):
@@ -703,10 +722,12 @@ def run_extra(args) -> int:
         elif args.extra == "c1":
             r = []
             for rows, cols in ((17408, 5120), (5120, 17408)):
-                for m in (1, 4, 16, 64):
-                    r.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10))
+                for m in (1, 4, 16, 32, 48, 64):
+                    if m < 16 or m == 64:
+                        r.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10))
                     if m >= 16:  # what q35_mm_fp8_batch runs at this size
-                        r.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10, path="tc"))
+                        r.append(time_gemv_rotating(q35cu, torch, rows, cols, m, copies=3, rounds=10, path="tc",
+                                                    graph=True))
         elif args.extra == "lm_head":
             r = time_lm_head(q35cu, torch, hbm_peak)
         elif args.extra == "c2":

@@ -334,36 +334,45 @@ int weight_fill_fp8(q35cu_weight *w, const uint8_t *W, const uint16_t *sc, uint3
     return Q35CU_OK;
 }
 
-// Content fingerprint of a host weight: the whole scale grid (up to 64 KB)
-// plus 16 evenly spaced 8-byte words of W.  A cache hit whose fingerprint
-// differs (the caller freed the tensor and reused the address for another
-// one) is treated as a miss.  Q35CU_CACHE_CHECK=0 skips the check.
+// Content fingerprint of a host weight: 64 evenly spaced 8-byte words of
+// the scale grid (all of it when smaller) and 8 of W, hashed in four
+// independent lanes.  A cache hit whose fingerprint differs (the caller
+// freed the tensor and reused the address for another one, whose scales
+// differ almost everywhere) is treated as a miss.  It runs on every host
+// call, so it reads few bytes: hashing a whole 11 KB scale grid took ~3 us
+// a call.  Q35CU_CACHE_CHECK=0 skips the check.
 uint64_t fingerprint(const void *W, size_t wbytes, const void *S, size_t sbytes)
 {
-    uint64_t h = 0x9E3779B97F4A7C15ULL ^ wbytes;
-    auto mix = [&h](uint64_t v) {
-        h ^= v;
-        h *= 0xFF51AFD7ED558CCDULL;
-        h ^= h >> 32;
+    uint64_t h[4] = {0x9E3779B97F4A7C15ULL ^ wbytes, 0xC2B2AE3D27D4EB4FULL ^ sbytes, 0x165667B19E3779F9ULL,
+                     0x27D4EB2F165667C5ULL};
+    auto mix = [](uint64_t &x, uint64_t v) {
+        x ^= v;
+        x *= 0xFF51AFD7ED558CCDULL;
+        x ^= x >> 32;
     };
-    const uint8_t *s = static_cast<const uint8_t *>(S);
-    if (sbytes > 65536) sbytes = 65536;
-    size_t i = 0;
-    for (; i + 8 <= sbytes; i += 8) {
-        uint64_t v;
-        memcpy(&v, s + i, 8);
-        mix(v);
-    }
-    for (; i < sbytes; ++i) mix(s[i]);
-    const uint8_t *w = static_cast<const uint8_t *>(W);
-    const size_t take = wbytes < 8 ? wbytes : 8;
-    for (int j = 0; j < 16; ++j) {
-        const size_t off = wbytes <= 8 ? 0 : (wbytes - 8) * j / 15;
+    auto word = [](const uint8_t *base, size_t bytes, size_t off) {
         uint64_t v = 0;
-        memcpy(&v, w + off, take);
-        mix(v);
+        memcpy(&v, base + off, bytes - off < 8 ? bytes - off : 8);
+        return v;
+    };
+    const uint8_t *sp = static_cast<const uint8_t *>(S);
+    if (sbytes) {
+        const size_t nw = (sbytes + 7) / 8, take = nw < 64 ? nw : 64;
+        for (size_t j = 0; j < take; ++j) {
+            const size_t wi = take == nw ? j : (nw - 1) * j / (take - 1);
+            mix(h[j & 3], word(sp, sbytes, wi * 8));
+        }
     }
-    return h;
+    const uint8_t *wp = static_cast<const uint8_t *>(W);
+    if (wbytes) {
+        for (int j = 0; j < 8; ++j) {
+            const size_t off = wbytes <= 8 ? 0 : ((wbytes - 8) * j / 7) & ~(size_t)7;
+            mix(h[j & 3], word(wp, wbytes, off));
+        }
+    }
+    uint64_t r = h[0];
+    for (int i = 1; i < 4; ++i) mix(r, h[i]);
+    return r;
 }
 
 bool cache_check_enabled()

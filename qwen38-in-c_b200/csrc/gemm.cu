@@ -1,13 +1,23 @@
-// Tensor-core prefill GEMM (M >= 128 tokens), sm_100a: TMA + tcgen05 + TMEM.
+// Tensor-core GEMMs of q35_mm_fp8_batch, sm_100a: TMA + tcgen05 + TMEM.
 //
 // Replaces the CPU loop of q35_mm_fp8_batch (qwen35-c/src/q35_mm.c:158-172)
-// for prefill-sized batches.  Y[t, n] = sum_k xb[t, k] * e4m3(W[n, k]) * s[n/128, k/128]
-// with xb = bf16(X) (the prefill contract: relative L2 error <= 5e-3 against
-// the reference on the same bf16-valued activations).
+// for batches of 16 tokens or more.  Y[t, n] = sum_k x[t, k] * e4m3(W[n, k])
+// * s[n/128, k/128].  Three kernels, each promoting every 128-column block's
+// fp32 partial with its scale in registers:
+//   * gemm_e4m3_tc_kernel -- prefill (M >= 128, activations rounded to bf16,
+//     the contract: relative L2 <= 5e-3): e4m3 weights x a two-term e4m3
+//     split of the activations, block-scaled MMAs (section further down);
+//   * gemm_dec_kernel -- multi-token decode, 16..48 tokens of exact fp32
+//     activations (the GEMV bound): e4m3 weights x five e4m3 terms per token;
+//   * gemm_fp8_tc_kernel (below) -- f16 operands: the weight converted
+//     e4m3 -> f16 into TMEM; decode of 49..127 tokens on hi/lo-split fp32
+//     activations, and prefill when Q35CU_GEMM_F16 is set.
+// Few row tiles (decode): split-K or stream-K, chosen by plan_stream_k.
 //
-// Roofline: tensor cores.  2*M*N*K flops per launch.
+// Roofline: tensor cores for prefill (2*M*N*K flops per launch); HBM for
+// decode (each weight byte once per launch).
 //
-// Operands are f16 on the tensor cores (kind::f16, both operands f16):
+// The f16-operand kernel: both operands f16 on the tensor cores (kind::f16):
 //   * every e4m3 value is an f16 value, so a weight tile converts exactly with
 //     one cvt.rn.f16x2.e4m3x2 per two elements (bf16 would need four
 //     instructions per two: e4m3 -> f16 -> f32 -> bf16);
@@ -1255,7 +1265,7 @@ struct Cfg {
     // scale-factor byte 0 (bits 29-30), K = 32 (bit 31 = 0).  D is fp32.
     static constexpr uint32_t kIdesc = ((uint32_t)(kBN >> 3) << 17) | (1u << 23) | ((uint32_t)(kBM >> 4) << 24);
     static_assert(kBN % 16 == 0 && kBN <= 256, "M = 128 MMAs take N = 16..256 in steps of 16");
-    static_assert(kBN % kEpiCols == 0 && kEpiCols % 32 == 0 && (kEarly || kEpiCols % 32 == 0), "epilogue columns");
+    static_assert(kBN % kEpiCols == 0 && kEpiCols % 16 == 0, "epilogue columns: whole 16-column loads");
     // full, empty [S]; tfull, tempty [D]; fin [2]; abort flag; TMEM address
     static_assert((2 * kS + 2 * kD + 2) * 8 + 8 <= 256, "barriers fit their 256 bytes");
     static_assert(kSfB1 + 8 <= kTmemCols, "TMEM budget");
@@ -1268,6 +1278,8 @@ constexpr uint32_t kUe8m0One = 0x7F7F7F7Fu, kUe8m0Sixteenth = 0x7B7B7B7Bu;  // 2
 // 4 stages, 3 accumulators and 20 early-releasing epilogue warps of 32
 // columns -- 1034 vs 1067 TFLOP/s at M = 2048, 1053 vs 1110 at M = 8192
 // (faster only on gate / up at M = 2048: 1174 vs 1113).
+// 16 epilogue warps of 48 columns: 1066-1072 vs 1088-1091 TFLOP/s at
+// M = 2048, 1103-1122 vs 1135-1137 at M = 8192 (same box).
 using Wide = Cfg<192, 3, 2, 64, false>;
 }  // namespace e4
 
@@ -1443,6 +1455,13 @@ __global__ void __launch_bounds__(C::kThreads, 1)
                         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                         promote16(acc + 32 * c, p0, sc, kb == 0);
                         promote16(acc + 32 * c + 16, p1, sc, kb == 0);
+                    }
+                    if constexpr (C::kEpiCols % 32 != 0) {  // a last 16 columns
+                        constexpr int c0 = C::kEpiCols - 16;
+                        uint32_t p0[16];
+                        tmem_ld16(tbase + j * C::kBN + c0, p0);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        promote16(acc + c0, p0, sc, kb == 0);
                     }
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     __syncwarp();

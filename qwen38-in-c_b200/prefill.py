@@ -52,10 +52,11 @@ class PrefillLayers:
         # Under TP the collectives run beside the GEMMs, which are persistent
         # (one CTA per SM): a GEMM CTA whose SM a collective holds starts late
         # and holds up its tiles.  The literal scheme, whose all-gathers keep
-        # NCCL busy through most of a layer, leaves NCCL 32 SMs (measured at
-        # TP 2, M = 8192: 347 -> 294 ms per pass); the paired scheme's two
-        # all-reduces per layer cost less than 32 SMs of GEMM (262 ms with
-        # none reserved, 278 with 32).  Q35_PREFILL_RESERVE_SMS overrides.
+        # NCCL busy through most of a layer, leaves NCCL 32 SMs; the paired
+        # scheme's two all-reduces per layer cost less than reserved SMs of
+        # GEMM.  Measured at TP 2, M = 8192, e4m3 GEMM, ms per pass: literal
+        # 337 / 341 / 300 / 314 with 0 / 16 / 32 / 48 reserved, paired 256 /
+        # 259 with 0 / 16.  Q35_PREFILL_RESERVE_SMS overrides.
         default = "32" if scheme == "literal" else "0"
         self.reserve = int(__import__("os").environ.get("Q35_PREFILL_RESERVE_SMS", default)) if st.world > 1 else 0
         self.dn = next(L for L in st.layers if L.kind == "dn")

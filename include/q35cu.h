@@ -134,9 +134,11 @@ int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint32_t ldx
  * the dequantised weight, fp32 accumulation with per-128-K block-scale
  * promotion.  Needs cols % 16 == 0.  The caller provides a device workspace
  * of at least q35cu_gemm_fp8_workspace_bytes(m, cols) bytes (16-byte
- * aligned) for the prepared activations (f16 with a per-token power-of-two
- * scale, which carries every bf16 value exactly); calls on different streams
- * need different workspaces.  The library allocates nothing here. */
+ * aligned) for the prepared activations: two e4m3 terms per value with a
+ * per-token power of two (exact down to 2^-13 of a row's largest magnitude,
+ * within 2^-21 of it below; with Q35CU_GEMM_F16 set, f16 values, exact);
+ * calls on different streams need different workspaces.  The library
+ * allocates nothing here. */
 size_t q35cu_gemm_fp8_workspace_bytes(uint32_t m, uint32_t cols);
 int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m,
                    float *Y, void *workspace, size_t workspace_bytes, void *stream);
@@ -160,13 +162,16 @@ int q35cu_gemm_fp8_f32_noalloc(const q35cu_weight *w, const float *X, uint32_t m
                                float *Y, void *stream);
 /* Multi-token decode on the tensor cores with exact fp32 activations: Y [m,
  * rows] = X [m, cols] fp32 times the dequantised weight.  Each token row is
- * scaled by a power of two and split into two f16 rows (hi = f16(x), lo =
- * f16(x - hi): about 22 bits of x), both multiplied on the tcgen05 GEMM, and
- * summed in the epilogue; the weight streams once per 96 tokens instead of
- * once per 4.  Meets the decode GEMV's per-element bound (guarded 1e-5) but
- * is not bit-identical to q35cu_gemv_fp8.  q35_mm_fp8_batch uses it for
- * batches of 16 (Q35CU_GEMV_TC_MIN_TOKENS) to 127 tokens.  cols % 16 == 0;
- * workspace >= q35cu_gemv_fp8_tc_workspace_bytes(m, cols), 16-byte aligned. */
+ * scaled by a power of two and, up to 48 tokens, split into five e4m3 terms
+ * (to 2^-33 of the row's largest magnitude) multiplied on e4m3 tensor-core
+ * MMAs; above 48 tokens (or with Q35CU_GEMV_TC_F16) into two f16 rows (hi =
+ * f16(x), lo = f16(x - hi): about 22 bits of x).  The term columns are
+ * summed in the epilogue; the weight streams once per token tile instead of
+ * once per 4 tokens.  Meets the decode GEMV's per-element bound (guarded
+ * 1e-5) but is not bit-identical to q35cu_gemv_fp8.  q35_mm_fp8_batch uses
+ * it for batches of 16 (Q35CU_GEMV_TC_MIN_TOKENS) to 127 tokens.  cols % 16
+ * == 0; workspace >= q35cu_gemv_fp8_tc_workspace_bytes(m, cols), 16-byte
+ * aligned. */
 size_t q35cu_gemv_fp8_tc_workspace_bytes(uint32_t m, uint32_t cols);
 int q35cu_gemv_fp8_tc(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
                       size_t workspace_bytes, void *stream);

@@ -142,6 +142,12 @@ int q35cu_multi_fp8(const q35cu_weight *const w[4], const float *X, uint32_t ldx
 size_t q35cu_gemm_fp8_workspace_bytes(uint32_t m, uint32_t cols);
 int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m,
                    float *Y, void *workspace, size_t workspace_bytes, void *stream);
+/* q35cu_gemm_fp8 on fp32 activations X [m, cols] (device memory), rounded
+ * to bf16 (nearest even) as they are prepared: the same results as
+ * converting X to bf16 first and calling q35cu_gemm_fp8, without that
+ * separate pass over X.  Same workspace. */
+int q35cu_gemm_fp8_f32(const q35cu_weight *w, const float *X, uint32_t m,
+                       float *Y, void *workspace, size_t workspace_bytes, void *stream);
 /* The prefill GEMM of q35cu_gemm_fp8 on fp32 activations, for callers that
  * may not have the library allocate device memory and hold no workspace: a
  * serving process that reserved its HBM budget up front, or a loop that

@@ -1040,6 +1040,17 @@ Q35_API int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m
     return launch_gemm_bf16(w, Xb, false, m, Y, workspace, pick(stream));
 }
 
+Q35_API int q35cu_gemm_fp8_f32(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,
+                               size_t workspace_bytes, void *stream)
+{
+    if (!w || w->kind != 0 || !X || !Y) return set_error(Q35CU_ERR_ARG, "gemm_fp8_f32: bad arguments");
+    if (!m) return Q35CU_OK;
+    const size_t need = gemm_workspace_bytes(m, w->cols);
+    if (!workspace || workspace_bytes < need)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8_f32: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    return launch_gemm_bf16(w, X, true, m, Y, workspace, pick(stream));
+}
+
 Q35_API int q35cu_gemm_reserve_sms(int n) { return gemm_reserve_sms(n); }
 
 Q35_API int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream)

@@ -8,15 +8,17 @@ layer here issues the same projections, in the same order, on the weights of
 a ``stack.Stack`` (this rank's tensor-parallel shards):
 
   DeltaNet: qkv, z = GEMM(x)           column-parallel
-            o = GEMM_out(bf16(z))       row-parallel (the caller-batched out)
+            o = GEMM_out(z)             row-parallel (the caller-batched out)
   GQA:      q, k, v = GEMM(x)           column-parallel
-            o = GEMM_o(bf16(attn))      row-parallel (attn: the local heads'
+            o = GEMM_o(attn)            row-parallel (attn: the local heads'
                                         attention output, a stand-in)
-  MLP:      gate, up = GEMM(bf16(o))    column-parallel
-            y = GEMM_down(bf16(gate))   row-parallel
+  MLP:      gate, up = GEMM(o)          column-parallel
+            y = GEMM_down(gate)         row-parallel
 
-Every GEMM is ``q35cu_gemm_fp8`` (the tcgen05 kernel, bf16 activations, one
-caller workspace).  The recurrence, attention and swiglu arithmetic between
+Every GEMM is the tcgen05 kernel with one caller workspace: on the bf16
+input x through ``q35cu_gemm_fp8``, on the fp32 outputs of earlier
+projections through ``q35cu_gemm_fp8_f32``, which rounds them to bf16 as
+it prepares them (no separate conversion pass).  The recurrence, attention and swiglu arithmetic between
 projections is not part of the matmul path and is not run.
 
 Tensor parallelism (world > 1): "literal" all-gathers each column-parallel
@@ -69,7 +71,6 @@ class PrefillLayers:
         layers = (self.dn, self.gqa)
         kmax = max(max(p.w.cols for p in L.col_in + [L.attn_out, L.gate, L.up, L.down]) for L in layers)
         self.work = torch.empty(q35cu.gemm_workspace_bytes(m, kmax), dtype=torch.uint8, device=dev)
-        self.xb = torch.empty((m * kmax,), dtype=torch.bfloat16, device=dev)
         self.o = torch.empty((m, stack.HIDDEN), **f32)
         self.y = torch.empty((m, stack.HIDDEN), **f32)
         self.col = {p.name: torch.empty((m, p.window[1]), **f32) for L in layers for p in L.col_in}
@@ -90,12 +91,6 @@ class PrefillLayers:
         finally:
             q35cu.check(lib.q35cu_gemm_reserve_sms(0))
 
-    def bf16(self, src, stream=None):
-        """bf16(src) into the shared conversion buffer, as [rows, cols]."""
-        n = src.numel()
-        q35cu.f32_to_bf16(src, self.xb[:n], stream)
-        return self.xb[:n].view(src.shape[0], -1)
-
     def layer(self, L, stream=None, keep=None) -> None:
         """Issue one layer's projections (asynchronous on `stream`, the
         current stream if None; the collectives of a TP run go on the
@@ -111,13 +106,20 @@ class PrefillLayers:
         if self.comm is not None:
             self.comm.wait_stream(cs)  # buffers written before this layer
 
-        def gemm(w, xin, yout, name):
-            """the GEMM slab by slab on cs; the event after each slab"""
+        def gemm(w, xin, yout, name, waits=None):
+            """the GEMM slab by slab on cs (slab i after waits[i], if given);
+            the event after each slab.  An fp32 input is rounded to bf16
+            inside the GEMM's preparation (q35cu_gemm_fp8_f32), with no
+            separate conversion pass."""
+            f32 = xin.dtype == torch.float32
             if keep is not None:
-                keep[name] = xin.clone()
+                keep[name] = xin.to(torch.bfloat16) if f32 else xin.clone()
             evs = []
-            for r in rows:
-                q35cu.gemm(w, xin[r], yout[r], self.work, cs)  # one workspace: slabs in order on cs
+            for i, r in enumerate(rows):
+                if waits is not None:
+                    cs.wait_event(waits[i])
+                # one workspace: slabs in order on cs
+                (q35cu.gemm_f32 if f32 else q35cu.gemm)(w, xin[r], yout[r], self.work, cs)
                 if self.comm is not None:
                     ev = torch.cuda.Event()
                     ev.record(cs)
@@ -145,23 +147,16 @@ class PrefillLayers:
             if literal:
                 exchange(evs, self.col[p.name], self.gath[p.name])
         src = self.col["z"] if L.kind == "dn" else self.attn
-        evs = gemm(L.attn_out.w, self.bf16(src, cs), self.o, L.attn_out.name)
-        xo = self.xb[:self.o.numel()].view(self.m, -1)
-        if self.world > 1:
-            # gate / up of slab i wait for that slab's all-reduce only
-            done = exchange(evs, self.o)
-            for i, r in enumerate(rows):
-                cs.wait_event(done[i])
-                q35cu.f32_to_bf16(self.o[r], xo[r], cs)
-        else:
-            q35cu.f32_to_bf16(self.o, xo, cs)
-        g_evs = gemm(L.gate.w, xo, self.gu["gate"], "gate")
+        evs = gemm(L.attn_out.w, src, self.o, L.attn_out.name)
+        # under TP, gate's slab i waits for that slab's all-reduce only
+        done = exchange(evs, self.o) if self.world > 1 else None
+        g_evs = gemm(L.gate.w, self.o, self.gu["gate"], "gate", done)
         if literal:
             exchange(g_evs, self.gu["gate"], self.gu_g["gate"])
-        u_evs = gemm(L.up.w, xo, self.gu["up"], "up")
+        u_evs = gemm(L.up.w, self.o, self.gu["up"], "up")
         if literal:
             exchange(u_evs, self.gu["up"], self.gu_g["up"])
-        evs = gemm(L.down.w, self.bf16(self.gu["gate"], cs), self.y, "down")
+        evs = gemm(L.down.w, self.gu["gate"], self.y, "down")
         if self.world > 1:
             exchange(evs, self.y)
             cs.wait_stream(self.comm)

@@ -78,6 +78,7 @@ _SIGS = [
     ("q35cu_gemv_fp8_tc_workspace_bytes", C.c_size_t, [_u32, _u32]),
     ("q35cu_gemv_fp8_tc", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
+    ("q35cu_gemm_fp8_f32", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8_f32_noalloc", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
     ("q35cu_f32_to_bf16", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_reserve_sms", C.c_int, [C.c_int]),
@@ -341,6 +342,20 @@ def gemm(w: Weight, Xb, Y, workspace=None, stream=None) -> None:
     assert workspace.numel() * workspace.element_size() >= need
     check(load().q35cu_gemm_fp8(w.h, _ptr(Xb), m, _ptr(Y), _ptr(workspace),
                                 workspace.numel() * workspace.element_size(), _stream(stream)))
+
+
+def gemm_f32(w: Weight, X, Y, workspace=None, stream=None) -> None:
+    """gemm() on fp32 activations X[m, cols] (device), rounded to bf16 as they
+    are prepared: the same results as gemm(w, bf16(X), Y)."""
+    assert X.dtype.itemsize == 4 and X.is_contiguous() and Y.is_contiguous()
+    m = X.shape[0]
+    need = gemm_workspace_bytes(m, w.cols)
+    if workspace is None:
+        import torch
+        workspace = torch.empty(need, dtype=torch.uint8, device=X.device)
+    assert workspace.numel() * workspace.element_size() >= need
+    check(load().q35cu_gemm_fp8_f32(w.h, _ptr(X), m, _ptr(Y), _ptr(workspace),
+                                    workspace.numel() * workspace.element_size(), _stream(stream)))
 
 
 def gemv_tc(w: Weight, X, Y, workspace=None, stream=None) -> None:

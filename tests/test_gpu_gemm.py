@@ -188,6 +188,29 @@ def test_fp8_and_f16_kernels_agree(gpu, orc, monkeypatch, rows, cols, n):
         w.free()
 
 
+@pytest.mark.parametrize("kernel", ["e4m3", "f16"])
+def test_gemm_f32_input_equals_bf16_input(gpu, orc, monkeypatch, kernel):
+    """q35cu_gemm_fp8_f32 rounds fp32 activations to bf16 while preparing
+    them: the same bits as converting to bf16 first and calling
+    q35cu_gemm_fp8, with either kernel."""
+    import torch
+
+    if kernel == "f16":
+        monkeypatch.setenv("Q35CU_GEMM_F16", "1")
+    w = q35cu.Weight.synth_fp8(97, 1024, 2048)
+    try:
+        X = torch.from_numpy(orc.synth_act(98, (300, 2048))).cuda()
+        Y1 = torch.empty((300, 1024), device="cuda")
+        Y2 = torch.empty_like(Y1)
+        q35cu.gemm_f32(w, X, Y1)
+        q35cu.gemm(w, X.to(torch.bfloat16).view(torch.int16), Y2)
+        torch.cuda.synchronize()
+        q35cu.check_device_status()
+        assert torch.equal(Y1, Y2)
+    finally:
+        w.free()
+
+
 def test_gemm_nonfinite_activation(gpu, orc, monkeypatch):
     """A token holding an infinity or a NaN gets non-finite outputs (the fp8
     kernel: NaN); every other token is unchanged."""

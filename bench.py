@@ -499,6 +499,11 @@ C2_SHAPES = [("qkv", 10240, 5120), ("z", 6144, 5120), ("out", 5120, 6144), ("q",
              ("up", 17408, 5120), ("down", 5120, 17408)]
 
 
+# projections of one layer that multiply the same activations (DeltaNet
+# input, attention input, MLP input); out, o and down each read their own
+C2_GROUPS = [("qkv", "z"), ("q", "k", "v"), ("gate", "up"), ("out",), ("o",), ("down",)]
+
+
 def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
     """Configuration 2: one decoder layer's projections at M=2048 tokens through
     the tensor-core GEMM (device API, bf16-rounded activations resident in HBM)."""
@@ -529,10 +534,35 @@ def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
             per[n] = {"rows": w.rows, "cols": w.cols, "us": round(dt * 1e6, 1), "TFLOPs": round(fl / dt / 1e12, 1)}
             tot_f += fl
             tot_t += dt
+        # the projections that read one input, as one q35cu_gemm_fp8_multi call each
+        byname = dict(ws)
+        fused, fz_t = {}, 0.0
+        for grp in C2_GROUPS:
+            gw = [byname[n] for n in grp]
+            ys = [torch.empty((m, w.rows), device="cuda") for w in gw]
+            x = xs[gw[0].cols].view(torch.int16)
+            for _ in range(3):
+                q35cu.gemm_multi(gw, x, ys, work)
+            torch.cuda.synchronize()
+            evs = []
+            for _ in range(reps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                q35cu.gemm_multi(gw, x, ys, work)
+                e1.record()
+                evs.append((e0, e1))
+            torch.cuda.synchronize()
+            dt = sum(a.elapsed_time(b) for a, b in evs) * 1e-3 / reps
+            fl = sum(2.0 * m * w.rows * w.cols for w in gw)
+            fused["|".join(grp)] = {"us": round(dt * 1e6, 1), "TFLOPs": round(fl / dt / 1e12, 1)}
+            fz_t += dt
+        q35cu.check_device_status()
     finally:
         for _, w in ws:
             w.free()
     ach = tot_f / tot_t / 1e12
+    fz = tot_f / fz_t / 1e12
     return {"m": m, "flops": tot_f, "ms": round(tot_t * 1e3, 3), "TFLOPs": round(ach, 1),
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": bf16_peak, "unit": "TFLOP/s",
                          "frac": round(ach / bf16_peak, 4),
@@ -540,7 +570,12 @@ def time_prefill_c2(q35cu, torch, bf16_peak, m=2048, reps=5):
                                     else "gemm_prep_e4m3_kernel + gemm_e4m3_tc_kernel (e4m3 operands)")
                          + " -- one q35cu_gemm_fp8 call, L2 flushed before each",
                          "peak_source": "measured bf16_tflops (burst, MEASURED_PEAKS.json)"},
-            "by_projection": per}
+            "by_projection": per,
+            "fused_by_input": {"ms": round(fz_t * 1e3, 3), "TFLOPs": round(fz, 1),
+                               "frac": round(fz / bf16_peak, 4),
+                               "note": "projections that read the same input in one q35cu_gemm_fp8_multi call "
+                                       "(one preparation, one launch over their row blocks); L2 flushed before each",
+                               "by_group": fused}}
 
 
 # ---------------------------------------------------------------------------

@@ -148,6 +148,17 @@ int q35cu_gemm_fp8(const q35cu_weight *w, const uint16_t *Xb, uint32_t m,
  * separate pass over X.  Same workspace. */
 int q35cu_gemm_fp8_f32(const q35cu_weight *w, const float *X, uint32_t m,
                        float *Y, void *workspace, size_t workspace_bytes, void *stream);
+/* Up to four prefill GEMMs on the same activations, as one: weight i (all
+ * nw of them with the same cols) times X into Y[i] [m, rows_i], with one
+ * preparation of X and one persistent launch over the weights' row blocks
+ * together -- the projections that read one input (q | k | v, gate | up,
+ * qkv | z) fill the GPU where a small one alone would not.  X [m, cols] is
+ * bf16 bits (x_f32 = 0) or fp32 (x_f32 = 1, rounded to bf16).  Results are
+ * those of q35cu_gemm_fp8 / q35cu_gemm_fp8_f32 weight by weight, bit for
+ * bit.  nw in 1..4; same workspace as q35cu_gemm_fp8 (m, cols). */
+int q35cu_gemm_fp8_multi(const q35cu_weight *const *w, uint32_t nw, const void *X, int x_f32,
+                         uint32_t m, float *const *Y, void *workspace, size_t workspace_bytes,
+                         void *stream);
 /* The prefill GEMM of q35cu_gemm_fp8 on fp32 activations, for callers that
  * may not have the library allocate device memory and hold no workspace: a
  * serving process that reserved its HBM budget up front, or a loop that

@@ -1044,9 +1044,9 @@ uint32_t raster_group(uint32_t mtiles, uint32_t bn, uint32_t K)
 
 // launch a GEMM kernel as the programmatic dependent of the preparation
 // kernel just issued on st
-template <typename Kern>
+template <typename Kern, typename W>
 int launch_after_prep(Kern k, uint32_t grid, uint32_t threads, size_t smem, cudaStream_t st,
-                      const CUtensorMap &mx, const CUtensorMap &mw, const GemmArgs &a)
+                      const CUtensorMap &mx, const W &mw, const GemmArgs &a)
 {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
@@ -1281,6 +1281,30 @@ constexpr uint32_t kUe8m0One = 0x7F7F7F7Fu, kUe8m0Sixteenth = 0x7B7B7B7Bu;  // 2
 // 16 epilogue warps of 48 columns: 1066-1072 vs 1088-1091 TFLOP/s at
 // M = 2048, 1103-1122 vs 1135-1137 at M = 8192 (same box).
 using Wide = Cfg<192, 3, 2, 64, false>;
+
+// The weights of one launch: up to kMaxSeg weights with the same K that
+// multiply the same activations.  Their row blocks are concatenated --
+// segment i owns row blocks [rb0[i], rb0[i+1]) of the launch's tile grid --
+// and each has its own tensor map, scales, output and row count, so weights
+// that share an input (q | k | v, gate | up) fill the GPU as one GEMM.
+constexpr int kMaxSeg = 4;
+struct Segs {
+    CUtensorMap w[kMaxSeg];
+    const float *S[kMaxSeg];  // [ceil(N/128), kblocks]
+    float *Y[kMaxSeg];        // [m, N]
+    uint32_t N[kMaxSeg];
+    uint32_t rb0[kMaxSeg + 1];
+    uint32_t nseg;
+};
+// the segment of launch row block rb: the number of later segments' first
+// row blocks at or below it
+__device__ __forceinline__ uint32_t seg_of(const Segs &s, uint32_t rb)
+{
+    uint32_t i = 0;
+#pragma unroll
+    for (int j = 1; j < kMaxSeg; ++j) i += ((uint32_t)j < s.nseg && rb >= s.rb0[j]) ? 1u : 0u;
+    return i;
+}
 }  // namespace e4
 
 // D[tmem] (+)= (A * sfa)[smem descriptor] * (B * sfb)[smem descriptor], e4m3 x e4m3 -> f32
@@ -1303,7 +1327,7 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, uint32_t v)
 
 template <class C>
 __global__ void __launch_bounds__(C::kThreads, 1)
-    gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+    gemm_e4m3_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ e4::Segs sg,
                         const __grid_constant__ GemmArgs a)
 {
     constexpr uint32_t kFull = 0xffffffffu;
@@ -1367,8 +1391,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
         for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
             uint32_t rb_, mt_;
             tile_rc(tile, a, rb_, mt_);
+            const uint32_t si = e4::seg_of(sg, rb_);
+            const CUtensorMap *map_w = &sg.w[si];
             const int m0 = (int)(mt_ * C::kBN);
-            const int n0 = (int)(rb_ * kBM);
+            const int n0 = (int)((rb_ - sg.rb0[si]) * kBM);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
                 const int s = g % C::kS;
                 if (g >= (uint32_t)C::kS)
@@ -1378,7 +1404,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
                 bar_expect(&full[s], C::kStage, leader);
                 tma_2d(stage, &map_x, (int)(kb * kBK), m0, &full[s], leader);                          // t0
                 tma_2d(stage + C::kXTile, &map_x, (int)(kb * kBK), (int)a.m + m0, &full[s], leader);  // t1
-                tma_2d(stage + 2 * C::kXTile, &map_w, (int)(kb * kBK), n0, &full[s], leader);
+                tma_2d(stage + 2 * C::kXTile, map_w, (int)(kb * kBK), n0, &full[s], leader);
             }
         }
         drain(full, C::kS, g);
@@ -1423,9 +1449,12 @@ __global__ void __launch_bounds__(C::kThreads, 1)
         for (uint32_t tile = blockIdx.x; ok && tile < a.ntiles; tile += gridDim.x) {
             uint32_t rb, mt;
             tile_rc(tile, a, rb, mt);
-            const uint32_t n = rb * kBM + quad * 32 + lane;                   // weight row
-            const uint32_t tok0 = mt * C::kBN + grp * C::kEpiCols;                    // first token
-            const float *srow = a.S + (size_t)rb * nkb;
+            const uint32_t si = e4::seg_of(sg, rb);
+            const uint32_t lrb = rb - sg.rb0[si], N = sg.N[si];
+            float *const Y = sg.Y[si];
+            const uint32_t n = lrb * kBM + quad * 32 + lane;         // weight row
+            const uint32_t tok0 = mt * C::kBN + grp * C::kEpiCols;  // first token
+            const float *srow = sg.S[si] + (size_t)lrb * nkb;
             float acc[C::kEpiCols];
             float sc = __ldg(srow);
             for (uint32_t kb = 0; kb < nkb; ++kb, ++g) {
@@ -1469,11 +1498,11 @@ __global__ void __launch_bounds__(C::kThreads, 1)
                 }
                 sc = sc_next;
             }
-            if (ok && n < a.N) {
+            if (ok && n < N) {
 #pragma unroll
                 for (int i = 0; i < C::kEpiCols; ++i) {
                     const uint32_t tok = tok0 + i;
-                    if (tok < a.m) a.Y[(size_t)tok * a.N + n] = acc[i] * __ldg(a.tscale + tok);
+                    if (tok < a.m) Y[(size_t)tok * N + n] = acc[i] * __ldg(a.tscale + tok);
                 }
             }
         }
@@ -1553,19 +1582,37 @@ __global__ void __launch_bounds__(kPrepThreads) gemm_prep_e4m3_kernel(const void
     if (threadIdx.x == 0) tscale[row] = __uint_as_float((uint32_t)(127 + e) << 23);
 }
 
+// One launch over nw weights (1..e4::kMaxSeg) of the same K that multiply
+// the prepared activations Xq / tscale: weight i into Y[i] [m, rows_i].
 template <class C>
-int launch_gemm_e4m3_cfg(const q35cu_weight *w, const uint8_t *Xq, const float *tscale, uint32_t m, float *Y,
-                         cudaStream_t st)
+int launch_gemm_e4m3_cfg(const q35cu_weight *const *w, float *const *Y, uint32_t nw, const uint8_t *Xq,
+                         const float *tscale, uint32_t m, cudaStream_t st)
 {
-    const uint32_t N = w->rows, K = w->cols;
-    const uint64_t mtiles = (m + C::kBN - 1) / C::kBN, ntiles = mtiles * ((N + kBM - 1) / kBM);
+    if (nw < 1 || nw > (uint32_t)e4::kMaxSeg) return set_error(Q35CU_ERR_ARG, "gemm_fp8: %u weights in one launch", nw);
+    const uint32_t K = w[0]->cols;
+    const uint64_t mtiles = (m + C::kBN - 1) / C::kBN;
+    e4::Segs sg{};
+    uint64_t rbs = 0;
+    for (uint32_t i = 0; i < nw; ++i) {
+        if (w[i]->cols != K) return set_error(Q35CU_ERR_ARG, "gemm_fp8: weights of %u and %u columns", K, w[i]->cols);
+        if ((uintptr_t)w[i]->d_w % 16) return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned weight");
+        const int rc = make_map(&sg.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w[i]->d_w, K, w[i]->rows, K, 128, kBM);
+        if (rc) return rc;
+        sg.S[i] = w[i]->d_s;
+        sg.Y[i] = Y[i];
+        sg.N[i] = w[i]->rows;
+        sg.rb0[i] = (uint32_t)rbs;
+        rbs += (w[i]->rows + kBM - 1) / kBM;
+    }
+    sg.nseg = nw;
+    for (uint32_t i = nw; i <= (uint32_t)e4::kMaxSeg; ++i) sg.rb0[i] = (uint32_t)rbs;
+    const uint64_t ntiles = mtiles * rbs;
     if (ntiles > 0x7FFFFFFFu || (uint64_t)m * 2 > 0x7FFFFFFFu) return set_error(Q35CU_ERR_ARG, "gemm_fp8: shape too large");
-    CUtensorMap mx, mw;
+    if (!ntiles) return Q35CU_OK;
+    CUtensorMap mx;
     int rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, Xq, K, (uint64_t)m * 2, K, 128, C::kBN);
     if (rc) return rc;
-    rc = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->d_w, K, N, K, 128, kBM);
-    if (rc) return rc;
-    GemmArgs a{w->d_s, tscale, Y, N, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, 0u,
+    GemmArgs a{nullptr, tscale, nullptr, 0u, K, m, (K + kBK - 1) / kBK, (uint32_t)mtiles, (uint32_t)ntiles, 0u,
                0u, 0u, nullptr, nullptr, 0u};
     a.gm = raster_group((uint32_t)mtiles, C::kBN, K);
     static bool configured[64] = {};  // per configuration and device
@@ -1581,13 +1628,13 @@ int launch_gemm_e4m3_cfg(const q35cu_weight *w, const uint8_t *Xq, const float *
         configured[dev] = true;
     }
     const uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
-    return launch_after_prep(gemm_e4m3_tc_kernel<C>, grid, C::kThreads, smem, st, mx, mw, a);
+    return launch_after_prep(gemm_e4m3_tc_kernel<C>, grid, C::kThreads, smem, st, mx, sg, a);
 }
 
-int launch_gemm_e4m3(const q35cu_weight *w, const uint8_t *Xq, const float *tscale, uint32_t m, float *Y,
-                     cudaStream_t st)
+int launch_gemm_e4m3(const q35cu_weight *const *w, float *const *Y, uint32_t nw, const uint8_t *Xq,
+                     const float *tscale, uint32_t m, cudaStream_t st)
 {
-    return launch_gemm_e4m3_cfg<e4::Wide>(w, Xq, tscale, m, Y, st);
+    return launch_gemm_e4m3_cfg<e4::Wide>(w, Y, nw, Xq, tscale, m, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -1967,19 +2014,24 @@ constexpr uint32_t kDecMaxTokens = 48;  // larger batches take the hi/lo kernel
 // the fp8-operand kernel unless Q35CU_GEMM_F16 asks for the f16 one
 bool use_e4m3() { return getenv("Q35CU_GEMM_F16") == nullptr; }
 
-// preparation into acts (2 m K bytes) and ts (m scales), then the GEMM
-int gemm_bf16_into(const q35cu_weight *w, const void *X, bool f32, uint32_t m, float *Y, void *acts, float *ts,
-                   cudaStream_t st)
+// preparation into acts (2 m K bytes) and ts (m scales), then the GEMM of
+// nw weights with the same K: weight i into Y[i]
+int gemm_bf16_multi_into(const q35cu_weight *const *w, float *const *Y, uint32_t nw, const void *X, bool f32,
+                         uint32_t m, void *acts, float *ts, cudaStream_t st)
 {
-    const uint32_t K = w->cols;
+    const uint32_t K = w[0]->cols;
     if (K % 16) return set_error(Q35CU_ERR_UNSUPPORTED, "gemm_fp8: cols %u not a multiple of 16", K);
-    if ((uintptr_t)X % 16 || (uintptr_t)acts % 16 || (uintptr_t)ts % 4 || (uintptr_t)w->d_w % 16)
-        return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned activations, weight or workspace");
-    if (!use_e4m3()) {
+    if ((uintptr_t)X % 16 || (uintptr_t)acts % 16 || (uintptr_t)ts % 4)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned activations or workspace");
+    for (uint32_t i = 0; i < nw; ++i) {
+        if (w[i]->cols != K) return set_error(Q35CU_ERR_ARG, "gemm_fp8: weights of %u and %u columns", K, w[i]->cols);
+        if ((uintptr_t)w[i]->d_w % 16) return set_error(Q35CU_ERR_ARG, "gemm_fp8: misaligned weight");
+    }
+    if (!use_e4m3()) {  // one preparation, a launch per weight
         uint16_t *xh = static_cast<uint16_t *>(acts);
         int rc = launch_gemm_prep(X, f32, m, K, xh, ts, st);
-        if (rc) return rc;
-        return launch_gemm_fp8(w, xh, ts, m, Y, st);
+        for (uint32_t i = 0; !rc && i < nw; ++i) rc = launch_gemm_fp8(w[i], xh, ts, m, Y[i], st);
+        return rc;
     }
     uint8_t *xq = static_cast<uint8_t *>(acts);
     if (f32)
@@ -1988,7 +2040,13 @@ int gemm_bf16_into(const q35cu_weight *w, const void *X, bool f32, uint32_t m, f
         gemm_prep_e4m3_kernel<false><<<m, kPrepThreads, 0, st>>>(X, K, m, xq, ts);
     count_launch();
     Q35CU_CUDA(cudaGetLastError());
-    return launch_gemm_e4m3(w, xq, ts, m, Y, st);
+    return launch_gemm_e4m3(w, Y, nw, xq, ts, m, st);
+}
+
+int gemm_bf16_into(const q35cu_weight *w, const void *X, bool f32, uint32_t m, float *Y, void *acts, float *ts,
+                   cudaStream_t st)
+{
+    return gemm_bf16_multi_into(&w, &Y, 1, X, f32, m, acts, ts, st);
 }
 
 }  // namespace
@@ -2030,6 +2088,15 @@ int launch_gemm_bf16(const q35cu_weight *w, const void *X, bool f32, uint32_t m,
     const size_t need = gemm_workspace_bytes(m, w->cols);
     float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + need - (size_t)m * 4);
     return gemm_bf16_into(w, X, f32, m, Y, workspace, ts, st);
+}
+
+int launch_gemm_bf16_multi(const q35cu_weight *const *w, float *const *Y, uint32_t nw, const void *X, bool f32,
+                           uint32_t m, void *workspace, cudaStream_t st)
+{
+    if (!m) return Q35CU_OK;
+    const size_t need = gemm_workspace_bytes(m, w[0]->cols);
+    float *ts = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + need - (size_t)m * 4);
+    return gemm_bf16_multi_into(w, Y, nw, X, f32, m, workspace, ts, st);
 }
 
 // ---------------------------------------------------------------------------

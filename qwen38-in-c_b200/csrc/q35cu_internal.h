@@ -95,6 +95,10 @@ int launch_gemm_fp8(const q35cu_weight *w, const uint16_t *Xh, const float *tsca
 // (fp8 operands by default; Q35CU_GEMM_F16 selects the f16-operand kernel)
 int launch_gemm_bf16(const q35cu_weight *w, const void *X, bool f32, uint32_t m, float *Y, void *workspace,
                      cudaStream_t st);
+// the same over nw (1..4) weights of equal cols that multiply the same X:
+// one preparation and one launch, weight i into Y[i] [m, rows_i]
+int launch_gemm_bf16_multi(const q35cu_weight *const *w, float *const *Y, uint32_t nw, const void *X, bool f32,
+                           uint32_t m, void *workspace, cudaStream_t st);
 // multi-token decode on the tensor cores, fp32 activations split hi/lo
 size_t gemm_exact_workspace_bytes(uint32_t m, uint32_t K);
 int launch_gemm_exact(const q35cu_weight *w, const float *X, uint32_t m, float *Y, void *workspace,

@@ -1051,6 +1051,23 @@ Q35_API int q35cu_gemm_fp8_f32(const q35cu_weight *w, const float *X, uint32_t m
     return launch_gemm_bf16(w, X, true, m, Y, workspace, pick(stream));
 }
 
+Q35_API int q35cu_gemm_fp8_multi(const q35cu_weight *const *w, uint32_t nw, const void *X, int x_f32, uint32_t m,
+                                 float *const *Y, void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (!w || !X || !Y || nw < 1 || nw > 4) return set_error(Q35CU_ERR_ARG, "gemm_fp8_multi: bad arguments");
+    for (uint32_t i = 0; i < nw; ++i) {
+        if (!w[i] || w[i]->kind != 0 || !Y[i]) return set_error(Q35CU_ERR_ARG, "gemm_fp8_multi: bad weight or output %u", i);
+        if (w[i]->cols != w[0]->cols)
+            return set_error(Q35CU_ERR_ARG, "gemm_fp8_multi: weight %u has %u columns, weight 0 %u", i, w[i]->cols,
+                             w[0]->cols);
+    }
+    if (!m) return Q35CU_OK;
+    const size_t need = gemm_workspace_bytes(m, w[0]->cols);
+    if (!workspace || workspace_bytes < need)
+        return set_error(Q35CU_ERR_ARG, "gemm_fp8_multi: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    return launch_gemm_bf16_multi(w, Y, nw, X, x_f32 != 0, m, workspace, pick(stream));
+}
+
 Q35_API int q35cu_gemm_reserve_sms(int n) { return gemm_reserve_sms(n); }
 
 Q35_API int q35cu_f32_to_bf16(const float *x, uint16_t *y, size_t n, void *stream)

@@ -15,10 +15,11 @@ a ``stack.Stack`` (this rank's tensor-parallel shards):
   MLP:      gate, up = GEMM(o)          column-parallel
             y = GEMM_down(gate)         row-parallel
 
-Every GEMM is the tcgen05 kernel with one caller workspace: on the bf16
-input x through ``q35cu_gemm_fp8``, on the fp32 outputs of earlier
-projections through ``q35cu_gemm_fp8_f32``, which rounds them to bf16 as
-it prepares them (no separate conversion pass).  The recurrence, attention and swiglu arithmetic between
+Every GEMM is the tcgen05 kernel with one caller workspace, through
+``q35cu_gemm_fp8_multi``: the projections that read the same input (qkv | z,
+q | k | v, gate | up) as one preparation and one launch over their row
+blocks together; on the fp32 outputs of earlier projections it rounds them
+to bf16 as it prepares them (no separate conversion pass).  The recurrence, attention and swiglu arithmetic between
 projections is not part of the matmul path and is not run.
 
 Tensor parallelism (world > 1): "literal" all-gathers each column-parallel
@@ -106,20 +107,23 @@ class PrefillLayers:
         if self.comm is not None:
             self.comm.wait_stream(cs)  # buffers written before this layer
 
-        def gemm(w, xin, yout, name, waits=None):
-            """the GEMM slab by slab on cs (slab i after waits[i], if given);
-            the event after each slab.  An fp32 input is rounded to bf16
-            inside the GEMM's preparation (q35cu_gemm_fp8_f32), with no
-            separate conversion pass."""
+        def gemm(ws, xin, youts, names, waits=None):
+            """the GEMMs of weights ws on one input, slab by slab on cs (slab
+            i after waits[i], if given): one q35cu_gemm_fp8_multi call per
+            slab over all of ws (one preparation, one launch).  An fp32 input
+            is rounded to bf16 inside that preparation, with no separate
+            conversion pass.  Returns the event after each slab."""
             f32 = xin.dtype == torch.float32
             if keep is not None:
-                keep[name] = xin.to(torch.bfloat16) if f32 else xin.clone()
+                kx = xin.to(torch.bfloat16) if f32 else xin.clone()
+                for n in names:
+                    keep[n] = kx
             evs = []
             for i, r in enumerate(rows):
                 if waits is not None:
                     cs.wait_event(waits[i])
                 # one workspace: slabs in order on cs
-                (q35cu.gemm_f32 if f32 else q35cu.gemm)(w, xin[r], yout[r], self.work, cs)
+                q35cu.gemm_multi(ws, xin[r], [y[r] for y in youts], self.work, cs)
                 if self.comm is not None:
                     ev = torch.cuda.Event()
                     ev.record(cs)
@@ -142,21 +146,21 @@ class PrefillLayers:
                 done.append(ev)
             return done
 
-        for p in L.col_in:
-            evs = gemm(p.w, self.x, self.col[p.name], p.name)
-            if literal:
+        # the column-parallel projections of x (qkv | z, q | k | v) as one GEMM
+        evs = gemm([p.w for p in L.col_in], self.x, [self.col[p.name] for p in L.col_in],
+                   [p.name for p in L.col_in])
+        if literal:
+            for p in L.col_in:
                 exchange(evs, self.col[p.name], self.gath[p.name])
         src = self.col["z"] if L.kind == "dn" else self.attn
-        evs = gemm(L.attn_out.w, src, self.o, L.attn_out.name)
-        # under TP, gate's slab i waits for that slab's all-reduce only
+        evs = gemm([L.attn_out.w], src, [self.o], [L.attn_out.name])
+        # under TP, the gate | up GEMM's slab i waits for that slab's all-reduce only
         done = exchange(evs, self.o) if self.world > 1 else None
-        g_evs = gemm(L.gate.w, self.o, self.gu["gate"], "gate", done)
+        g_evs = gemm([L.gate.w, L.up.w], self.o, [self.gu["gate"], self.gu["up"]], ["gate", "up"], done)
         if literal:
             exchange(g_evs, self.gu["gate"], self.gu_g["gate"])
-        u_evs = gemm(L.up.w, self.o, self.gu["up"], "up")
-        if literal:
-            exchange(u_evs, self.gu["up"], self.gu_g["up"])
-        evs = gemm(L.down.w, self.gu["gate"], self.y, "down")
+            exchange(g_evs, self.gu["up"], self.gu_g["up"])
+        evs = gemm([L.down.w], self.gu["gate"], [self.y], [L.down.name])
         if self.world > 1:
             exchange(evs, self.y)
             cs.wait_stream(self.comm)

@@ -79,6 +79,7 @@ _SIGS = [
     ("q35cu_gemv_fp8_tc", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8_f32", C.c_int, [_vp, _vp, _u32, _vp, _vp, C.c_size_t, _vp]),
+    ("q35cu_gemm_fp8_multi", C.c_int, [_vp, _u32, _vp, C.c_int, _u32, _vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_fp8_f32_noalloc", C.c_int, [_vp, _vp, _u32, _vp, _vp]),
     ("q35cu_f32_to_bf16", C.c_int, [_vp, _vp, C.c_size_t, _vp]),
     ("q35cu_gemm_reserve_sms", C.c_int, [C.c_int]),
@@ -356,6 +357,24 @@ def gemm_f32(w: Weight, X, Y, workspace=None, stream=None) -> None:
     assert workspace.numel() * workspace.element_size() >= need
     check(load().q35cu_gemm_fp8_f32(w.h, _ptr(X), m, _ptr(Y), _ptr(workspace),
                                     workspace.numel() * workspace.element_size(), _stream(stream)))
+
+
+def gemm_multi(ws, X, Ys, workspace=None, stream=None) -> None:
+    """Up to four GEMMs on the same activations in one launch: Ys[i][m, rows_i]
+    = X[m, cols] (W_i.s)^T.  X is bf16 bits (any 2-byte dtype) or fp32 (rounded
+    to bf16); the weights share cols.  Bit-identical to gemm()/gemm_f32() per weight."""
+    assert 1 <= len(ws) == len(Ys) <= 4 and X.is_contiguous() and all(y.is_contiguous() for y in Ys)
+    assert X.element_size() in (2, 4)
+    m = X.shape[0]
+    need = gemm_workspace_bytes(m, ws[0].cols)
+    if workspace is None:
+        import torch
+        workspace = torch.empty(need, dtype=torch.uint8, device=X.device)
+    assert workspace.numel() * workspace.element_size() >= need
+    wp = (_vp * len(ws))(*[w.h.value for w in ws])
+    yp = (_vp * len(Ys))(*[_ptr(y) for y in Ys])
+    check(load().q35cu_gemm_fp8_multi(wp, len(ws), _ptr(X), int(X.element_size() == 4), m, yp, _ptr(workspace),
+                                      workspace.numel() * workspace.element_size(), _stream(stream)))
 
 
 def gemv_tc(w: Weight, X, Y, workspace=None, stream=None) -> None:

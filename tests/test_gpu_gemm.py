@@ -211,6 +211,55 @@ def test_gemm_f32_input_equals_bf16_input(gpu, orc, monkeypatch, kernel):
         w.free()
 
 
+@pytest.mark.parametrize("kernel", ["e4m3", "f16"])
+@pytest.mark.parametrize("rows,m", [
+    ((1024, 300, 1000, 128), 300),        # ragged last row blocks between segments
+    ((2048, 256), 1),                     # one token: one token tile
+    ((640,), 420),                        # one weight: the single-GEMM path
+])
+def test_gemm_multi_equals_single(gpu, orc, monkeypatch, kernel, rows, m):
+    """q35cu_gemm_fp8_multi: weights sharing one input in one launch (their
+    row blocks concatenated, a row block of each segment partial) give the
+    bits of one q35cu_gemm_fp8 call per weight, on bf16 and fp32 inputs."""
+    import torch
+
+    if kernel == "f16":
+        monkeypatch.setenv("Q35CU_GEMM_F16", "1")
+    K = 1536
+    ws = [q35cu.Weight.synth_fp8(700 + i, r, K) for i, r in enumerate(rows)]
+    try:
+        X = torch.from_numpy(orc.synth_act(720, (m, K))).cuda()
+        Xb = X.to(torch.bfloat16).view(torch.int16)
+        for x in (Xb, X):
+            Ym = [torch.full((m, w.rows), 7.0, device="cuda") for w in ws]
+            q35cu.gemm_multi(ws, x, Ym)
+            for w, y in zip(ws, Ym):
+                ys = torch.empty((m, w.rows), device="cuda")
+                q35cu.gemm(w, Xb, ys)
+                torch.cuda.synchronize()
+                assert torch.equal(y, ys), (w.rows, x.dtype)
+        q35cu.check_device_status()
+    finally:
+        for w in ws:
+            w.free()
+
+
+def test_gemm_multi_rejects_mixed_columns(gpu):
+    """Weights of different cols cannot share one activation matrix."""
+    import torch
+
+    a = q35cu.Weight.synth_fp8(730, 256, 512)
+    b = q35cu.Weight.synth_fp8(731, 256, 1024)
+    try:
+        X = torch.zeros((128, 512), dtype=torch.int16, device="cuda")
+        Y = [torch.empty((128, 256), device="cuda") for _ in range(2)]
+        with pytest.raises(q35cu.Q35Error):
+            q35cu.gemm_multi([a, b], X, Y)
+    finally:
+        a.free()
+        b.free()
+
+
 def test_gemm_nonfinite_activation(gpu, orc, monkeypatch):
     """A token holding an infinity or a NaN gets non-finite outputs (the fp8
     kernel: NaN); every other token is unchanged."""

@@ -404,6 +404,18 @@ __global__ void __launch_bounds__(kMaxCons + 32, 1) gemv_tma_kernel(const __grid
 // After a round of row blocks, the partials of each output are added in
 // column order.  Results depend only on (row, token, K): batch, multi and
 // single calls agree bit for bit, and repeat exactly.
+//
+// K split over a cluster (standalone launches, ksplit = 2 or 4): the CTAs of
+// a cluster own the same rows and each multiplies a contiguous range of the
+// items' 256-column splits (and converts only that part of the activation);
+// after a round, each CTA adds the partials of a share of the outputs in
+// column order, reading the other CTAs' partials from their shared memory
+// (distributed shared memory), so the sum is the same as without the split.
+// It serves launches whose rows give each CTA a few 16-row blocks with a
+// ragged last one (the 5120-row projections over 148 SMs: 34.6 rows = three
+// blocks, one of 2.6 rows; a pair of CTAs holds five blocks over half the
+// columns), and multi-token launches whose activation would not fit one
+// CTA's shared memory otherwise.
 constexpr int kM2Warps = 16;
 constexpr int kM2Threads = kM2Warps * 32;
 constexpr uint32_t kItemCols = 256;   // columns per work item
@@ -414,9 +426,10 @@ struct alignas(16) MArgs {
     Seg seg[4];
     const float *X;
     uint32_t K, ldx, m, kblocks, total_rows;
-    uint32_t xcol_bytes;  // bytes of one f16 activation column in shared memory (2K + 32)
+    uint32_t xcol_bytes;  // bytes of one f16 activation column in shared memory (2 x columns held + 32)
     uint32_t ipr;         // items per row block = ceil(K / 256)
     uint32_t rb_round;    // row blocks per round (partials buffer)
+    uint32_t ksplit;      // CTAs per cluster splitting the columns (1, 2, 4)
     int nseg;
     int tp_mode;          // GemvTp::mode (m == 1 only)
     float *gathered;      // all-gather destination [world][total_rows]
@@ -503,6 +516,21 @@ __device__ __forceinline__ void chain_wait(uint32_t *bar, uint32_t target)
 // waits on its grid barrier `bar` for the previous op instead (op > 0) and
 // arrives for the next one when its outputs are written (last == false).  In
 // both, the warps' first two weight items are in flight when they wait.
+// barrier over every thread of the cluster's CTAs (release / acquire: the
+// shared-memory stores before it are visible to the other CTAs after it)
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the same shared-memory variable in the cluster's CTA r (generic address)
+template <typename T>
+__device__ __forceinline__ const T *cluster_peer(const T *p, uint32_t r)
+{
+    uint64_t out;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(p), "r"(r));
+    return reinterpret_cast<const T *>(out);
+}
+
 template <int MT, bool CHAIN>
 __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const MmaSmem &L, uint32_t *xflag,
                                           uint32_t epoch, uint32_t *bar, uint32_t op, bool last = true)
@@ -515,8 +543,14 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t g = lane >> 2, tq = lane & 3;
     const uint32_t K = a.K, ipr = a.ipr, kbn = a.kblocks;
-    const uint32_t vr0 = (uint32_t)(((uint64_t)blockIdx.x * a.total_rows) / gridDim.x);
-    const uint32_t vr1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * a.total_rows) / gridDim.x);
+    // K split: cluster rank cr of cs takes the splits [s0, s1) of every row
+    // block; the cluster's rows are those of CTA cid of ncl
+    const uint32_t cs = CHAIN ? 1u : a.ksplit;
+    const uint32_t cr = blockIdx.x % cs, cid = blockIdx.x / cs, ncl = gridDim.x / cs;
+    const uint32_t s0 = cr * ipr / cs, s1 = (cr + 1) * ipr / cs, iw = s1 - s0;
+    const uint32_t kc0 = s0 * kItemCols;  // first activation column held in shared memory
+    const uint32_t vr0 = (uint32_t)(((uint64_t)cid * a.total_rows) / ncl);
+    const uint32_t vr1 = (uint32_t)(((uint64_t)(cid + 1) * a.total_rows) / ncl);
     const uint32_t tok0 = blockIdx.y * MT;
 
     if (!CHAIN) griddep_launch();
@@ -573,7 +607,8 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     // multiply one item (2 blocks of 128 columns) held in v; write its partial.
     // Lanes with g >= 2*MT feed B columns no output reads: they load a live
     // column (finite data) rather than zeros, as MMA output columns never mix.
-    const uint8_t *xcol = xs + (size_t)(g % (2 * MT)) * a.xcol_bytes + tq * 32;
+    // (biased by the first column held, kc0: indexed with absolute columns)
+    const uint8_t *xcol = xs + (size_t)(g % (2 * MT)) * a.xcol_bytes + tq * 32 - (size_t)kc0 * 2;
     auto compute = [&](const uint4 (&v)[8], const float (&sc)[4], uint32_t sp, uint32_t slot) {
         const uint32_t c0 = sp * kItemCols;
         if (MT == 1 && !CHAIN) {  // this item's activation chunk is converted (bounded wait)
@@ -624,13 +659,14 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
         }
     };
 
-    // items of this warp in round order: (row block, split) advanced by 16 items
-    const uint32_t nitems = nrb * ipr;
-    uint32_t it = warp, rbi = warp / ipr, sp = warp % ipr;
+    // items of this warp in round order: (row block, split in [s0, s1))
+    // advanced by 16 items
+    const uint32_t nitems = nrb * iw;
+    uint32_t it = warp, rbi = warp / iw, sp = s0 + warp % iw;
     auto advance = [&]() {
         it += kM2Warps;
         sp += kM2Warps;
-        while (sp >= ipr) { sp -= ipr; ++rbi; }
+        while (sp >= s1) { sp -= iw; ++rbi; }
     };
 
     // issue cursor (items are issued in compute order, two ahead of the one
@@ -639,7 +675,7 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     auto advance_issue = [&]() {
         jt += kM2Warps;
         sj += kM2Warps;
-        while (sj >= ipr) { sj -= ipr; ++rbj; }
+        while (sj >= s1) { sj -= iw; ++rbj; }
     };
     uint4 va[8], vb[8];
     float sa[4], sb[4];
@@ -672,9 +708,9 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
             hi[j] = f16_bits(xv[j]);
             lo[j] = f16_bits(xv[j] - __half2float(__ushort_as_half(hi[j])));
         }
-        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + k * 2) =
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt) * a.xcol_bytes + (k - kc0) * 2) =
             make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
-        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + k * 2) =
+        *reinterpret_cast<uint2 *>(xs + (size_t)(2 * tt + 1) * a.xcol_bytes + (k - kc0) * 2) =
             make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
         if (lane == 0) xmul[tt * kbn + kb] = down;
     };
@@ -686,8 +722,9 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
         // blocks of one item; its own first item's chunk comes first) and
         // marks each chunk ready with this op's epoch: a warp then waits only
         // for the chunks of the item it multiplies, not for the whole vector.
-        const uint32_t nchunk = (kbn + 1) / 2;
-        for (uint32_t c0 = warp; c0 < nchunk; c0 += 4 * kM2Warps) {
+        // (this CTA's chunks: the splits [s0, s1))
+        const uint32_t nchunk = s1;
+        for (uint32_t c0 = s0 + warp; c0 < nchunk; c0 += 4 * kM2Warps) {
             float4 xv4[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
@@ -713,22 +750,24 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     } else {
         // one warp per (token, 128-column block), XU blocks of a warp loaded
         // at once so their L2 round trips overlap
+        // (this CTA's blocks: [2 s0, min(2 s1, kblocks)))
         constexpr int XU = MT == 1 ? 8 : 4;
-        for (uint32_t base = warp; base < MT * kbn; base += XU * kM2Warps) {
+        const uint32_t kb0 = 2 * s0, kbl = (2 * s1 < kbn ? 2 * s1 : kbn) - kb0;
+        for (uint32_t base = warp; base < MT * kbl; base += XU * kM2Warps) {
             float4 xv4[XU];
 #pragma unroll
             for (int u = 0; u < XU; ++u) {
                 const uint32_t idx = base + u * kM2Warps;
-                const uint32_t tt = idx / kbn, kb = idx % kbn;
+                const uint32_t tt = idx / kbl, kb = kb0 + idx % kbl;
                 xv4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (idx < MT * kbn && tok0 + tt < a.m)
+                if (idx < MT * kbl && tok0 + tt < a.m)
                     xv4[u] = __ldcg(reinterpret_cast<const float4 *>(a.X + (size_t)(tok0 + tt) * a.ldx + kb * 128 + lane * 4));
             }
 #pragma unroll
             for (int u = 0; u < XU; ++u) {
                 const uint32_t idx = base + u * kM2Warps;
-                if (idx >= MT * kbn) break;
-                convert_block(idx / kbn, idx % kbn, xv4[u]);
+                if (idx >= MT * kbl) break;
+                convert_block(idx / kbl, kb0 + idx % kbl, xv4[u]);
             }
         }
     }
@@ -739,17 +778,17 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
     bool flip = false;  // the warp's next item sits in vb
     for (uint32_t rb0 = 0; rb0 < nrb; rb0 += a.rb_round) {
         const uint32_t nrb_r = (nrb - rb0) < a.rb_round ? (nrb - rb0) : a.rb_round;
-        const uint32_t iend = (rb0 + nrb_r) * ipr;  // items of this round: [rb0 * ipr, iend)
+        const uint32_t iend = (rb0 + nrb_r) * iw;  // items of this round: [rb0 * iw, iend)
         // ping-pong: buffer P holds item it, Q the next one; a buffer is
         // refilled with the item two ahead as soon as it has been multiplied.
         // Returns true when the round ends with the next item in Q.
         auto run = [&](uint4 (&P)[8], float (&Ps)[4], uint4 (&Q)[8], float (&Qs)[4]) -> bool {
             while (it < iend) {
-                compute(P, Ps, sp, it - rb0 * ipr);
+                compute(P, Ps, sp, it - rb0 * iw);
                 advance();
                 if (jt < nitems) { issue(P, Ps, rbj, sj); advance_issue(); }
                 if (it >= iend) return true;
-                compute(Q, Qs, sp, it - rb0 * ipr);
+                compute(Q, Qs, sp, it - rb0 * iw);
                 advance();
                 if (jt < nitems) { issue(Q, Qs, rbj, sj); advance_issue(); }
             }
@@ -757,13 +796,24 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
         };
         flip ^= flip ? run(vb, sb, va, sa) : run(va, sa, vb, sb);
         __syncthreads();
-        // combine: output (row i of block, token tt) = sum over the block's items, in column order
-        for (uint32_t o = t; o < nrb_r * 16 * MT; o += kM2Threads) {
+        if (cs > 1) cluster_sync_all();  // every CTA of the cluster has its partials
+        // combine: output (row i of block, token tt) = sum over the block's
+        // items, in column order (under a K split: outputs cr, cr + cs, ...
+        // of the round, the splits of CTA r read from its shared memory)
+        for (uint32_t o = t * cs + cr; o < nrb_r * 16 * MT; o += kM2Threads * cs) {
             const uint32_t rbl = o / (16 * MT), i = (o / MT) % 16, tt = o % MT;
             const RowBlock rb = rbt[rb0 + rbl];
             if (i >= (rb.nrows_seg & 0xFF) || tok0 + tt >= a.m) continue;
             float y = 0.f;
-            for (uint32_t s = 0; s < ipr; ++s) y += part[((size_t)(rbl * ipr + s) * 16 + i) * MT + tt];
+            if (cs == 1) {
+                for (uint32_t s = 0; s < ipr; ++s) y += part[((size_t)(rbl * ipr + s) * 16 + i) * MT + tt];
+            } else {
+                for (uint32_t r = 0; r < cs; ++r) {
+                    const uint32_t r0 = r * ipr / cs, rw = (r + 1) * ipr / cs - r0;
+                    const float *pr = cluster_peer(part, r);
+                    for (uint32_t s = 0; s < rw; ++s) y += pr[((size_t)(rbl * rw + s) * 16 + i) * MT + tt];
+                }
+            }
             const Seg &sg = a.seg[rb.nrows_seg >> 8];
             if (MT == 1 && a.tp_mode) {  // one token: publish the row to every rank
                 const uint32_t v = sg.vbegin + rb.r + i, tp_seq = tp_seq_s;
@@ -772,7 +822,10 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
             }
             sg.Y[(size_t)(tok0 + tt) * sg.ldy + rb.r + i] = y;
         }
-        __syncthreads();
+        if (cs > 1)
+            cluster_sync_all();  // the partials were read: the next round may overwrite them, or the CTA leave
+        else
+            __syncthreads();
     }
 
     // Tensor-parallel epilogue (one token).  Every rank splits the rows over
@@ -806,7 +859,7 @@ __global__ void __launch_bounds__(kM2Threads, 1) gemv_mma_kernel(const __grid_co
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t xflag[kMaxChunks];
     for (uint32_t i = threadIdx.x; i < kMaxChunks; i += kM2Threads) xflag[i] = 0;  // ordered by the body's first barrier
-    const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * a.ipr);
+    const MmaSmem L = mma_smem_layout(MT, a.xcol_bytes, a.kblocks, a.rb_round * ((a.ipr + a.ksplit - 1) / a.ksplit));
     gemv_body<MT, false>(a, smem, L, xflag, 1, nullptr, 0);
     if (a.sig_flag) {
         // host-pointer call: the last CTA out tells the waiting host thread,
@@ -970,31 +1023,75 @@ int launch_tma(const Args &a, dim3 grid, size_t smem, cudaStream_t st)
     return launch_pdl(k, grid, dim3(a.cons + 32), smem, st, a);
 }
 
+constexpr uint32_t kMmaSmemAttr = 220 * 1024;
+
+template <int MT>
+int mma_configure(int dev)
+{
+    static bool configured[64] = {};
+    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
+    if (!configured[dev]) {
+        Q35CU_CUDA(cudaFuncSetAttribute(gemv_mma_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMmaSmemAttr));
+        configured[dev] = true;
+    }
+    return Q35CU_OK;
+}
+
 template <int MT>
 int launch_mma(const MArgs &a, dim3 grid, size_t smem, cudaStream_t st)
 {
-    auto k = gemv_mma_kernel<MT>;
-    static bool configured[64] = {};
     int dev = 0;
     Q35CU_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(Q35CU_ERR_NODEV, "device %d", dev);
-    if (!configured[dev]) {
-        Q35CU_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        configured[dev] = true;
-    }
+    int rc = mma_configure<MT>(dev);
+    if (rc) return rc;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kM2Threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = a.ksplit;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    Q35CU_CUDA(cudaLaunchKernelEx(&cfg, k, a));
+    cfg.numAttrs = a.ksplit > 1 ? 2 : 1;
+    Q35CU_CUDA(cudaLaunchKernelEx(&cfg, gemv_mma_kernel<MT>, a));
     count_launch();
     return Q35CU_OK;
+}
+
+// clusters of cs CTAs of gemv_mma_kernel<MT> that the device holds at once
+// (one CTA per SM; cached per device)
+template <int MT>
+uint32_t mma_max_clusters(uint32_t cs)
+{
+    static int cache[64][5] = {};  // [device][cs]: 0 = not asked, -1 = none
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || cs > 4) return 0;
+    int &c = cache[dev][cs];
+    if (c == 0) {
+        c = -1;
+        if (mma_configure<MT>(dev) == Q35CU_OK) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(cs * 64);
+            cfg.blockDim = dim3(kM2Threads);
+            cfg.dynamicSmemBytes = kMmaSmemAttr - 4096;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = cs;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, gemv_mma_kernel<MT>, &cfg) == cudaSuccess && n > 0) c = n;
+            cudaGetLastError();  // an unsupported query leaves no error behind
+        }
+    }
+    return c > 0 ? (uint32_t)c : 0u;
 }
 
 // FP8 weights with cols % 128 == 0: the tensor-core decode GEMV
@@ -1014,7 +1111,6 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp, const Hos
     a.kblocks = a0.kblocks;
     a.total_rows = a0.total_rows;
     a.nseg = a0.nseg;
-    a.xcol_bytes = 2 * a0.K + 32;
     a.ipr = (a0.K + kItemCols - 1) / kItemCols;
     a.tp_mode = tp.mode;
     a.gathered = tp.gathered;
@@ -1026,23 +1122,71 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp, const Hos
     }
     const uint32_t budget = 216 * 1024;
     const uint32_t sms = (uint32_t)device_sms();
-    const uint32_t gx = ((a.total_rows + 15) / 16) < sms ? (a.total_rows + 15) / 16 : sms;
-    const uint32_t rows_cta = (a.total_rows + gx - 1) / gx;
-    const uint32_t nrb_max = (rows_cta + 15) / 16 + 2 * (uint32_t)a.nseg;
-    if (nrb_max > kMaxRowBlocks) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: %u rows per CTA", rows_cta);
+    const uint32_t gx1 = ((a.total_rows + 15) / 16) < sms ? (a.total_rows + 15) / 16 : sms;
     if ((a.kblocks + 1) / 2 > kMaxChunks) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: cols %u too large", a0.K);
-    int mt = a0.m >= 3 ? 4 : (int)a0.m;
-    auto fits = [&](int mtt, uint32_t rbr) {
-        return mma_smem_layout(mtt, a.xcol_bytes, a.kblocks, rbr * a.ipr).total <= budget;
+    const int mt_want = a0.m >= 3 ? 4 : (int)a0.m;
+    // One geometry per column split cs (CTAs per cluster): grid, row blocks
+    // of the busiest CTA, token tile and shared-memory layout.  Cost = the
+    // items (16-row block x 256 columns) the busiest CTA multiplies times the
+    // token tiles each row range is streamed for, plus kSplitCost items for
+    // the cluster's hand-off; the cheapest wins (Q35CU_GEMV_KSPLIT = 1, 2 or
+    // 4 forces one).  Tensor-parallel launches keep cs = 1: their epilogue
+    // exchanges each CTA's own rows.
+    struct Geo {
+        uint32_t cs, gx, nrb_max, iw, xcol, mt, rbr, gy;
+        size_t smem;
+        uint64_t cost;
     };
-    while (mt > 1 && !fits(mt, 1)) mt /= 2;
-    if (!fits(mt, 1)) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: cols %u too large", a0.K);
-    // row blocks per round: all of the CTA's if they fit, else as many as fit
-    uint32_t rbr = nrb_max;
-    while (rbr > 1 && !fits(mt, rbr)) --rbr;
-    a.rb_round = rbr;
-    const size_t smem = mma_smem_layout(mt, a.xcol_bytes, a.kblocks, rbr * a.ipr).total;
-    const uint32_t gy = (a0.m + mt - 1) / mt;
+    uint32_t split_cost = 16;
+    if (const char *e = getenv("Q35CU_GEMV_KSPLIT_COST")) split_cost = (uint32_t)strtoul(e, nullptr, 10);
+    int forced = 0;
+    if (const char *e = getenv("Q35CU_GEMV_KSPLIT")) forced = atoi(e);
+    auto geometry = [&](uint32_t cs, Geo &g) -> bool {
+        g.cs = cs;
+        g.gx = gx1 / cs * cs;
+        if (!g.gx || (cs > 1 && (tp.mode || a.ipr < cs))) return false;
+        if (cs > 1 && mma_max_clusters<1>(cs) < g.gx / cs) return false;
+        const uint32_t rows_cl = (a.total_rows + g.gx / cs - 1) / (g.gx / cs);
+        g.nrb_max = (rows_cl + 15) / 16 + 2 * (uint32_t)a.nseg;
+        if (g.nrb_max > kMaxRowBlocks) return false;
+        g.iw = (a.ipr + cs - 1) / cs;
+        const uint32_t kloc = g.iw * kItemCols < a0.K ? g.iw * kItemCols : a0.K;
+        g.xcol = 2 * kloc + 32;
+        auto fits = [&](int mtt, uint32_t rbr) {
+            return mma_smem_layout(mtt, g.xcol, a.kblocks, rbr * g.iw).total <= budget;
+        };
+        int mt = mt_want;
+        while (mt > 1 && !fits(mt, 1)) mt /= 2;
+        if (!fits(mt, 1)) return false;
+        // row blocks per round: all of the CTA's if they fit, else as many as fit
+        uint32_t rbr = g.nrb_max;
+        while (rbr > 1 && !fits(mt, rbr)) --rbr;
+        g.mt = (uint32_t)mt;
+        g.rbr = rbr;
+        g.smem = mma_smem_layout(mt, g.xcol, a.kblocks, rbr * g.iw).total;
+        g.gy = (a0.m + mt - 1) / mt;
+        const uint32_t blocks = (rows_cl + 15) / 16 + (uint32_t)a.nseg - 1;
+        g.cost = (uint64_t)blocks * g.iw * g.gy + (cs > 1 ? split_cost : 0);
+        return true;
+    };
+    Geo best{}, cand{};
+    bool have = false;
+    for (uint32_t cs : {1u, 2u, 4u}) {
+        if (forced && (uint32_t)forced != cs) continue;
+        if (geometry(cs, cand) && (!have || cand.cost < best.cost)) {
+            best = cand;
+            have = true;
+        }
+    }
+    if (!have && forced) have = geometry(1, best);
+    if (!have) return set_error(Q35CU_ERR_UNSUPPORTED, "gemv: %u rows x %u cols do not fit a CTA", a.total_rows, a0.K);
+    a.ksplit = best.cs;
+    a.xcol_bytes = best.xcol;
+    a.rb_round = best.rbr;
+    const int mt = (int)best.mt;
+    const uint32_t gx = best.gx;
+    const size_t smem = best.smem;
+    const uint32_t gy = best.gy;
     if (gy > 65535) return set_error(Q35CU_ERR_ARG, "gemv: too many tokens (%u)", a0.m);
     const dim3 grid(gx, gy);
     if (mt == 1) return launch_mma<1>(a, grid, smem, st);

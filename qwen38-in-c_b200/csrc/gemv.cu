@@ -804,14 +804,27 @@ __device__ __forceinline__ void gemv_body(const MArgs &a, uint8_t *smem, const M
             const uint32_t rbl = o / (16 * MT), i = (o / MT) % 16, tt = o % MT;
             const RowBlock rb = rbt[rb0 + rbl];
             if (i >= (rb.nrows_seg & 0xFF) || tok0 + tt >= a.m) continue;
+            // the partials are loaded 8 at a time and added in column order:
+            // the loads' round trips (distributed shared memory under a K
+            // split) overlap, the sum is the same
             float y = 0.f;
+            auto sum_splits = [&](const float *pp, uint32_t n) {
+                uint32_t s = 0;
+                for (; s + 8 <= n; s += 8) {
+                    float v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[u] = pp[(size_t)(s + u) * 16 * MT];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) y += v[u];
+                }
+                for (; s < n; ++s) y += pp[(size_t)s * 16 * MT];
+            };
             if (cs == 1) {
-                for (uint32_t s = 0; s < ipr; ++s) y += part[((size_t)(rbl * ipr + s) * 16 + i) * MT + tt];
+                sum_splits(part + ((size_t)(rbl * ipr) * 16 + i) * MT + tt, ipr);
             } else {
                 for (uint32_t r = 0; r < cs; ++r) {
                     const uint32_t r0 = r * ipr / cs, rw = (r + 1) * ipr / cs - r0;
-                    const float *pr = cluster_peer(part, r);
-                    for (uint32_t s = 0; s < rw; ++s) y += pr[((size_t)(rbl * rw + s) * 16 + i) * MT + tt];
+                    sum_splits(cluster_peer(part, r) + ((size_t)(rbl * rw) * 16 + i) * MT + tt, rw);
                 }
             }
             const Seg &sg = a.seg[rb.nrows_seg >> 8];

@@ -121,7 +121,12 @@ def pin_from_reference(fixture_dir: str) -> tuple[dict, dict]:
 
 if __name__ == "__main__":
     if len(sys.argv) >= 2 and sys.argv[1] == "--pin":
-        src = sys.argv[2] if len(sys.argv) > 2 else "/root/reference/qwen35-c/tests/fixtures/mm"
+        if len(sys.argv) > 2:
+            src = sys.argv[2]
+        elif os.environ.get("Q35_REF"):  # the reference's qwen35-c directory
+            src = os.path.join(os.environ["Q35_REF"], "tests", "fixtures", "mm")
+        else:
+            sys.exit("usage: mm_fixtures.py --pin FIXTURE_DIR (or set Q35_REF to the qwen35-c tree)")
         files, yref32 = pin_from_reference(src)
         data = {"source": "qwen35-c/tests/fixtures/mm", "files": files, "yref_f32": yref32,
                 "fnv1a_reference_outputs": {

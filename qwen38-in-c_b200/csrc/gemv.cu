@@ -1158,7 +1158,13 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp, const Hos
         g.cs = cs;
         g.gx = gx1 / cs * cs;
         if (!g.gx || (cs > 1 && (tp.mode || a.ipr < cs))) return false;
-        if (cs > 1 && mma_max_clusters<1>(cs) < g.gx / cs) return false;
+        if (cs > 1) {
+            // as many clusters as the device holds at once (clusters of 4
+            // do not tile every GPC: fewer than SMs / 4 of them fit)
+            const uint32_t ncl_max = mma_max_clusters<1>(cs);
+            if (!ncl_max) return false;
+            if (ncl_max < g.gx / cs) g.gx = ncl_max * cs;
+        }
         const uint32_t rows_cl = (a.total_rows + g.gx / cs - 1) / (g.gx / cs);
         g.nrb_max = (rows_cl + 15) / 16 + 2 * (uint32_t)a.nseg;
         if (g.nrb_max > kMaxRowBlocks) return false;
@@ -1182,11 +1188,18 @@ int launch_gemv_mma(const Args &a0, cudaStream_t st, const GemvTp &tp, const Hos
         g.cost = (uint64_t)blocks * g.iw * g.gy + (cs > 1 ? split_cost : 0);
         return true;
     };
+    // Shared memory above kSmemSoft is taken from the L1 that holds the
+    // weight loads in flight: a geometry within it wins over any beyond it
+    // (5120x17408 at 4 tokens: 4-CTA split, 122 KB, 33.4 us against the
+    // 2-CTA split, 207 KB, 42.8 us, at equal item cost).
+    constexpr size_t kSmemSoft = 160 * 1024;
     Geo best{}, cand{};
     bool have = false;
     for (uint32_t cs : {1u, 2u, 4u}) {
         if (forced && (uint32_t)forced != cs) continue;
-        if (geometry(cs, cand) && (!have || cand.cost < best.cost)) {
+        if (!geometry(cs, cand)) continue;
+        const bool soft = cand.smem <= kSmemSoft, best_soft = have && best.smem <= kSmemSoft;
+        if (!have || (soft && !best_soft) || (soft == best_soft && cand.cost < best.cost)) {
             best = cand;
             have = true;
         }

@@ -407,3 +407,23 @@ def test_stream_k_tensor_core_decode(gpu, orc, ref, monkeypatch, rows, cols, n):
     _check(orc, W, sc, X, Y1, Yr, f"stream-K {rows}x{cols} n={n}")
     monkeypatch.setenv("Q35CU_GEMM_NO_STREAMK", "1")
     _check(orc, W, sc, X, q35cu.mm_fp8_batch(W, sc, X), Yr, f"whole tiles {rows}x{cols} n={n}")
+
+
+@pytest.mark.parametrize("rows,cols", [(5120, 17408), (5120, 6144), (1040, 5120)])
+def test_gemv_column_split_widths(gpu, orc, ref, monkeypatch, rows, cols):
+    """The decode GEMV's column split over a cluster of 1, 2 or 4 CTAs (each
+    CTA a contiguous range of the 256-column splits, the partials added in
+    column order across the cluster): bit-identical to the unsplit kernel at
+    1..8 tokens, including when fewer clusters of 4 fit the device than the
+    grid would hold, and within the GEMV bound of the reference."""
+    W, sc = _synth(orc, 3100 + rows, rows, cols)
+    for n in (1, 2, 4, 8):
+        X = orc.synth_act(3200 + n, (n, cols))
+        monkeypatch.setenv("Q35CU_GEMV_KSPLIT", "1")
+        Y1 = q35cu.mm_fp8_batch(W, sc, X)
+        for cs in ("2", "4"):
+            monkeypatch.setenv("Q35CU_GEMV_KSPLIT", cs)
+            Ys = q35cu.mm_fp8_batch(W, sc, X)
+            assert np.array_equal(Ys.view(np.uint32), Y1.view(np.uint32)), (rows, cols, n, cs)
+        if n in (1, 4):
+            _check(orc, W, sc, X, Y1, ref.mm_fp8_batch(W, sc, X), f"column split {rows}x{cols} n={n}")
